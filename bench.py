@@ -1,0 +1,389 @@
+#!/usr/bin/env python3
+"""Decode throughput of woolly's quantized forward on B200.
+
+Workload (the metric's config): LLaMA-2-7B shape
+(d 4096, 32 layers, 32 heads MHA, FFN 11008, vocab 32000), Q4_0 weights drawn
+N(0, 0.02) from a seed, 16 sessions each prefilled with 512 random tokens,
+then teacher-forced decode at batch 16 (headline) and at batch 1.  One step =
+one batched decode step (16 tokens).  The weights (3.7 GB) and KV cache are
+far larger than L2, so no flush is needed between steps.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+
+Prints one JSON line (rank 0).  Under torchrun each rank runs an independent
+replica on its own GPU (weak scaling; sessions shard across GPUs with no
+collective); timing is max over ranks of the CUDA-event time.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import tempfile
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+CFG = dict(hidden=4096, layers=32, heads=32, kv_heads=32, ff=11008, vocab=32000)
+PREFILL = 512
+BATCH = 16
+SEED = 7
+METRIC = "decode tok/s, 7B-shape Q4_0 (bs1/bs16); dequant-GEMV HBM GB/s vs peak"
+WORKLOAD = "llama2-7b-shape Q4_0, 16 sessions x 512-token prefill, teacher-forced decode bs16 (and bs1)"
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def weight_bytes_7b():
+    d, L, ff, V = CFG["hidden"], CFG["layers"], CFG["ff"], CFG["vocab"]
+    per_layer = (4 * d * d + 3 * d * ff) // 32 * 18
+    return L * per_layer + d * V // 32 * 18
+
+
+def kv_bytes(ctx_lens):
+    d, L = CFG["hidden"], CFG["layers"]
+    return sum(L * 2 * c * d * 2 for c in ctx_lens)
+
+
+class Clocks:
+    """Samples SM clocks and throttle reasons during the timed region."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, dev):
+        self.dev = dev
+        self.p = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.p = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.dev), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.p = None
+
+    def _read(self):
+        for line in self.p.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if not self.p:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.p.terminate()
+        try:
+            self.p.wait(timeout=5)
+        except Exception:
+            self.p.kill()
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 7:
+                continue
+            try:
+                sm.append(float(f[0]))
+                mx = float(f[1])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[3:7]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def dist_init():
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if ws > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", device_id=None)
+    return ws, rank, local
+
+
+def max_over_ranks(x, ws):
+    if ws == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(ws):
+    if ws > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def model_path(tmpdir, rank, ws):
+    from woolly_b200.gguf import write_synthetic
+    path = os.path.join(tmpdir, "llama7b_q4_0.gguf")
+    if rank == 0 and not os.path.exists(path):
+        write_synthetic(path, **CFG, weight_type=2, context_length=4096, seed=SEED)
+    barrier(ws)
+    return path
+
+
+# ---------------------------------------------------------------- CPU baseline
+def cpu_baseline(path, steps=2, ctx=640):
+    """Times the CPU oracle (plain-C restatement of woolly's forward, f32
+    weights as woolly's dequantization cache holds them, OpenMP over all host
+    cores) on a bounded sample: 16 sessions x `steps` decode steps at context
+    `ctx`, once with 1 and once with 2 of 32 layers loaded; the per-step time
+    is extrapolated linearly to 32 layers."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+    cores = os.cpu_count() or 1
+    times = {}
+    for nl in (1, 2):
+        m = O.Model(path, threads=cores, max_layers=nl)
+        kvs = [m.new_kv(ctx + steps + 2) for _ in range(BATCH)]
+        for i, kv in enumerate(kvs):
+            kv.fill_synthetic(ctx, seed=i)
+        ids = np.arange(BATCH, dtype=np.uint32)
+        m.decode_batch(kvs, ids)  # warm
+        t0 = time.perf_counter()
+        for _ in range(steps):
+            m.decode_batch(kvs, ids)
+        times[nl] = (time.perf_counter() - t0) / steps
+        for kv in kvs:
+            kv.close()
+        m.close()
+    per_layer = max(times[2] - times[1], 1e-9)
+    fixed = max(times[1] - per_layer, 0.0)
+    step = fixed + CFG["layers"] * per_layer
+    return {"value": BATCH / step, "unit": "tok/s", "cores": cores, "kind": "port",
+            "sample": f"{BATCH} sessions x {steps} decode steps at context {ctx} with 1 and 2 of "
+                      f"32 layers loaded, f32 weights; step time extrapolated to 32 layers "
+                      f"({step * 1e3:.0f} ms/step)"}
+
+
+def run_reference(args):
+    ws, rank, local = dist_init()
+    if rank != 0:
+        return
+    with tempfile.TemporaryDirectory(dir=args.tmpdir) as td:
+        path = model_path(td, 0, 1)
+        steps = max(1, min(args.steps, 3))
+        res = None
+        t0 = time.perf_counter()
+        for _ in range(max(0, min(args.warmup, 1))):
+            cpu_baseline(path, steps=1)
+        samples = []
+        for _ in range(max(1, min(args.steps, 2))):
+            res = cpu_baseline(path, steps=steps)
+            samples.append(res["value"])
+        wall = time.perf_counter() - t0
+    v = float(np.median(samples))
+    line = {"impl": "reference", "metric": METRIC, "value": v, "unit": "tok/s",
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": BATCH / v * 1e3, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": WORKLOAD, "model": "llama2-7b-shape", "global_batch": BATCH,
+                       "seq_len": PREFILL, "parallelism": "cpu"},
+            "cpu_baseline": dict(res, value=v),
+            "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "wall_s": wall}
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------- GPU arm
+def gemv_roofline(torch, dev, hbm_peak, reps=20):
+    """Average duration of the layout-B Q4_0 GEMV at B=16 over the four 7B
+    projection shapes, weights rotated across copies totalling > 4x L2."""
+    from woolly_b200 import ops
+    shapes = [(4096, 12288), (4096, 4096), (4096, 22016), (11008, 4096)]
+    copies = 4
+    res = {}
+    tot_bytes, tot_ms = 0, 0.0
+    for K, N in shapes:
+        nbytes = K * N // 32 * 18
+        ws = [torch.randint(0, 256, (nbytes,), dtype=torch.uint8, device=dev) for _ in range(copies)]
+        for w in ws:  # realistic f16 scales (0x2000 ~ 0.0078) in every block
+            w.view(-1, 18)[:, 1] = 0x20
+            w.view(-1, 18)[:, 0] = 0
+        x = torch.randn(BATCH, K, device=dev)
+        for i in range(3):
+            ops.qgemv(ws[i % copies], 2, 1, x, N)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for i in range(reps):
+            ops.qgemv(ws[i % copies], 2, 1, x, N)
+        e1.record()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / reps
+        alg = nbytes + 4 * BATCH * K + 4 * BATCH * N
+        res[f"{K}x{N}"] = {"us": ms * 1e3, "GBps": alg / ms / 1e6}
+        tot_bytes += alg
+        tot_ms += ms
+        del ws
+    achieved = tot_bytes / tot_ms / 1e6
+    return achieved, res
+
+
+def run_gpu(args):
+    import torch
+    ws, rank, local = dist_init()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    from woolly_b200.model import CudaTransformer, Session
+    hbm_peak, peak_kind = peaks()
+    os.makedirs(args.tmpdir, exist_ok=True)
+    td = args.tmpdir
+    path = model_path(td, rank, ws)
+    max_ctx = PREFILL + args.warmup + args.steps + args.bs1_steps + 8
+    m = CudaTransformer(path, device=local, max_sessions=BATCH + 1, max_context=max_ctx,
+                        max_batch=BATCH, max_prefill=PREFILL)
+    rng = np.random.default_rng(SEED + 1_000_000 + rank)
+    sess = [Session(m) for _ in range(BATCH)]
+    for s in sess:
+        s.infer_last(rng.integers(0, CFG["vocab"], PREFILL).tolist())
+    total = args.warmup + args.steps
+    forced = torch.from_numpy(rng.integers(0, CFG["vocab"], (total, BATCH)).astype(np.int32)).to(dev)
+    logits = torch.empty(BATCH, CFG["vocab"], device=dev)
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    for t in range(args.warmup):
+        m.decode_step_device(sess, forced[t].data_ptr(), logits.data_ptr(), stream)
+    torch.cuda.synchronize()
+    barrier(ws)
+    ctx0 = [len(s) for s in sess]
+    clk = Clocks(local)
+    clk.start()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    e0.record()
+    for t in range(args.warmup, total):
+        m.decode_step_device(sess, forced[t].data_ptr(), logits.data_ptr(), stream)
+    e1.record()
+    torch.cuda.synchronize()
+    clocks = clk.stop()
+    ms_total = max_over_ranks(e0.elapsed_time(e1), ws)
+    ms_step = ms_total / args.steps
+    value = ws * BATCH * args.steps / (ms_total / 1e3)
+    # algorithmic bytes of the timed steps: weights once per step + KV read
+    kv = sum(kv_bytes([c + i + 1 for c in ctx0]) for i in range(args.steps)) / args.steps
+    step_bytes = weight_bytes_7b() + kv
+    step_gbs = step_bytes / (ms_step / 1e3) / 1e9
+    barrier(ws)
+
+    # ---- end to end through the public API: host ids in, host logits out ----
+    e2e_steps = max(3, min(args.steps, 32))
+    for s in sess:
+        s.reset()
+    for s in sess:
+        s.infer_last(rng.integers(0, CFG["vocab"], PREFILL).tolist())
+    host_ids = rng.integers(0, CFG["vocab"], (e2e_steps + 1, BATCH)).astype(np.uint32)
+    m.forward_sessions(sess, [[int(i)] for i in host_ids[0]])
+    torch.cuda.synchronize()
+    barrier(ws)
+    t0 = time.perf_counter()
+    for t in range(1, e2e_steps + 1):
+        out = m.forward_sessions(sess, [[int(i)] for i in host_ids[t]])
+    e2e_s = max_over_ranks(time.perf_counter() - t0, ws)
+    e2e_value = ws * BATCH * e2e_steps / e2e_s
+    assert np.isfinite(out[0]).all()
+
+    # ---- batch 1 ----
+    s1 = Session(m)
+    s1.infer_last(rng.integers(0, CFG["vocab"], PREFILL).tolist())
+    ids1 = torch.from_numpy(rng.integers(0, CFG["vocab"], args.bs1_steps + 3).astype(np.int32)).to(dev)
+    for t in range(3):
+        m.decode_step_device([s1], ids1[t].data_ptr(), logits.data_ptr(), stream)
+    torch.cuda.synchronize()
+    e0.record()
+    for t in range(3, args.bs1_steps + 3):
+        m.decode_step_device([s1], ids1[t].data_ptr(), logits.data_ptr(), stream)
+    e1.record()
+    torch.cuda.synchronize()
+    ms1 = max_over_ranks(e0.elapsed_time(e1), ws) / args.bs1_steps
+    bs1 = {"value": ws * 1e3 / ms1, "unit": "tok/s", "ms_per_step": ms1,
+           "hbm_frac_of_" + peak_kind: (weight_bytes_7b() + kv_bytes([PREFILL + 3])) / (ms1 / 1e3) / 1e9 / hbm_peak}
+    launches = m.decode_kernel_count(BATCH) * args.steps
+    s1.close()
+    for s in sess:
+        s.close()
+    m.close()
+
+    # ---- dominant kernel: the layout-B Q4_0 GEMV ----
+    achieved, per_shape = gemv_roofline(torch, dev, hbm_peak)
+    traffic = None
+    try:
+        with open(os.path.join(ROOT, "profiles", "qgemv_b_q4_0_7b_decode.json")) as f:
+            traffic = json.load(f).get("dram_bytes_per_launch")
+    except Exception:
+        pass
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": ws, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "q4_0 weights, f16 MMA operands, f32 accumulate",
+            "data": "synthetic (seeded N(0,0.02) weights, uniform random token ids)",
+            "config": {"workload": WORKLOAD, "model": "llama2-7b-shape", "global_batch": BATCH * ws,
+                       "seq_len": PREFILL, "parallelism": f"replicas x{ws}",
+                       "l2": "inputs larger than L2 (3.7 GB weights + KV per step)"},
+            "e2e": {"value": e2e_value, "unit": "tok/s", "h2d_bytes_per_step": BATCH * 12,
+                    "d2h_bytes_per_step": BATCH * CFG["vocab"] * 4},
+            "bs1": bs1,
+            "step_roofline": {"bound": "hbm", "achieved": step_gbs, "peak": hbm_peak,
+                              "unit": "GB/s", "frac": step_gbs / hbm_peak,
+                              "bytes_per_step": step_bytes, "peak_kind": peak_kind},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
+                         "frac": achieved / hbm_peak, "traffic": traffic,
+                         "kernel": "k_qgemv_b<Q4_0, B=16>", "peak_kind": peak_kind,
+                         "shapes": per_shape},
+            "clocks": clocks,
+            "gpu_launches": launches,
+        }
+        if not args.no_cpu_baseline and ws == 1:
+            line["cpu_baseline"] = cpu_baseline(path)
+        print(json.dumps(line), flush=True)
+    barrier(ws)
+    if ws > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=253)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--bs1-steps", type=int, default=64)
+    ap.add_argument("--impl", default="woolly_b200", choices=["woolly_b200", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--tmpdir", default=os.environ.get("WOOLLY_BENCH_DIR", "/tmp/woolly_bench"))
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_gpu(args)
+
+
+if __name__ == "__main__":
+    main()

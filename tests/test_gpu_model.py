@@ -1,0 +1,178 @@
+"""Model-level parity: the CUDA runtime vs the CPU oracle on seeded synthetic
+GGUF models (GPU).
+
+The bar (north_star): per-step teacher-forced logits within max-abs 1e-2 of
+the oracle and top-1 agreement >= 99%.  Prompts are uniform random ids;
+decode steps feed pre-drawn ids (teacher forcing), not the argmax.
+"""
+import os
+
+import numpy as np
+import pytest
+
+import oracle as O
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+from woolly_b200 import Q4_0, WoollyError, _lib  # noqa: E402
+from woolly_b200.gguf import write_synthetic  # noqa: E402
+from woolly_b200.model import CudaTransformer, Session  # noqa: E402
+
+LOGIT_TOL = 1e-2
+TOP1_MIN = 0.99
+GOLD = os.path.join(os.path.dirname(__file__), "golden")
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _cuda():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+
+
+def compare(got, ref, what=""):
+    got = np.asarray(got, np.float32).reshape(ref.shape)
+    err = np.abs(got - ref).max()
+    top1 = np.mean(got.reshape(-1, ref.shape[-1]).argmax(-1) == ref.reshape(-1, ref.shape[-1]).argmax(-1))
+    assert err <= LOGIT_TOL, f"{what}: max-abs {err}"
+    assert top1 >= TOP1_MIN, f"{what}: top-1 agreement {top1}"
+    return err, top1
+
+
+def teacher_forced(path, prompts, steps, seed=0, oracle_kw=None, **model_kw):
+    """Prefill each prompt, then `steps` batched decode steps; returns the
+    per-step logits of the GPU path and of the oracle."""
+    rng = np.random.default_rng(seed + 1_000_000)
+    m = CudaTransformer(path, **model_kw)
+    V = m.vocab_size()
+    forced = rng.integers(0, V, size=(steps, len(prompts)), dtype=np.uint32)
+    sess = [Session(m) for _ in prompts]
+    gpu_pref = m.forward_sessions(sess, prompts, all_logits=True)
+    gpu_steps = []
+    for t in range(steps):
+        out = m.forward_sessions(sess, [[int(i)] for i in forced[t]])
+        gpu_steps.append(np.stack(out))
+    for s in sess:
+        s.close()
+    m.close()
+    om = O.Model(path, **(oracle_kw or {}))
+    kvs = [om.new_kv(max(len(p) for p in prompts) + steps + 1) for _ in prompts]
+    or_pref = [om.forward(kv, p, all_rows=True) for kv, p in zip(kvs, prompts)]
+    or_steps = [om.decode_batch(kvs, forced[t]) for t in range(steps)]
+    om.close()
+    return gpu_pref, np.stack(gpu_steps), or_pref, np.stack(or_steps)
+
+
+def run_parity(path, prompts, steps, oracle_kw=None, **model_kw):
+    gp, gs, op, os_ = teacher_forced(path, prompts, steps, oracle_kw=oracle_kw, **model_kw)
+    for i, (a, b) in enumerate(zip(gp, op)):
+        compare(a, b, f"prefill session {i}")
+    compare(gs, os_, "decode steps")
+
+
+def test_golden_tiny_forward(tmp_path):
+    g = np.load(os.path.join(GOLD, "tiny_forward.npz"))
+    import json
+    spec = json.loads(str(g["spec"]))
+    p = write_synthetic(str(tmp_path / "tiny.gguf"), **spec)
+    m = CudaTransformer(p, max_sessions=2, max_context=64)
+    logits = m.forward(g["ids"].tolist())
+    m.close()
+    compare(logits.reshape(g["logits"].shape), g["logits"], "golden tiny forward")
+
+
+@pytest.mark.parametrize("name", ["gqa_q4_0", "mha_q4_1", "gqa_q8_0", "tied_q4_0"])
+def test_teacher_forced_parity(tiny_models, name):
+    prompts = [[1, 2, 3, 4, 5, 6, 7], [100, 200], list(range(40, 73))]
+    run_parity(tiny_models[name], prompts, steps=12, max_sessions=4, max_context=128)
+
+
+def test_decode_without_graphs_matches(tiny_models):
+    prompts = [[9, 8, 7], [1]]
+    run_parity(tiny_models["gqa_q4_0"], prompts, steps=5, max_sessions=2, max_context=64,
+               use_graphs=0)
+
+
+def test_rope_neox_parity(tiny_models):
+    prompts = [list(range(3, 20)), [5, 6]]
+    run_parity(tiny_models["gqa_q4_0"], prompts, steps=6, oracle_kw=dict(rope=1),
+               max_sessions=2, max_context=64, rope_mode=_lib.ROPE_NEOX)
+
+
+def test_sliding_window_parity(tiny_models):
+    # window 16 from metadata; contexts run past it
+    prompts = [list(range(10, 40)), [3] * 5]
+    run_parity(tiny_models["swa_q4_1"], prompts, steps=20, oracle_kw=dict(window=16),
+               max_sessions=2, max_context=128)
+
+
+def test_long_prefill_chunked_and_paged(tiny_models):
+    # a prompt longer than max_prefill runs in chunks; contexts cross many pages
+    rng = np.random.default_rng(4)
+    prompts = [rng.integers(0, 1024, 150).tolist()]
+    run_parity(tiny_models["gqa_q4_0"], prompts, steps=3, max_sessions=1, max_context=200,
+               max_prefill=64)
+
+
+def test_device_step_matches_host_step(tiny_models):
+    m = CudaTransformer(tiny_models["gqa_q4_0"], max_sessions=4, max_context=64)
+    a = [Session(m) for _ in range(3)]
+    b = [Session(m) for _ in range(1)]
+    for s in a:
+        s.infer([1, 2, 3])
+    ids = np.array([4, 5, 6], np.uint32)
+    host = np.stack(m.forward_sessions(a, [[int(i)] for i in ids]))
+    for s in a:
+        s.reset()
+        s.infer([1, 2, 3])
+    d_ids = torch.from_numpy(ids.view(np.int32)).cuda()
+    d_log = torch.empty(3, m.vocab_size(), device="cuda")
+    torch.cuda.synchronize()
+    m.decode_step_device(a, d_ids.data_ptr(), d_log.data_ptr(), torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    assert np.abs(d_log.cpu().numpy() - host).max() <= 1e-5
+    assert [len(s) for s in a] == [4, 4, 4]
+    for s in a + b:
+        s.close()
+    m.close()
+
+
+def test_errors(tiny_models):
+    m = CudaTransformer(tiny_models["mha_q4_1"], max_sessions=2, max_context=16, max_batch=2)
+    s = Session(m)
+    with pytest.raises(WoollyError) as e:
+        s.infer([512])  # vocab is 512
+    assert e.value.code == _lib.WL_ERR_TOKEN_OUT_OF_RANGE
+    with pytest.raises(WoollyError) as e:
+        s.infer([])
+    assert e.value.code == _lib.WL_ERR_INVALID_ARGUMENT
+    s.infer(list(range(16)))
+    with pytest.raises(WoollyError) as e:
+        s.infer([1])
+    assert e.value.code == _lib.WL_ERR_CONTEXT_FULL
+    s2 = Session(m)
+    with pytest.raises(WoollyError) as e:
+        Session(m)
+    assert e.value.code == _lib.WL_ERR_OUT_OF_MEMORY
+    s.reset()
+    assert len(s) == 0
+    s.infer([1, 2])
+    s.close()
+    s2.close()
+    m.close()
+    with pytest.raises(WoollyError) as e:
+        CudaTransformer("/nonexistent.gguf")
+    assert e.value.code == _lib.WL_ERR_IO
+
+
+def test_tinyllama_config_teacher_forced(tmp_path):
+    """TinyLlama-1.1B shape, Q4_0, 128-token prompt + 128
+    teacher-forced decode steps at batch 1, against the oracle."""
+    p = write_synthetic(str(tmp_path / "tinyllama.gguf"), hidden=2048, layers=22, heads=32,
+                        kv_heads=4, ff=5632, vocab=32000, weight_type=Q4_0, seed=1)
+    prompt = np.random.default_rng(1 + 1_000_000).integers(0, 32000, 128).tolist()
+    gp, gs, op, os_ = teacher_forced(p, [prompt], 128, seed=2, max_sessions=1, max_context=512,
+                                     max_batch=1)
+    e1, t1 = compare(gp[0], op[0], "tinyllama prefill")
+    e2, t2 = compare(gs, os_, "tinyllama decode")
+    print(f"tinyllama parity: prefill max-abs {e1:.2e} top1 {t1:.3f}; decode max-abs {e2:.2e} top1 {t2:.3f}")

@@ -1,0 +1,228 @@
+"""Op-level parity of the CUDA kernels against the CPU oracle (GPU).
+
+Tolerances: dequantization is bit-exact (integer unpack and f16 widening
+must match woolly_gguf::dequantize exactly).  The GEMV feeds the tensor cores
+f16 operands (weights rounded once to f16, activations rounded to f16) and
+accumulates in f32: |y - ref| <= 4e-3 * max|ref| per output vector.  f32 ops
+(RMSNorm, SwiGLU, RoPE, attention) are held to 2e-5 relative.
+"""
+import json
+import os
+import struct
+
+import numpy as np
+import pytest
+
+import oracle as O
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+from woolly_b200 import LAYOUT_A, LAYOUT_B, Q4_0, Q4_1, Q8_0, WoollyError, _lib  # noqa: E402
+from woolly_b200 import ops  # noqa: E402
+from woolly_b200.gguf import quantize  # noqa: E402
+
+GOLD = os.path.join(os.path.dirname(__file__), "golden")
+TS = {Q4_0: 18, Q4_1: 20, Q8_0: 34}
+GEMV_TOL = 4e-3
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _cuda():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    torch.cuda.init()
+
+
+def dev(a, dtype=None):
+    t = torch.from_numpy(np.ascontiguousarray(a))
+    if dtype is not None:
+        t = t.to(dtype)
+    return t.cuda()
+
+
+def random_blocks(qt, nb, seed, scales=(0.0123, -0.5, 3e-5, 1.0, 6e-8, 2.0)):
+    rng = np.random.default_rng(seed)
+    raw = rng.integers(0, 256, size=(nb, TS[qt]), dtype=np.uint8)
+    sc = rng.choice(np.array(scales, np.float16), nb * 2)
+    raw[:, 0:2] = sc[:nb].view(np.uint8).reshape(nb, 2)
+    if qt == Q4_1:
+        raw[:, 2:4] = sc[nb:].view(np.uint8).reshape(nb, 2)
+    return raw.reshape(-1)
+
+
+def quant_matrix(qt, rows, cols, seed, std=0.02):
+    rng = np.random.default_rng(seed)
+    w = (rng.standard_normal(rows * cols) * std).astype(np.float32)
+    return quantize(qt, w)
+
+
+@pytest.mark.parametrize("qt", [Q4_0, Q4_1, Q8_0])
+def test_dequant_bit_exact(qt):
+    nb = 50_000
+    raw = random_blocks(qt, nb, qt)
+    ref = O.dequantize(raw.tobytes(), qt, nb * 32)
+    got = ops.dequantize(dev(raw), qt, nb * 32).cpu().numpy()
+    assert np.array_equal(got.view(np.uint32), ref.view(np.uint32))
+
+
+@pytest.mark.parametrize("qt", [Q4_0, Q4_1, Q8_0])
+def test_dequant_any_bytes_and_partial_block(qt):
+    nb = 4096
+    raw = np.random.default_rng(100 + qt).integers(0, 256, size=nb * TS[qt], dtype=np.uint8)
+    n = nb * 32 - 7
+    ref = O.dequantize(raw.tobytes(), qt, n)
+    got = ops.dequantize(dev(raw), qt, n).cpu().numpy()
+    nan = np.isnan(ref)
+    assert np.array_equal(np.isnan(got), nan)
+    assert np.array_equal(got[~nan].view(np.uint32), ref[~nan].view(np.uint32))
+
+
+def test_dequant_kats_on_gpu():
+    with open(os.path.join(GOLD, "kats.json")) as f:
+        kats = json.load(f)["dequant"]
+    for k in kats:
+        raw = np.frombuffer(bytes.fromhex(k["hex"]), np.uint8)
+        got = ops.dequantize(dev(raw), k["type"], k["n"]).cpu().numpy()
+        assert got.tolist() == k["expect"], k["source"]
+
+
+def test_dequant_buffer_too_small():
+    with pytest.raises(WoollyError) as e:
+        ops.dequantize(dev(np.zeros(17, np.uint8)), Q4_0, 32)
+    assert e.value.code == _lib.WL_ERR_BUFFER_TOO_SMALL
+
+
+def ref_gemv(qt, layout, raw, K, N, x):
+    W = O.dequantize(raw.tobytes(), qt, K * N).astype(np.float64)
+    W = W.reshape(K, N) if layout == LAYOUT_B else W.reshape(N, K).T
+    return x.astype(np.float64) @ W
+
+
+def check_gemv(y, ref):
+    y = np.asarray(y, np.float64)
+    scale = np.abs(ref).max()
+    assert np.abs(y - ref).max() <= GEMV_TOL * scale + 1e-6, (np.abs(y - ref).max(), scale)
+
+
+@pytest.mark.parametrize("qt", [Q4_0, Q4_1, Q8_0])
+@pytest.mark.parametrize("layout", [LAYOUT_B, LAYOUT_A])
+@pytest.mark.parametrize("K,N", [(512, 1024), (2048, 256), (768, 96), (256, 4096), (160, 64)])
+@pytest.mark.parametrize("B", [1, 5, 16, 33])
+def test_qgemv_vs_oracle(qt, layout, K, N, B):
+    raw = quant_matrix(qt, K, N, seed=K * 7 + N + qt)
+    x = np.random.default_rng(B).standard_normal((B, K)).astype(np.float32)
+    y = ops.qgemv(dev(raw), qt, layout, dev(x), N).cpu().numpy()
+    check_gemv(y, ref_gemv(qt, layout, raw, K, N, x))
+
+
+@pytest.mark.parametrize("qt", [Q4_0, Q4_1, Q8_0])
+@pytest.mark.parametrize("K,N", [(4096, 4096), (4096, 14336), (14336, 4096)])
+def test_qgemv_sweep_shapes(qt, K, N):
+    """The standalone sweep shapes, both layouts, B = 1 and 16."""
+    raw = quant_matrix(qt, K, N, seed=3)
+    W = O.dequantize(raw.tobytes(), qt, K * N).astype(np.float32)
+    for layout in (LAYOUT_B, LAYOUT_A):
+        Wm = W.reshape(K, N) if layout == LAYOUT_B else W.reshape(N, K).T
+        Wt = dev(Wm)
+        for B in (1, 16):
+            x = np.random.default_rng(B).standard_normal((B, K)).astype(np.float32)
+            y = ops.qgemv(dev(raw), qt, layout, dev(x), N)
+            ref = (dev(x).double() @ Wt.double()).cpu().numpy()
+            check_gemv(y.cpu().numpy(), ref)
+
+
+def test_matmul_2x2_kat_layout_b():
+    """tensor_utils.rs:608-620 ([1,2;3,4] @ [5,6;7,8] = [19,22;43,50]) through the
+    layout-B GEMV with Q8_0 blocks of scale 1: the K=2 case takes the generic
+    kernel, the zero-padded K=32 case the tensor-core kernel."""
+    for K in (2, 32):
+        Wf = np.zeros((K, 32), np.float32)
+        Wf[0, :2] = [5, 6]
+        Wf[1, :2] = [7, 8]
+        raw = bytearray()
+        for r in range(K):
+            raw += struct.pack("<e", 1.0) + Wf[r].astype(np.int8).tobytes()
+        x = np.zeros((2, K), np.float32)
+        x[0, :2] = [1, 2]
+        x[1, :2] = [3, 4]
+        y = ops.qgemv(dev(np.frombuffer(bytes(raw), np.uint8)), Q8_0, LAYOUT_B, dev(x), 32)
+        assert y[:, :2].cpu().numpy().ravel().tolist() == [19.0, 22.0, 43.0, 50.0]
+
+
+@pytest.mark.parametrize("qt", [Q4_0, Q8_0])
+def test_quantized_matvec_vs_scalar_reference(qt):
+    m, k = 1024, 4096
+    raw = quant_matrix(qt, m, k, seed=9)
+    x = np.random.default_rng(1).standard_normal(k).astype(np.float32)
+    ref = O.quantized_matvec(qt, raw, x, m, k).astype(np.float64)
+    out = torch.zeros(m, dtype=torch.float32, device="cuda")
+    ops.quantized_matvec(dev(raw), qt, dev(x), out, m, k)
+    check_gemv(out.cpu().numpy(), ref)
+
+
+def test_quantized_matvec_q4_1_unsupported():
+    out = torch.zeros(1, dtype=torch.float32, device="cuda")
+    with pytest.raises(WoollyError) as e:
+        ops.quantized_matvec(dev(np.zeros(40, np.uint8)), Q4_1, dev(np.zeros(64, np.float32)), out, 1, 64)
+    assert e.value.code == _lib.WL_ERR_UNSUPPORTED
+
+
+@pytest.mark.parametrize("d", [64, 2048, 4096, 5120])
+def test_rmsnorm(d):
+    rng = np.random.default_rng(d)
+    x = rng.standard_normal((7, d)).astype(np.float32)
+    w = (1 + 0.02 * rng.standard_normal(d)).astype(np.float32)
+    ref = O.rms_norm(x, w, 1e-5)
+    y = ops.rmsnorm_rope(dev(x), dev(w), 1e-5).cpu().numpy()
+    assert np.allclose(y, ref, rtol=2e-5, atol=1e-6)
+    yh = ops.rmsnorm_rope(dev(x), dev(w), 1e-5, out_dtype=torch.float16).cpu().numpy()
+    assert np.allclose(yh.astype(np.float32), ref.astype(np.float16).astype(np.float32),
+                       rtol=1e-3, atol=1e-3)
+
+
+def test_rmsnorm_fused_rope():
+    rng = np.random.default_rng(5)
+    rows, heads, hd = 6, 8, 64
+    x = rng.standard_normal((rows, heads * hd)).astype(np.float32)
+    w = (1 + 0.02 * rng.standard_normal(heads * hd)).astype(np.float32)
+    pos = np.array([0, 1, 7, 100, 1000, 4095], np.int32)
+    normed = O.rms_norm(x, w, 1e-5)
+    ref = np.stack([O.rope_neox(normed[r], [pos[r]], 1, 1, heads, hd, 10000.0) for r in range(rows)])
+    y = ops.rmsnorm_rope(dev(x), dev(w), 1e-5, rope=True, positions=dev(pos), head_dim=hd).cpu().numpy()
+    assert np.allclose(y, ref.reshape(rows, -1), rtol=5e-5, atol=5e-5)
+
+
+def test_swiglu_exact():
+    rng = np.random.default_rng(2)
+    g = (rng.standard_normal(100_003) * 4).astype(np.float32)
+    u = rng.standard_normal(100_003).astype(np.float32)
+    ref = O.swiglu(g, u, 0)
+    out = torch.empty(g.size, dtype=torch.float32, device="cuda")
+    ops.TransformerSIMD.swiglu_activation(dev(g), dev(u), out)
+    assert np.allclose(out.cpu().numpy(), ref, rtol=2e-6, atol=1e-7)
+
+
+def test_rope_apply_f32():
+    rng = np.random.default_rng(3)
+    batch, seq, heads, hd = 2, 5, 4, 128
+    x = rng.standard_normal((batch, seq, heads, hd)).astype(np.float32)
+    pos = np.array([0, 3, 17, 511, 2047], np.int32)
+    ref = O.rope_neox(x, pos, batch, seq, heads, hd, 10000.0)
+    out = torch.empty(x.size, dtype=torch.float32, device="cuda")
+    ops.RoPE.apply_f32(dev(x), out, dev(pos), 10000.0, batch, seq, heads, hd)
+    assert np.allclose(out.cpu().numpy().reshape(x.shape), ref.reshape(x.shape), rtol=5e-5, atol=5e-5)
+
+
+@pytest.mark.parametrize("heads,kv_heads,hd,rows,past,window",
+                         [(8, 2, 64, 5, 37, 0), (4, 4, 128, 1, 300, 0), (8, 1, 64, 3, 10, 0),
+                          (4, 2, 128, 4, 60, 16), (2, 1, 32, 2, 5, 0), (2, 2, 256, 2, 70, 0)])
+def test_attention_f32_vs_oracle(heads, kv_heads, hd, rows, past, window):
+    rng = np.random.default_rng(heads * 100 + past)
+    q = rng.standard_normal((rows, heads * hd)).astype(np.float32)
+    k = rng.standard_normal((past + rows, kv_heads * hd)).astype(np.float32)
+    v = rng.standard_normal((past + rows, kv_heads * hd)).astype(np.float32)
+    ref = O.attention(q, k, v, rows, past, heads, kv_heads, hd, window)
+    got = ops.attention(dev(q), dev(k), dev(v), past=past, heads=heads, kv_heads=kv_heads,
+                        head_dim=hd, window=window).cpu().numpy()
+    assert np.allclose(got, ref, rtol=2e-5, atol=2e-5)

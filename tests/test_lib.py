@@ -1,0 +1,63 @@
+"""The C-ABI library loads and exports every symbol include/woolly_cuda.h
+declares; host-only entry points behave (CPU only, no compute calls)."""
+import ctypes as C
+import os
+import re
+
+import numpy as np
+import pytest
+
+from woolly_b200 import _lib
+from woolly_b200.gguf import synth_normal
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def header_symbols():
+    txt = open(os.path.join(ROOT, "include", "woolly_cuda.h")).read()
+    txt = re.sub(r"/\*.*?\*/", "", txt, flags=re.S)
+    return sorted(set(re.findall(r"\b(wl_[a-z0-9_]+)\s*\(", txt)))
+
+
+def test_library_exports_every_header_symbol():
+    lib = _lib.lib()
+    syms = header_symbols()
+    assert len(syms) > 30
+    missing = [s for s in syms if not hasattr(lib, s)]
+    assert not missing, missing
+
+
+def test_python_binding_covers_header():
+    assert set(header_symbols()) <= set(_lib.exported_symbols())
+
+
+def test_version_and_sizes():
+    lib = _lib.lib()
+    assert b"sm_100a" in lib.wl_version()
+    assert [lib.wl_type_size(t) for t in (0, 1, 2, 3, 8)] == [4, 2, 18, 20, 34]
+    assert lib.wl_block_size(2) == 32 and lib.wl_block_size(4) == 0
+
+
+def test_synth_normal_deterministic_and_normal():
+    a = synth_normal(1, 2, 200_000, 0.0, 1.0)
+    b = synth_normal(1, 2, 200_000, 0.0, 1.0)
+    assert np.array_equal(a, b)
+    assert abs(a.mean()) < 0.01 and abs(a.std() - 1.0) < 0.01
+    assert not np.array_equal(a, synth_normal(1, 3, 200_000))
+
+
+def test_errors_without_gpu_are_reported():
+    # no crash and a status code when asked for a device that is not there
+    lib = _lib.lib()
+    h = C.c_void_p()
+    st = lib.wl_init(999, C.byref(h))
+    assert st != 0
+    assert lib.wl_last_error()
+
+
+def test_model_load_rejects_missing_file():
+    from woolly_b200.model import model_options
+    lib = _lib.lib()
+    h = C.c_void_p()
+    st = lib.wl_model_load_gguf(None, b"/nonexistent.gguf", C.byref(model_options()), C.byref(h))
+    assert st == _lib.WL_ERR_INVALID_ARGUMENT

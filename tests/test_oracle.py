@@ -1,0 +1,147 @@
+"""Pins the CPU oracle to the reference's own known-answer tests (CPU only).
+
+KAT sources (woolly, read as text):
+  crates/woolly-tensor/src/quantization.rs:1294-1386  dequant KATs, block sizes
+  crates/woolly-gguf/src/loader.rs:676-682            align_offset table
+  crates/woolly-gguf/src/tensor_info.rs:281-305       Q4_0 64x64 data_size = 2304
+  crates/woolly-core/src/tensor_utils.rs:608-620      2x2 matmul = [19, 22, 43, 50]
+plus an independent cross-check against gguf-py's dequantizers (llama.cpp's
+Python package, present in this image) and numpy's IEEE f16 widening.
+"""
+import json
+import os
+import struct
+
+import numpy as np
+import pytest
+
+import oracle as O
+
+GOLD = os.path.join(os.path.dirname(__file__), "golden")
+
+
+def blk_q4_0(d, qs):
+    return struct.pack("<e", d) + bytes(qs)
+
+
+def blk_q4_1(d, m, qs):
+    return struct.pack("<ee", d, m) + bytes(qs)
+
+
+def blk_q8_0(d, qs):
+    return struct.pack("<e", d) + np.asarray(qs, dtype=np.int8).tobytes()
+
+
+def test_q4_0_kat():  # quantization.rs:1294-1307
+    out = O.dequantize(blk_q4_0(2.0, [0] * 16), O.Q4_0, 32)
+    assert np.all(out == -16.0)
+
+
+def test_q4_1_kat():  # quantization.rs:1310-1326
+    out = O.dequantize(blk_q4_1(1.0, 5.0, [0x01] * 16), O.Q4_1, 32)
+    assert np.all(out[:16] == 6.0) and np.all(out[16:] == 5.0)
+
+
+def test_q8_0_kat():  # quantization.rs:1329-1344
+    qs = [0] * 32
+    qs[0], qs[1] = 10, -5
+    out = O.dequantize(blk_q8_0(0.5, qs), O.Q8_0, 32)
+    assert out[0] == 5.0 and out[1] == -2.5 and np.all(out[2:] == 0)
+
+
+def test_block_sizes():  # quantization.rs:1347-1356, dequantize.rs:221-244
+    assert [O.lib().or_type_size(t) for t in (2, 3, 6, 7, 8)] == [18, 20, 22, 24, 34]
+    assert [O.lib().or_block_size(t) for t in (0, 2, 12, 14)] == [1, 32, 256, 256]
+
+
+def test_dispatcher_two_blocks():  # quantization.rs:1359-1386
+    data = blk_q4_0(1.0, [0x11] * 16) + blk_q4_0(2.0, [0x22] * 16)
+    out = O.dequantize(data, O.Q4_0, 64)
+    assert np.all(out[:32] == -7.0) and np.all(out[32:] == -12.0)
+
+
+def test_batch_equals_scalar():  # quantization.rs:1389-1407
+    data = b"".join(blk_q4_0(float(i + 1), [0] * 16) for i in range(8))
+    out = O.dequantize(data, O.Q4_0, 256)
+    assert np.array_equal(out, np.repeat(-8.0 * np.arange(1, 9), 32).astype(np.float32))
+
+
+def test_align_offset():  # loader.rs:676-682
+    for a, b in [(0, 0), (1, 32), (31, 32), (32, 32), (33, 64)]:
+        assert O.lib().or_align_offset(a, 32) == b
+
+
+def test_matmul_2x2():  # tensor_utils.rs:608-620
+    y = O.matmul_b([1, 2, 3, 4], [5, 6, 7, 8], 2, 2)
+    assert y.ravel().tolist() == [19.0, 22.0, 43.0, 50.0]
+
+
+def test_f16_widening_exhaustive():
+    h = np.arange(65536, dtype=np.uint32).astype(np.uint16)
+    ref = h.view(np.float16).astype(np.float32)
+    got = np.array([O.half_to_float(int(x)) for x in h], dtype=np.float32)
+    nan = np.isnan(ref)
+    assert np.array_equal(np.isnan(got), nan)
+    assert np.array_equal(got[~nan].view(np.uint32), ref[~nan].view(np.uint32))
+
+
+def test_buffer_too_small():  # dequantize.rs:295-301, :250-256
+    with pytest.raises(ValueError):
+        O.dequantize(b"\x00" * 17, O.Q4_0, 32)
+    with pytest.raises(ValueError):
+        O.dequantize(b"\x00" * 7, O.F32, 2)
+
+
+def test_partial_block_truncates():  # dequantize.rs:324: result.truncate(nelements)
+    out = O.dequantize(blk_q8_0(1.0, list(range(32))), O.Q8_0, 20)
+    assert out.tolist() == [float(i) for i in range(20)]
+
+
+@pytest.mark.parametrize("qt", [O.Q4_0, O.Q4_1, O.Q8_0])
+def test_dequant_matches_gguf_py(qt):
+    gguf = pytest.importorskip("gguf")
+    from gguf import quants
+    rng = np.random.default_rng(qt)
+    ts = {O.Q4_0: 18, O.Q4_1: 20, O.Q8_0: 34}[qt]
+    nb = 4096
+    raw = rng.integers(0, 256, size=(nb, ts), dtype=np.uint8)
+    # finite, varied scales (including subnormals and negatives)
+    scales = rng.choice(np.array([1e-6, 3e-5, 0.01, 0.5, -2.0, 100.0, 6e-8], np.float16), nb * 2)
+    raw[:, 0:2] = scales[:nb].view(np.uint8).reshape(nb, 2)
+    if qt == O.Q4_1:
+        raw[:, 2:4] = scales[nb:].view(np.uint8).reshape(nb, 2)
+    mine = O.dequantize(raw.tobytes(), qt, nb * 32)
+    theirs = quants.dequantize(raw.reshape(-1), gguf.GGMLQuantizationType(qt)).astype(np.float32)
+    assert np.array_equal(mine, theirs.ravel())
+
+
+def test_quantized_matvec_scalar_semantics():
+    # layout A: y[r] = sum over blocks of (q-8)*d*x, Q4_1 unsupported
+    rng = np.random.default_rng(3)
+    m, k = 8, 64
+    raw = rng.integers(0, 256, size=(m * k // 32, 18), dtype=np.uint8)
+    raw[:, 0:2] = np.full(m * k // 32, 0.25, np.float16).view(np.uint8).reshape(-1, 2)
+    x = rng.standard_normal(k).astype(np.float32)
+    y = O.quantized_matvec(O.Q4_0, raw, x, m, k)
+    W = O.dequantize(raw.tobytes(), O.Q4_0, m * k).reshape(m, k).astype(np.float64)
+    assert np.allclose(y, W @ x, rtol=1e-5, atol=1e-5)
+    with pytest.raises(ValueError):
+        O.quantized_matvec(O.Q4_1, np.zeros(20 * 2, np.uint8), x, 1, 64)
+
+
+def test_swiglu_modes():
+    g = np.linspace(-3, 3, 16, dtype=np.float32)
+    u = np.ones(16, np.float32)
+    exact = O.swiglu(g, u, 0)
+    assert np.allclose(exact, g / (1 + np.exp(-g.astype(np.float64))), atol=1e-6)
+    approx = O.swiglu(g, u, 1)  # AVX2: exp(-g) ~ 1 - g, over full 8-lanes
+    assert np.allclose(approx, g * (1 / (1 + (1 - g))), atol=1e-6)
+
+
+def test_kat_fixture_file():
+    """The KAT fixture file (tests/golden/kats.json) replays through the oracle."""
+    with open(os.path.join(GOLD, "kats.json")) as f:
+        kats = json.load(f)
+    for k in kats["dequant"]:
+        out = O.dequantize(bytes.fromhex(k["hex"]), k["type"], k["n"])
+        assert out.tolist() == k["expect"], k["source"]

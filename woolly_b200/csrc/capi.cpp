@@ -1,0 +1,405 @@
+// extern "C" boundary (include/woolly_cuda.h).  Argument checks mirror the
+// reference's error behaviour; device work is stream-ordered.
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstring>
+#include <string>
+
+#include "common.h"
+#include "gguf.h"
+#include "kernels.cuh"
+#include "model.h"
+#include "qgemv.cuh"
+
+namespace wl {
+
+thread_local std::string g_err;
+void set_error(const std::string& m) { g_err = m; }
+
+int model_load(wl_ctx*, const char*, const wl_model_options*, wl_model**);
+void model_free(wl_model*);
+int session_create(wl_model*, wl_session**);
+int session_reset(wl_session*);
+void session_free(wl_session*);
+int forward(wl_model*, wl_session* const*, int, const uint32_t*, const int*, float*, int);
+int decode_step_device(wl_model*, wl_session* const*, int, const uint32_t*, float*, cudaStream_t);
+int decode_kernel_count(const wl_model*, int);
+int nccl_unique_id(void*);
+int nccl_comm_init(int, const void*, int, void**);
+int nccl_comm_destroy(void*);
+
+namespace {
+
+int bb(int t) { return t == WL_Q4_0 ? 18 : t == WL_Q4_1 ? 20 : t == WL_Q8_0 ? 34 : 0; }
+
+int sm_count() {
+  int dev = 0, n = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  return n > 0 ? n : 148;
+}
+
+// stream-ordered scratch for op-level calls
+struct Scratch {
+  void* p = nullptr;
+  cudaStream_t st;
+  explicit Scratch(cudaStream_t s) : st(s) {}
+  int alloc(size_t bytes) {
+    WL_CUDA_TRY(cudaMallocAsync(&p, std::max<size_t>(bytes, 16), st));
+    return WL_OK;
+  }
+  ~Scratch() {
+    if (p) cudaFreeAsync(p, st);
+  }
+};
+
+// y[b][n] = sum_k x[b][k] W(k, n) through the tensor-core GEMV, rows in chunks of 32
+int qgemv_op(int type, int layout, const uint8_t* W, int K, int N, const float* x, int B, float* y,
+             cudaStream_t st) {
+  const int S = bb(type);
+  const int pitch = layout == WL_LAYOUT_B ? N / 32 * S : K / 32 * S;
+  Scratch xh(st);
+  WL_TRY(xh.alloc((size_t)B * K * sizeof(__half)));
+  WL_TRY(launch_f32_to_f16(x, (__half*)xh.p, (size_t)B * K, st));
+  const bool fast = layout == WL_LAYOUT_B ? qgemv_b_fast_ok(type, K, N, pitch, W)
+                                          : qgemv_a_fast_ok(type, K, N, pitch, W);
+  if (!fast)
+    return launch_qgemv_generic(type, layout, W, K, N, pitch, (const __half*)xh.p, K, B, y, N,
+                                false, st);
+  const int gcols = qgemv_group_cols(layout);
+  const int groups = (N + gcols - 1) / gcols;
+  GemvArgs a;
+  a.type = type;
+  a.nseg = 1;
+  a.seg[0].W = W;
+  a.seg[0].N = N;
+  a.seg[0].pitch = pitch;
+  a.seg[0].groups = groups;
+  a.K = K;
+  a.total_cols = groups * gcols;
+  a.B = std::min(B, 32);
+  qgemv_plan(a, layout, sm_count(), &a.ksplit, &a.kchunk);
+  Scratch ws(st);
+  size_t wsf = qgemv_ws_floats(a.ksplit, std::min(B, 32), a.total_cols);
+  size_t cnt_bytes = (size_t)groups * sizeof(unsigned);
+  WL_TRY(ws.alloc(wsf * sizeof(float) + cnt_bytes + 256));
+  a.ws = (float*)ws.p;
+  a.counters = (unsigned*)((uint8_t*)ws.p + (wsf * sizeof(float) + 255) / 256 * 256);
+  WL_CUDA_TRY(cudaMemsetAsync(a.counters, 0, cnt_bytes, st));
+  for (int r0 = 0; r0 < B; r0 += 32) {
+    a.B = std::min(32, B - r0);
+    a.x = (const __half*)xh.p + (size_t)r0 * K;
+    a.ldx = K;
+    a.epi.kind = EPI_F32;
+    a.epi.y = y + (size_t)r0 * N;
+    a.epi.ldy = N;
+    WL_TRY(layout == WL_LAYOUT_B ? launch_qgemv_b(a, st) : launch_qgemv_a(a, st));
+  }
+  return WL_OK;
+}
+
+}  // namespace
+}  // namespace wl
+
+using namespace wl;
+
+extern "C" {
+
+const char* wl_last_error(void) { return g_err.c_str(); }
+const char* wl_version(void) { return "woolly-b200 0.1 (sm_100a)"; }
+
+size_t wl_block_size(int t) { return type_valid((uint32_t)t) ? type_block_size((uint32_t)t) : 0; }
+size_t wl_type_size(int t) { return type_valid((uint32_t)t) ? type_size((uint32_t)t) : 0; }
+
+// ---------------- GGUF ----------------
+struct wl_gguf {
+  GgufFile* f;
+};
+
+int wl_gguf_open(const char* path, wl_gguf** out) {
+  if (!path || !out) return fail(WL_ERR_INVALID_ARGUMENT, "null argument");
+  GgufFile* f = nullptr;
+  WL_TRY(gguf_open_file(path, &f));
+  *out = new wl_gguf{f};
+  return WL_OK;
+}
+
+int wl_gguf_open_memory(const void* bytes, size_t n, wl_gguf** out) {
+  if ((!bytes && n) || !out) return fail(WL_ERR_INVALID_ARGUMENT, "null argument");
+  GgufFile* f = nullptr;
+  WL_TRY(gguf_open_bytes((const uint8_t*)bytes, n, &f));
+  *out = new wl_gguf{f};
+  return WL_OK;
+}
+
+void wl_gguf_close(wl_gguf* g) {
+  if (!g) return;
+  delete g->f;
+  delete g;
+}
+
+int wl_gguf_header(const wl_gguf* g, uint32_t* version, uint64_t* tc, uint64_t* kvc,
+                   uint32_t* alignment, uint64_t* data_start) {
+  if (!g) return fail(WL_ERR_INVALID_ARGUMENT, "null gguf");
+  if (version) *version = g->f->version;
+  if (tc) *tc = g->f->tensor_count;
+  if (kvc) *kvc = g->f->kv_count;
+  if (alignment) *alignment = g->f->alignment;
+  if (data_start) *data_start = g->f->data_start;
+  return WL_OK;
+}
+
+int wl_gguf_tensor_count(const wl_gguf* g) { return g ? (int)g->f->tensors.size() : 0; }
+
+static void fill_info(const GgufTensor& t, wl_tensor_info* o) {
+  o->name = t.name.c_str();
+  o->n_dims = t.n_dims;
+  for (int i = 0; i < 4; i++) o->dims[i] = i < (int)t.n_dims ? t.dims[i] : 1;
+  o->ggml_type = t.type;
+  o->offset = t.offset;
+  o->nbytes = t.nbytes();
+}
+
+int wl_gguf_tensor(const wl_gguf* g, int i, wl_tensor_info* out) {
+  if (!g || !out || i < 0 || i >= (int)g->f->tensors.size())
+    return fail(WL_ERR_INVALID_ARGUMENT, "tensor index out of range");
+  fill_info(g->f->tensors[i], out);
+  return WL_OK;
+}
+
+int wl_gguf_find_tensor(const wl_gguf* g, const char* name, wl_tensor_info* out) {
+  if (!g || !name || !out) return fail(WL_ERR_INVALID_ARGUMENT, "null argument");
+  const GgufTensor* t = g->f->find(name);
+  if (!t) return fail(WL_ERR_TENSOR_NOT_FOUND, std::string("Tensor not found: ") + name);
+  fill_info(*t, out);
+  return WL_OK;
+}
+
+int wl_gguf_tensor_data(const wl_gguf* g, const char* name, const void** data, uint64_t* nbytes) {
+  if (!g || !name || !data) return fail(WL_ERR_INVALID_ARGUMENT, "null argument");
+  const GgufTensor* t = g->f->find(name);
+  if (!t) return fail(WL_ERR_TENSOR_NOT_FOUND, std::string("Tensor not found: ") + name);
+  const uint8_t* p = g->f->data(*t);
+  if (!p)
+    return fail(WL_ERR_BUFFER_TOO_SMALL, "Buffer too small: tensor data extends past end of file");
+  *data = p;
+  if (nbytes) *nbytes = t->nbytes();
+  return WL_OK;
+}
+
+int wl_gguf_get_u32(const wl_gguf* g, const char* key, uint32_t* out) {
+  if (!g || !key || !out) return fail(WL_ERR_INVALID_ARGUMENT, "null argument");
+  if (!g->f->get_u32(key, out)) return fail(WL_ERR_TENSOR_NOT_FOUND, std::string("no u32 key ") + key);
+  return WL_OK;
+}
+
+int wl_gguf_get_f32(const wl_gguf* g, const char* key, float* out) {
+  if (!g || !key || !out) return fail(WL_ERR_INVALID_ARGUMENT, "null argument");
+  if (!g->f->get_f32(key, out)) return fail(WL_ERR_TENSOR_NOT_FOUND, std::string("no f32 key ") + key);
+  return WL_OK;
+}
+
+int wl_gguf_get_str(const wl_gguf* g, const char* key, const char** out, uint64_t* len) {
+  if (!g || !key || !out) return fail(WL_ERR_INVALID_ARGUMENT, "null argument");
+  auto it = g->f->kv.find(key);
+  if (it == g->f->kv.end() || it->second.type != 8)
+    return fail(WL_ERR_TENSOR_NOT_FOUND, std::string("no string key ") + key);
+  *out = it->second.s.c_str();
+  if (len) *len = it->second.s.size();
+  return WL_OK;
+}
+
+// GGUFModelLoader::extract_config (woolly-core/src/model/loader.rs:104-156)
+int wl_gguf_model_config(const wl_gguf* g, wl_model_config* c) {
+  if (!g || !c) return fail(WL_ERR_INVALID_ARGUMENT, "null argument");
+  const GgufFile* f = g->f;
+  std::string arch;
+  if (!f->get_str("general.architecture", &arch))
+    return fail(WL_ERR_INVALID_FORMAT, "No architecture specified in GGUF");
+  memset(c, 0, sizeof(*c));
+  snprintf(c->architecture, sizeof(c->architecture), "%s", arch.c_str());
+  uint32_t u;
+  float x;
+  c->vocab_size = f->get_u32(arch + ".vocab_size", &u) ? u : (f->get_u32("tokenizer.ggml.tokens.len", &u) ? u : 32000);
+  c->hidden_size = f->get_u32(arch + ".embedding_length", &u) ? u : (f->get_u32(arch + ".embed_dim", &u) ? u : 4096);
+  c->num_layers = f->get_u32(arch + ".block_count", &u) ? u : (f->get_u32(arch + ".layer_count", &u) ? u : 32);
+  c->num_heads = f->get_u32(arch + ".attention.head_count", &u) ? u : 32;
+  c->context_length = f->get_u32(arch + ".context_length", &u) ? u : (f->get_u32("tokenizer.ggml.context_length", &u) ? u : 2048);
+  c->intermediate_size = f->get_u32(arch + ".feed_forward_length", &u) ? u : c->hidden_size * 4;
+  c->num_kv_heads_meta = f->get_u32(arch + ".attention.head_count_kv", &u) ? u : 0;
+  c->rope_theta = f->get_f32(arch + ".rope.freq_base", &x) ? x : (f->get_f32(arch + ".attention.rope_theta", &x) ? x : 0.f);
+  c->layer_norm_epsilon = f->get_f32(arch + ".attention.layer_norm_epsilon", &x) ? x : (f->get_f32(arch + ".layer_norm_epsilon", &x) ? x : 1e-5f);
+  return WL_OK;
+}
+
+// ---------------- device ops ----------------
+int wl_dequantize(int type, const void* blocks, size_t nbytes, size_t n, float* out, void* stream) {
+  if ((!blocks && n) || (!out && n)) return fail(WL_ERR_INVALID_ARGUMENT, "null pointer");
+  size_t need;
+  if (type == WL_F32 || type == WL_F16) {
+    need = n * (type == WL_F32 ? 4 : 2);
+    if (nbytes != need)  // dequantize.rs:250-283 require the exact length
+      return fail(WL_ERR_BUFFER_TOO_SMALL, "Buffer too small: needed " + std::to_string(need) +
+                                                " bytes, but only " + std::to_string(nbytes) + " available");
+  } else if (bb(type)) {
+    need = (n + 31) / 32 * bb(type);
+    if (nbytes < need)
+      return fail(WL_ERR_BUFFER_TOO_SMALL, "Buffer too small: needed " + std::to_string(need) +
+                                                " bytes, but only " + std::to_string(nbytes) + " available");
+  } else {
+    return fail(type_valid((uint32_t)type) ? WL_ERR_UNSUPPORTED : WL_ERR_INVALID_TENSOR_TYPE,
+                "dequantize: type " + std::to_string(type) + " not supported");
+  }
+  return launch_dequant(type, blocks, n, out, (cudaStream_t)stream);
+}
+
+int wl_qgemv(int type, int layout, const void* W, int K, int N, const float* x, int B, float* y,
+             void* stream) {
+  if (!W || !x || !y) return fail(WL_ERR_INVALID_ARGUMENT, "null pointer");
+  if (!bb(type)) return fail(WL_ERR_UNSUPPORTED, "qgemv: type must be Q4_0, Q4_1 or Q8_0");
+  if (layout != WL_LAYOUT_A && layout != WL_LAYOUT_B) return fail(WL_ERR_INVALID_ARGUMENT, "bad layout");
+  if (K <= 0 || N <= 0 || B <= 0) return fail(WL_ERR_INVALID_ARGUMENT, "K, N, B must be positive");
+  if ((layout == WL_LAYOUT_B ? N : K) % 32)
+    return fail(WL_ERR_INVALID_ARGUMENT, "the blocked dimension must be a multiple of 32");
+  return qgemv_op(type, layout, (const uint8_t*)W, K, N, x, B, y, (cudaStream_t)stream);
+}
+
+// quantization::simd::quantized_matvec (woolly-tensor/src/quantization.rs:869-909)
+int wl_quantized_matvec(int type, const void* W, const float* input, float* output, int m, int k,
+                        void* stream) {
+  if (type != WL_Q4_0 && type != WL_Q8_0)
+    return fail(WL_ERR_UNSUPPORTED, "Quantized matvec not implemented for this scheme");
+  if (k % 32) return fail(WL_ERR_INVALID_ARGUMENT, "k must be a multiple of 32");
+  if (m <= 0 || k <= 0) return fail(WL_ERR_INVALID_ARGUMENT, "m, k must be positive");
+  return wl_qgemv(type, WL_LAYOUT_A, W, k, m, input, 1, output, stream);
+}
+
+int wl_rmsnorm_rope(const float* x, const float* w, int rows, int dim, float eps, int rope_mode,
+                    const int* pos, int head_dim, float theta, void* y, int y_f16, void* stream) {
+  if (!x || !w || !y || rows < 0 || dim <= 0) return fail(WL_ERR_INVALID_ARGUMENT, "bad argument");
+  if (rope_mode == WL_ROPE_NEOX && !pos) return fail(WL_ERR_INVALID_ARGUMENT, "rope needs positions");
+  return launch_rmsnorm(x, w, rows, dim, eps, rope_mode == WL_ROPE_NEOX, pos, head_dim, theta, y,
+                        y_f16, (cudaStream_t)stream);
+}
+
+int wl_swiglu(const float* gate, const float* up, size_t n, float* out, void* stream) {
+  if (n && (!gate || !up || !out)) return fail(WL_ERR_INVALID_ARGUMENT, "null pointer");
+  return launch_swiglu(gate, up, n, out, (cudaStream_t)stream);
+}
+
+int wl_rope(const float* x, float* out, const int* positions, float base, int batch, int seq,
+            int heads, int head_dim, void* stream) {
+  if (!x || !out || !positions || head_dim % 2 || batch < 0 || seq < 0 || heads < 0)
+    return fail(WL_ERR_INVALID_ARGUMENT, "bad argument (head_dim must be even)");
+  return launch_rope(x, out, positions, base, batch, seq, heads, head_dim, (cudaStream_t)stream);
+}
+
+int wl_attention(const float* q, const float* k, const float* v, int rows, int past, int heads,
+                 int kv_heads, int head_dim, int window, float* out, void* stream) {
+  if (!q || !k || !v || !out || rows <= 0 || past < 0 || heads <= 0 || kv_heads <= 0)
+    return fail(WL_ERR_INVALID_ARGUMENT, "bad argument");
+  return launch_attention_f32(q, k, v, rows, past, heads, kv_heads, head_dim, window, out,
+                              (cudaStream_t)stream);
+}
+
+// ---------------- runtime ----------------
+void wl_model_options_default(wl_model_options* o) {
+  if (!o) return;
+  memset(o, 0, sizeof(*o));
+  o->rope_mode = WL_ROPE_OFF;
+  o->sliding_window = 0;
+  o->max_sessions = 16;
+  o->max_context = 2048;
+  o->max_batch = 16;
+  o->max_prefill = 512;
+  o->use_graphs = 1;
+  o->tp_rank = 0;
+  o->tp_size = 1;
+  o->nccl_comm = nullptr;
+}
+
+int wl_init(int device, wl_ctx** out) {
+  if (!out) return fail(WL_ERR_INVALID_ARGUMENT, "null argument");
+  *out = nullptr;
+  int n = 0;
+  cudaError_t e = cudaGetDeviceCount(&n);
+  if (e != cudaSuccess || n == 0)
+    return fail(WL_ERR_CUDA, std::string("no CUDA device: ") + cudaGetErrorString(e));
+  if (device < 0 || device >= n) return fail(WL_ERR_INVALID_ARGUMENT, "device index out of range");
+  WL_CUDA_TRY(cudaSetDevice(device));
+  cudaDeviceProp p;
+  WL_CUDA_TRY(cudaGetDeviceProperties(&p, device));
+  if (p.major < 10)
+    return fail(WL_ERR_UNSUPPORTED, std::string("woolly-b200 needs an sm_100 GPU, found ") + p.name);
+  auto* c = new wl_ctx();
+  c->device = device;
+  c->num_sms = p.multiProcessorCount;
+  e = cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking);
+  if (e != cudaSuccess) {
+    delete c;
+    return fail(WL_ERR_CUDA, cudaGetErrorString(e));
+  }
+  *out = c;
+  return WL_OK;
+}
+
+void wl_ctx_free(wl_ctx* c) {
+  if (!c) return;
+  cudaSetDevice(c->device);
+  cudaStreamDestroy(c->stream);
+  delete c;
+}
+
+int wl_model_load_gguf(wl_ctx* ctx, const char* path, const wl_model_options* o, wl_model** out) {
+  if (!out) return fail(WL_ERR_INVALID_ARGUMENT, "null argument");
+  return model_load(ctx, path, o, out);
+}
+
+void wl_model_free(wl_model* m) { model_free(m); }
+
+int wl_model_get_config(const wl_model* m, wl_model_config* out) {
+  if (!m || !out) return fail(WL_ERR_INVALID_ARGUMENT, "null argument");
+  *out = m->cfg;
+  return WL_OK;
+}
+
+int wl_model_memory(const wl_model* m, uint64_t* wb, uint64_t* kb) {
+  if (!m) return fail(WL_ERR_INVALID_ARGUMENT, "null model");
+  if (wb) *wb = m->weight_bytes;
+  if (kb) *kb = m->kv_bytes;
+  return WL_OK;
+}
+
+int wl_session_create(wl_model* m, wl_session** out) {
+  if (!out) return fail(WL_ERR_INVALID_ARGUMENT, "null argument");
+  return session_create(m, out);
+}
+void wl_session_free(wl_session* s) { session_free(s); }
+int wl_session_reset(wl_session* s) { return session_reset(s); }
+int wl_session_length(const wl_session* s) { return s ? s->len : -1; }
+
+int wl_forward(wl_model* m, wl_session* const* ss, int n, const uint32_t* ids, const int* n_ids,
+               float* logits, int mode) {
+  return forward(m, ss, n, ids, n_ids, logits, mode);
+}
+
+int wl_decode_step_device(wl_model* m, wl_session* const* ss, int n, const uint32_t* d_ids,
+                          float* d_logits, void* stream) {
+  return decode_step_device(m, ss, n, d_ids, d_logits, (cudaStream_t)stream);
+}
+
+int wl_decode_kernel_count(const wl_model* m, int n) { return m ? decode_kernel_count(m, n) : 0; }
+
+int wl_nccl_unique_id(void* out) {
+  if (!out) return fail(WL_ERR_INVALID_ARGUMENT, "null argument");
+  return nccl_unique_id(out);
+}
+int wl_nccl_comm_init(int nranks, const void* id, int rank, void** comm) {
+  if (!id || !comm) return fail(WL_ERR_INVALID_ARGUMENT, "null argument");
+  return nccl_comm_init(nranks, id, rank, comm);
+}
+int wl_nccl_comm_destroy(void* comm) { return nccl_comm_destroy(comm); }
+
+}  // extern "C"

@@ -1,0 +1,52 @@
+// Device kernels other than the quantized GEMV: attention, norms, misc ops.
+#pragma once
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "qgemv.cuh"
+
+namespace wl {
+
+// Attention over a paged f16 KV cache for `rows` query rows.
+struct AttnArgs {
+  const float* q = nullptr;  // [rows][H*hd] f32
+  int ldq = 0;
+  KvPages kv{};
+  const int* row_pos = nullptr;   // [rows]
+  const int* row_sess = nullptr;  // [rows]
+  int rows = 0, heads = 0, kv_heads = 0, head_dim = 0;
+  int window = 0;   // 0 = full causal prefix
+  int nsplit = 1;
+  float* part_o = nullptr;   // [rows][H][nsplit][hd]
+  float* part_ml = nullptr;  // [rows][H][nsplit][2]
+  void* out = nullptr;       // [rows][H*hd], f16 (out_f16) or f32
+  int ldo = 0;
+  int out_f16 = 1;
+};
+int launch_attention_paged(const AttnArgs& a, cudaStream_t st);
+
+// Same math over contiguous f32 K/V [past+rows][KVH*hd] (the reference's KV
+// cache layout, lazy_transformer.rs:322-434).
+int launch_attention_f32(const float* q, const float* k, const float* v, int rows, int past,
+                         int heads, int kv_heads, int hd, int window, float* out,
+                         cudaStream_t st);
+
+int attention_plan_splits(int rows, int kv_heads, int max_len, int num_sms);
+
+// y = x / sqrt(mean(x^2) + eps) * w per row; optional NeoX rope per head.
+int launch_rmsnorm(const float* x, const float* w, int rows, int dim, float eps, int rope,
+                   const int* pos, int head_dim, float theta, void* y, int y_f16,
+                   cudaStream_t st);
+
+// h[r][j] = E[j*V + ids[r]] (token_embd stored [d][V], lazy_transformer.rs:1252-1262)
+int launch_embed(const float* E, int d, int V, const uint32_t* ids, int rows, float* h,
+                 int* err_flag, cudaStream_t st);
+
+int launch_swiglu(const float* g, const float* u, size_t n, float* out, cudaStream_t st);
+int launch_rope(const float* x, float* out, const int* pos, float base, int batch, int seq,
+                int heads, int hd, cudaStream_t st);
+int launch_dequant(int type, const void* blocks, size_t n, float* out, cudaStream_t st);
+
+}  // namespace wl

@@ -1,0 +1,838 @@
+// Model runtime: GGUF -> HBM loader, paged-KV sessions, batched forward,
+// CUDA-graph decode, tensor-parallel sharding with NCCL allreduce.
+//
+// Replaces LazyTransformer (woolly-core/src/model/lazy_transformer.rs):
+//   from_gguf (:29-95)      -> wl_model_load_gguf: blocks uploaded unchanged
+//                              (a TP shard copies its column/row byte slice)
+//   process_layer (:98-258) -> run_rows(): RMSNorm -> fused QKV GEMV with
+//                              paged-KV append -> flash-decoding attention ->
+//                              o GEMV (+residual) -> RMSNorm -> gate/up GEMV
+//                              with SiLU*up epilogue -> down GEMV (+residual)
+//   forward (:1155-1336)    -> embedding gather, layers, final norm, LM head
+//   OptimizedKVCache        -> per-session page tables over a device page pool
+#include "model.h"
+
+#include <dlfcn.h>
+
+#include <algorithm>
+#include <cstring>
+#include <string>
+
+#include "common.h"
+
+namespace wl {
+namespace {
+
+// ---- NCCL, resolved at run time so single-GPU use needs no NCCL ----
+struct Nccl {
+  bool ok = false;
+  int (*GetUniqueId)(void*) = nullptr;
+  int (*CommInitRank)(void**, int, /*ncclUniqueId by value*/ ...) = nullptr;
+  int (*AllReduce)(const void*, void*, size_t, int, int, void*, cudaStream_t) = nullptr;
+  int (*CommDestroy)(void*) = nullptr;
+  int (*CommAbort)(void*) = nullptr;
+  const char* (*GetErrorString)(int) = nullptr;
+};
+
+Nccl& nccl() {
+  static Nccl n;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+    if (!h) h = dlopen("libnccl.so", RTLD_NOW | RTLD_GLOBAL);
+    if (!h) return;
+    n.GetUniqueId = (int (*)(void*))dlsym(h, "ncclGetUniqueId");
+    n.CommInitRank = (int (*)(void**, int, ...))dlsym(h, "ncclCommInitRank");
+    n.AllReduce = (int (*)(const void*, void*, size_t, int, int, void*, cudaStream_t))dlsym(
+        h, "ncclAllReduce");
+    n.CommDestroy = (int (*)(void*))dlsym(h, "ncclCommDestroy");
+    n.CommAbort = (int (*)(void*))dlsym(h, "ncclCommAbort");
+    n.GetErrorString = (const char* (*)(int))dlsym(h, "ncclGetErrorString");
+    n.ok = n.GetUniqueId && n.CommInitRank && n.AllReduce && n.CommDestroy;
+  });
+  return n;
+}
+
+struct UniqueId {
+  char internal[128];
+};
+
+int block_bytes(uint32_t t) { return t == WL_Q4_0 ? 18 : t == WL_Q4_1 ? 20 : t == WL_Q8_0 ? 34 : 0; }
+
+size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+// One tensor's placement in the device weight buffer and how to fill it.
+struct Piece {
+  const uint8_t* src = nullptr;  // host bytes (mmap)
+  size_t src_pitch = 0;          // bytes per source row
+  size_t col_byte0 = 0;          // first byte of the slice within a row
+  size_t row_bytes = 0;          // bytes copied per row
+  size_t rows = 0;               // rows copied (starting at row0)
+  size_t row0 = 0;
+  size_t dst_pitch = 0;
+  size_t dst_off = 0;
+  size_t dst_bytes = 0;
+};
+
+int upload_pieces(uint8_t* dbase, const std::vector<Piece>& ps, cudaStream_t st) {
+  // contiguous pieces go straight from the mapping; sliced ones are packed
+  // row by row into a pinned staging buffer first.
+  const size_t kStage = 64u << 20;
+  uint8_t* stage = nullptr;
+  WL_CUDA_TRY(cudaMallocHost(&stage, 2 * kStage));
+  cudaEvent_t ev[2];
+  cudaEventCreateWithFlags(&ev[0], cudaEventDisableTiming);
+  cudaEventCreateWithFlags(&ev[1], cudaEventDisableTiming);
+  int which = 0;
+  bool used[2] = {false, false};
+  int st_code = WL_OK;
+  for (const Piece& p : ps) {
+    bool contiguous = p.src_pitch == p.row_bytes && p.dst_pitch == p.row_bytes && p.col_byte0 == 0;
+    if (contiguous) {
+      const uint8_t* src = p.src + p.row0 * p.src_pitch;
+      size_t total = p.rows * p.row_bytes;
+      for (size_t off = 0; off < total; off += kStage) {
+        size_t n = std::min(kStage, total - off);
+        if (used[which]) cudaEventSynchronize(ev[which]);
+        memcpy(stage + which * kStage, src + off, n);
+        cudaError_t e = cudaMemcpyAsync(dbase + p.dst_off + off, stage + which * kStage, n,
+                                        cudaMemcpyHostToDevice, st);
+        if (e != cudaSuccess) {
+          st_code = fail(WL_ERR_CUDA, std::string("weight upload: ") + cudaGetErrorString(e));
+          break;
+        }
+        cudaEventRecord(ev[which], st);
+        used[which] = true;
+        which ^= 1;
+      }
+    } else {
+      size_t rows_per = std::max<size_t>(1, kStage / p.dst_pitch);
+      for (size_t r = 0; r < p.rows; r += rows_per) {
+        size_t nr = std::min(rows_per, p.rows - r);
+        if (used[which]) cudaEventSynchronize(ev[which]);
+        uint8_t* s = stage + which * kStage;
+        memset(s, 0, nr * p.dst_pitch);
+        for (size_t i = 0; i < nr; i++)
+          memcpy(s + i * p.dst_pitch, p.src + (p.row0 + r + i) * p.src_pitch + p.col_byte0,
+                 p.row_bytes);
+        cudaError_t e = cudaMemcpyAsync(dbase + p.dst_off + r * p.dst_pitch, s, nr * p.dst_pitch,
+                                        cudaMemcpyHostToDevice, st);
+        if (e != cudaSuccess) {
+          st_code = fail(WL_ERR_CUDA, std::string("weight upload: ") + cudaGetErrorString(e));
+          break;
+        }
+        cudaEventRecord(ev[which], st);
+        used[which] = true;
+        which ^= 1;
+      }
+    }
+    if (st_code) break;
+  }
+  cudaStreamSynchronize(st);
+  cudaEventDestroy(ev[0]);
+  cudaEventDestroy(ev[1]);
+  cudaFreeHost(stage);
+  return st_code;
+}
+
+struct Loader {
+  GgufFile* g;
+  wl_model* m;
+  std::vector<Piece> pieces;
+  size_t cursor = 0;
+  std::string err;
+
+  const GgufTensor* need(const std::string& name) {
+    const GgufTensor* t = g->find(name);
+    if (!t) err = "Tensor not found: " + name;
+    return t;
+  }
+  // reserve a device region, 256-byte aligned, with 256 spare bytes
+  size_t reserve(size_t bytes) {
+    size_t off = cursor;
+    cursor = align_up(cursor + bytes + 256, 256);
+    return off;
+  }
+  // f32 vector / matrix copied whole
+  bool add_f32(const std::string& name, uint64_t expect, size_t* off) {
+    const GgufTensor* t = need(name);
+    if (!t) return false;
+    if (t->type != WL_F32) {
+      err = name + ": expected F32, got type " + std::to_string(t->type);
+      return false;
+    }
+    if (t->nelems() != expect) {
+      err = name + ": unexpected element count " + std::to_string(t->nelems());
+      return false;
+    }
+    const uint8_t* src = g->data(*t);
+    if (!src) {
+      err = name + ": data out of bounds";
+      return false;
+    }
+    Piece p;
+    p.src = src;
+    p.src_pitch = p.row_bytes = p.dst_pitch = t->nbytes();
+    p.rows = 1;
+    p.dst_bytes = t->nbytes();
+    p.dst_off = *off = reserve(p.dst_bytes);
+    pieces.push_back(p);
+    return true;
+  }
+  // layout-B matrix [K][N] (dims [K, N]); keeps rows [r0, r0+Kl) and
+  // columns [c0, c0+Nl) (c0, Nl multiples of 32).
+  bool add_mat(const std::string& name, int K, int N, int r0, int Kl, int c0, int Nl, QMat* out,
+               size_t* off) {
+    const GgufTensor* t = need(name);
+    if (!t) return false;
+    if (t->n_dims != 2 || t->dims[0] != (uint64_t)K || t->dims[1] != (uint64_t)N) {
+      err = name + ": expected dims [" + std::to_string(K) + ", " + std::to_string(N) + "]";
+      return false;
+    }
+    const uint8_t* src = g->data(*t);
+    if (!src) {
+      err = name + ": data out of bounds";
+      return false;
+    }
+    Piece p;
+    p.src = src;
+    p.rows = (size_t)Kl;
+    p.row0 = (size_t)r0;
+    if (t->type == WL_F32) {
+      p.src_pitch = (size_t)N * 4;
+      p.col_byte0 = (size_t)c0 * 4;
+      p.row_bytes = (size_t)Nl * 4;
+      p.dst_pitch = align_up(p.row_bytes, 16);
+    } else {
+      int S = block_bytes(t->type);
+      if (!S) {
+        err = name + ": weight type " + std::to_string(t->type) +
+              " is not supported (F32, Q4_0, Q4_1, Q8_0)";
+        return false;
+      }
+      if (N % 32 || c0 % 32 || Nl % 32) {
+        err = name + ": quantized columns must be multiples of 32";
+        return false;
+      }
+      p.src_pitch = (size_t)N / 32 * S;
+      p.col_byte0 = (size_t)c0 / 32 * S;
+      p.row_bytes = (size_t)Nl / 32 * S;
+      p.dst_pitch = align_up(p.row_bytes, 16);
+    }
+    p.dst_bytes = p.dst_pitch * p.rows;
+    p.dst_off = *off = reserve(p.dst_bytes);
+    pieces.push_back(p);
+    out->type = t->type;
+    out->K = Kl;
+    out->N = Nl;
+    out->pitch = (int)p.dst_pitch;
+    return true;
+  }
+};
+
+template <class T>
+int dalloc(T** p, size_t n) {
+  WL_CUDA_TRY(cudaMalloc((void**)p, std::max<size_t>(n, 1) * sizeof(T)));
+  return WL_OK;
+}
+
+}  // namespace
+
+int nccl_unique_id(void* out128) {
+  Nccl& n = nccl();
+  if (!n.ok) return fail(WL_ERR_NCCL, "NCCL library not available");
+  int r = n.GetUniqueId(out128);
+  if (r) return fail(WL_ERR_NCCL, std::string("ncclGetUniqueId: ") + n.GetErrorString(r));
+  return WL_OK;
+}
+
+int nccl_comm_init(int nranks, const void* id128, int rank, void** comm) {
+  Nccl& n = nccl();
+  if (!n.ok) return fail(WL_ERR_NCCL, "NCCL library not available");
+  UniqueId id;
+  memcpy(id.internal, id128, 128);
+  using Fn = int (*)(void**, int, UniqueId, int);
+  int r = ((Fn)n.CommInitRank)(comm, nranks, id, rank);
+  if (r) return fail(WL_ERR_NCCL, std::string("ncclCommInitRank: ") + n.GetErrorString(r));
+  return WL_OK;
+}
+
+int nccl_comm_destroy(void* comm) {
+  Nccl& n = nccl();
+  if (!n.ok || !comm) return WL_OK;
+  n.CommDestroy(comm);
+  return WL_OK;
+}
+
+static int allreduce_sum(wl_model* m, float* buf, size_t count) {
+  Nccl& n = nccl();
+  // ncclFloat32 = 7, ncclSum = 0
+  int r = n.AllReduce(buf, buf, count, 7, 0, m->nccl, m->st);
+  if (r) return fail(WL_ERR_NCCL, std::string("ncclAllReduce: ") + n.GetErrorString(r));
+  return WL_OK;
+}
+
+// ------------------------------------------------------------------ GEMV dispatch
+// y rows r in [0, R): up to 32 rows per launch.
+static int gemv(wl_model* m, int nseg, const QMat* mats, int R, const __half* x, int ldx,
+                Epilogue epi, int ldy_elems, size_t y_elem_bytes) {
+  for (int s = 0; s < nseg; s++)
+    if (mats[s].type != mats[0].type)
+      return fail(WL_ERR_UNSUPPORTED, "fused GEMV segments must share a quantization type");
+  const bool quant = block_bytes(mats[0].type) != 0;
+  for (int r0 = 0; r0 < R; r0 += 32) {
+    const int b = std::min(32, R - r0);
+    Epilogue e = epi;
+    if (e.y) e.y = (uint8_t*)e.y + (size_t)r0 * ldy_elems * y_elem_bytes;
+    if (e.row_pos) e.row_pos += r0;
+    if (e.row_sess) e.row_sess += r0;
+    const __half* xr = x + (size_t)r0 * ldx;
+    bool fast = quant;
+    for (int s = 0; s < nseg && fast; s++)
+      fast = qgemv_b_fast_ok(mats[s].type, mats[s].K, mats[s].N, mats[s].pitch, mats[s].w);
+    if (!fast) {
+      if (nseg != 1 || !(e.kind == EPI_F32 || e.kind == EPI_ADD))
+        return fail(WL_ERR_UNSUPPORTED, "GEMV: unaligned or F32 weights only support plain outputs");
+      WL_TRY(launch_qgemv_generic(mats[0].type, WL_LAYOUT_B, mats[0].w, mats[0].K, mats[0].N,
+                                  mats[0].pitch, xr, ldx, b, (float*)e.y, e.ldy,
+                                  e.kind == EPI_ADD, m->st));
+      continue;
+    }
+    GemvArgs a;
+    a.type = (int)mats[0].type;
+    a.nseg = nseg;
+    int gb = 0;
+    for (int s = 0; s < nseg; s++) {
+      a.seg[s].W = mats[s].w;
+      a.seg[s].N = mats[s].N;
+      a.seg[s].pitch = mats[s].pitch;
+      a.seg[s].groups = (mats[s].N + 255) / 256;
+      a.seg[s].group_base = gb;
+      gb += a.seg[s].groups;
+    }
+    a.K = mats[0].K;
+    a.B = b;
+    a.x = xr;
+    a.ldx = ldx;
+    a.total_cols = gb * 256;
+    a.epi = e;
+    qgemv_plan(a, WL_LAYOUT_B, m->sms, &a.ksplit, &a.kchunk);
+    if (qgemv_ws_floats(a.ksplit, b, a.total_cols) > m->ws_floats || gb > m->n_counters)
+      return fail(WL_ERR_INVALID_ARGUMENT, "GEMV workspace too small");
+    a.ws = m->ws;
+    a.counters = m->counters;
+    WL_TRY(launch_qgemv_b(a, m->st));
+  }
+  return WL_OK;
+}
+
+// The whole forward for R rows whose ids/positions/sessions are on device.
+// Logits are produced for rows [lfirst, R) into m->logits (row 0 = lfirst).
+static int run_rows(wl_model* m, int R, int nsplit, int lfirst) {
+  cudaStream_t st = m->st;
+  const bool tp = m->tp_size > 1;
+  WL_TRY(launch_embed(m->embd, m->d, m->V, m->ids, R, m->h, m->err, st));
+  for (int l = 0; l < m->L; l++) {
+    const Layer& y = m->layers[l];
+    WL_TRY(launch_rmsnorm(m->h, y.attn_norm, R, m->d, m->eps, 0, nullptr, 0, 0.f, m->xn, 1, st));
+    KvPages kv;
+    kv.k = reinterpret_cast<__half*>(m->kvbuf + (size_t)l * 2 * m->n_pages * m->page * m->kvdl * 2);
+    kv.v = kv.k + (size_t)m->n_pages * m->page * m->kvdl;
+    kv.page_table = m->d_tables;
+    kv.max_pages = m->max_pages;
+    kv.page = m->page;
+    kv.kvd = m->kvdl;
+    {
+      Epilogue e;
+      e.kind = EPI_QKV;
+      e.y = m->q;
+      e.ldy = m->Hl * m->hd;
+      e.rope = m->rope;
+      e.head_dim = m->hd;
+      e.theta = m->theta;
+      e.row_pos = m->row_pos;
+      e.row_sess = m->row_sess;
+      e.kv = kv;
+      QMat segs[3] = {y.wq, y.wk, y.wv};
+      WL_TRY(gemv(m, 3, segs, R, m->xn, m->d, e, e.ldy, 4));
+    }
+    {
+      AttnArgs a;
+      a.q = m->q;
+      a.ldq = m->Hl * m->hd;
+      a.kv = kv;
+      a.row_pos = m->row_pos;
+      a.row_sess = m->row_sess;
+      a.rows = R;
+      a.heads = m->Hl;
+      a.kv_heads = m->KVHl;
+      a.head_dim = m->hd;
+      a.window = m->window;
+      a.nsplit = nsplit;
+      a.part_o = m->part_o;
+      a.part_ml = m->part_ml;
+      a.out = m->att;
+      a.ldo = m->Hl * m->hd;
+      a.out_f16 = 1;
+      WL_TRY(launch_attention_paged(a, st));
+    }
+    {
+      Epilogue e;
+      e.kind = (tp && m->tp_rank != 0) ? EPI_F32 : EPI_ADD;  // rank 0 carries the residual
+      e.y = m->h;
+      e.ldy = m->d;
+      WL_TRY(gemv(m, 1, &y.wo, R, m->att, m->Hl * m->hd, e, m->d, 4));
+      if (tp) WL_TRY(allreduce_sum(m, m->h, (size_t)R * m->d));
+    }
+    WL_TRY(launch_rmsnorm(m->h, y.ffn_norm, R, m->d, m->eps, 0, nullptr, 0, 0.f, m->xn, 1, st));
+    {
+      Epilogue e;
+      e.kind = EPI_SWIGLU;
+      e.y = m->act;
+      e.ldy = m->ffl;
+      QMat segs[2] = {y.wg, y.wu};
+      WL_TRY(gemv(m, 2, segs, R, m->xn, m->d, e, m->ffl, 2));
+    }
+    {
+      Epilogue e;
+      e.kind = (tp && m->tp_rank != 0) ? EPI_F32 : EPI_ADD;
+      e.y = m->h;
+      e.ldy = m->d;
+      WL_TRY(gemv(m, 1, &y.wd, R, m->act, m->ffl, e, m->d, 4));
+      if (tp) WL_TRY(allreduce_sum(m, m->h, (size_t)R * m->d));
+    }
+  }
+  const int nl = R - lfirst;
+  if (nl > 0) {
+    WL_TRY(launch_rmsnorm(m->h + (size_t)lfirst * m->d, m->out_norm, nl, m->d, m->eps, 0, nullptr,
+                          0, 0.f, m->xn, 1, st));
+    Epilogue e;
+    e.kind = EPI_F32;
+    e.y = m->logits;
+    e.ldy = m->V;
+    WL_TRY(gemv(m, 1, &m->out, nl, m->xn, m->d, e, m->V, 4));
+  }
+  return WL_OK;
+}
+
+static int ensure_pages(wl_model* m, wl_session* s, int upto) {
+  int need = (upto + m->page - 1) / m->page;
+  if (need > m->max_pages)
+    return fail(WL_ERR_CONTEXT_FULL, "session context full: " + std::to_string(upto) + " > " +
+                                         std::to_string(m->max_pages * m->page) + " tokens");
+  int first_new = (int)s->pages.size();
+  while ((int)s->pages.size() < need) {
+    if (m->free_pages.empty()) return fail(WL_ERR_OUT_OF_MEMORY, "KV page pool exhausted");
+    int pg = m->free_pages.back();
+    m->free_pages.pop_back();
+    m->h_tables[(size_t)s->slot * m->max_pages + s->pages.size()] = pg;
+    s->pages.push_back(pg);
+  }
+  if ((int)s->pages.size() > first_new) {
+    size_t off = (size_t)s->slot * m->max_pages + first_new;
+    WL_CUDA_TRY(cudaMemcpyAsync(m->d_tables + off, m->h_tables.data() + off,
+                                (s->pages.size() - first_new) * sizeof(int),
+                                cudaMemcpyHostToDevice, m->st));
+  }
+  return WL_OK;
+}
+
+static int upload_meta(wl_model* m, int R) {
+  WL_CUDA_TRY(cudaMemcpyAsync(m->ids, m->h_meta, (size_t)R * 4, cudaMemcpyHostToDevice, m->st));
+  WL_CUDA_TRY(cudaMemcpyAsync(m->row_pos, m->h_meta + m->MR, (size_t)R * 4,
+                              cudaMemcpyHostToDevice, m->st));
+  WL_CUDA_TRY(cudaMemcpyAsync(m->row_sess, m->h_meta + 2 * m->MR, (size_t)R * 4,
+                              cudaMemcpyHostToDevice, m->st));
+  return WL_OK;
+}
+
+// one batched decode step over B sessions whose metadata is already on device
+static int decode_launch(wl_model* m, int B) {
+  if (!m->opt.use_graphs) {
+    int max_len = 0;
+    for (int i = 0; i < B; i++) max_len = std::max(max_len, m->h_meta[m->MR + i] + 1);
+    return run_rows(m, B, attention_plan_splits(B, m->KVHl, max_len, m->sms), 0);
+  }
+  const int nsplit = attention_plan_splits(B, m->KVHl, m->opt.max_context, m->sms);
+  auto it = m->graphs.find(B);
+  if (it == m->graphs.end()) {
+    if (m->graph_warm[B]++ == 0) return run_rows(m, B, nsplit, 0);  // first call runs eagerly
+    cudaGraph_t g;
+    WL_CUDA_TRY(cudaStreamBeginCapture(m->st, cudaStreamCaptureModeThreadLocal));
+    int rs = run_rows(m, B, nsplit, 0);
+    cudaError_t ce = cudaStreamEndCapture(m->st, &g);
+    if (rs) return rs;
+    if (ce != cudaSuccess) return fail(WL_ERR_CUDA, std::string("graph capture: ") + cudaGetErrorString(ce));
+    cudaGraphExec_t ex;
+    cudaError_t ie = cudaGraphInstantiate(&ex, g, 0);
+    cudaGraphDestroy(g);
+    if (ie != cudaSuccess) return fail(WL_ERR_CUDA, std::string("graph instantiate: ") + cudaGetErrorString(ie));
+    it = m->graphs.emplace(B, ex).first;
+  }
+  WL_CUDA_TRY(cudaGraphLaunch(it->second, m->st));
+  return WL_OK;
+}
+
+static int check_sessions(wl_model* m, wl_session* const* ss, int n) {
+  WL_CHECK_ARG(n >= 1, "n_sess must be >= 1");
+  for (int i = 0; i < n; i++) {
+    WL_CHECK_ARG(ss[i] && ss[i]->m == m, "session does not belong to this model");
+    for (int j = 0; j < i; j++) WL_CHECK_ARG(ss[i] != ss[j], "a session appears twice in one call");
+  }
+  return WL_OK;
+}
+
+// ------------------------------------------------------------------ public (C++)
+int model_load(wl_ctx* ctx, const char* path, const wl_model_options* o, wl_model** out) {
+  *out = nullptr;
+  WL_CHECK_ARG(ctx && path, "null argument");
+  wl_model_options opt;
+  wl_model_options_default(&opt);
+  if (o) opt = *o;
+  WL_CHECK_ARG(opt.max_sessions >= 1 && opt.max_context >= 1 && opt.max_batch >= 1 &&
+                   opt.max_prefill >= 1,
+               "model options: sizes must be >= 1");
+  WL_CHECK_ARG(opt.tp_size >= 1 && opt.tp_rank >= 0 && opt.tp_rank < opt.tp_size,
+               "model options: bad tensor-parallel rank/size");
+  WL_CUDA_TRY(cudaSetDevice(ctx->device));
+  GgufFile* g = nullptr;
+  WL_TRY(gguf_open_file(path, &g));
+  std::unique_ptr<GgufFile> gh(g);
+  auto m = std::make_unique<wl_model>();
+  m->ctx = ctx;
+  m->dev = ctx->device;
+  m->sms = ctx->num_sms;
+  m->st = ctx->stream;
+  m->opt = opt;
+  m->tp_rank = opt.tp_rank;
+  m->tp_size = opt.tp_size;
+  m->nccl = opt.nccl_comm;
+  if (m->tp_size > 1 && (!m->nccl || !nccl().ok))
+    return fail(WL_ERR_NCCL, "tensor parallel load needs an NCCL communicator");
+  // config, GGUFModelLoader::extract_config (model/loader.rs:104-156)
+  std::string arch;
+  if (!g->get_str("general.architecture", &arch))
+    return fail(WL_ERR_INVALID_FORMAT, "No architecture specified in GGUF");
+  wl_model_config& c = m->cfg;
+  memset(&c, 0, sizeof(c));
+  snprintf(c.architecture, sizeof(c.architecture), "%s", arch.c_str());
+  uint32_t u;
+  float f;
+  c.vocab_size = g->get_u32(arch + ".vocab_size", &u) ? u : (g->get_u32("tokenizer.ggml.tokens.len", &u) ? u : 32000);
+  c.hidden_size = g->get_u32(arch + ".embedding_length", &u) ? u : (g->get_u32(arch + ".embed_dim", &u) ? u : 4096);
+  c.num_layers = g->get_u32(arch + ".block_count", &u) ? u : (g->get_u32(arch + ".layer_count", &u) ? u : 32);
+  c.num_heads = g->get_u32(arch + ".attention.head_count", &u) ? u : 32;
+  c.context_length = g->get_u32(arch + ".context_length", &u) ? u : (g->get_u32("tokenizer.ggml.context_length", &u) ? u : 2048);
+  c.intermediate_size = g->get_u32(arch + ".feed_forward_length", &u) ? u : c.hidden_size * 4;
+  c.num_kv_heads_meta = g->get_u32(arch + ".attention.head_count_kv", &u) ? u : 0;
+  c.rope_theta = g->get_f32(arch + ".rope.freq_base", &f) ? f : (g->get_f32(arch + ".attention.rope_theta", &f) ? f : 0.f);
+  c.layer_norm_epsilon = g->get_f32(arch + ".attention.layer_norm_epsilon", &f) ? f : (g->get_f32(arch + ".layer_norm_epsilon", &f) ? f : 1e-5f);
+  m->d = (int)c.hidden_size;
+  m->L = (int)c.num_layers;
+  m->H = (int)c.num_heads;
+  m->V = (int)c.vocab_size;
+  m->eps = c.layer_norm_epsilon;
+  m->theta = c.rope_theta > 0 ? c.rope_theta : 10000.f;
+  m->rope = opt.rope_mode == WL_ROPE_NEOX;
+  if (m->H <= 0 || m->d % m->H) return fail(WL_ERR_INVALID_FORMAT, "hidden size not divisible by heads");
+  m->hd = m->d / m->H;
+  // KV width from attn_k's shape (lazy_transformer.rs:284-287); FFN from ffn_gate (:496)
+  const GgufTensor* tk = g->find("blk.0.attn_k.weight");
+  const GgufTensor* tg = g->find("blk.0.ffn_gate.weight");
+  if (!tk || !tg || tk->n_dims != 2 || tg->n_dims != 2)
+    return fail(WL_ERR_TENSOR_NOT_FOUND, "Tensor not found: blk.0.attn_k.weight / ffn_gate.weight");
+  m->kvd = (int)tk->dims[1];
+  m->ff = (int)tg->dims[1];
+  if (m->kvd % m->hd) return fail(WL_ERR_INVALID_FORMAT, "attn_k width not a multiple of head_dim");
+  m->KVH = m->kvd / m->hd;
+  if (m->H % m->KVH) return fail(WL_ERR_INVALID_FORMAT, "heads not divisible by kv heads");
+  uint32_t sw = 0;
+  if (opt.sliding_window > 0)
+    m->window = opt.sliding_window;
+  else if (opt.sliding_window == 0 && g->get_u32(arch + ".attention.sliding_window", &sw))
+    m->window = (int)sw;
+  // tensor-parallel shard sizes
+  const int T = m->tp_size, rk = m->tp_rank;
+  if (m->H % T || m->KVH % T || m->ff % (32 * T))
+    return fail(WL_ERR_INVALID_ARGUMENT, "tp_size must divide heads, kv heads and ffn/32");
+  m->Hl = m->H / T;
+  m->KVHl = m->KVH / T;
+  m->kvdl = m->KVHl * m->hd;
+  m->ffl = m->ff / T;
+  if ((m->hd % 32) || (m->Hl * m->hd) % 32 || m->kvdl % 32)
+    return fail(WL_ERR_UNSUPPORTED, "head_dim must be a multiple of 32");
+  if (m->rope && 256 % m->hd)
+    return fail(WL_ERR_UNSUPPORTED, "fused RoPE needs head_dim dividing 256");
+
+  // ---- plan the weight buffer ----
+  Loader ld{g, m.get()};
+  const int d = m->d, kvd = m->kvd, ff = m->ff, V = m->V;
+  size_t off_embd, off_onorm, off_out;
+  bool ok = ld.add_f32("token_embd.weight", (uint64_t)d * V, &off_embd) &&
+            ld.add_f32("output_norm.weight", (uint64_t)d, &off_onorm);
+  bool tied = ok && !g->find("output.weight");
+  if (ok && !tied) ok = ld.add_mat("output.weight", d, V, 0, d, 0, V, &m->out, &off_out);
+  struct LOff {
+    size_t an, fn, q, k, v, o, g, u, dn;
+  };
+  std::vector<LOff> lo(m->L);
+  m->layers.resize(m->L);
+  for (int l = 0; l < m->L && ok; l++) {
+    std::string p = "blk." + std::to_string(l) + ".";
+    Layer& y = m->layers[l];
+    LOff& z = lo[l];
+    const int qc = m->Hl * m->hd;
+    ok = ld.add_f32(p + "attn_norm.weight", d, &z.an) && ld.add_f32(p + "ffn_norm.weight", d, &z.fn) &&
+         ld.add_mat(p + "attn_q.weight", d, d, 0, d, rk * qc, qc, &y.wq, &z.q) &&
+         ld.add_mat(p + "attn_k.weight", d, kvd, 0, d, rk * m->kvdl, m->kvdl, &y.wk, &z.k) &&
+         ld.add_mat(p + "attn_v.weight", d, kvd, 0, d, rk * m->kvdl, m->kvdl, &y.wv, &z.v) &&
+         ld.add_mat(p + "attn_output.weight", d, d, rk * qc, qc, 0, d, &y.wo, &z.o) &&
+         ld.add_mat(p + "ffn_gate.weight", d, ff, 0, d, rk * m->ffl, m->ffl, &y.wg, &z.g) &&
+         ld.add_mat(p + "ffn_up.weight", d, ff, 0, d, rk * m->ffl, m->ffl, &y.wu, &z.u) &&
+         ld.add_mat(p + "ffn_down.weight", ff, d, rk * m->ffl, m->ffl, 0, d, &y.wd, &z.dn);
+  }
+  if (!ok) return fail(ld.err.rfind("Tensor not found", 0) == 0 ? WL_ERR_TENSOR_NOT_FOUND : WL_ERR_INVALID_FORMAT, ld.err);
+  m->weight_bytes = ld.cursor;
+  WL_CUDA_TRY(cudaMalloc(&m->dweights, m->weight_bytes));
+  {
+    int s = upload_pieces(m->dweights, ld.pieces, m->st);
+    if (s) return s;
+  }
+  uint8_t* B = m->dweights;
+  m->embd = (const float*)(B + off_embd);
+  m->out_norm = (const float*)(B + off_onorm);
+  if (tied) {
+    m->out.w = B + off_embd;
+    m->out.type = WL_F32;
+    m->out.K = d;
+    m->out.N = V;
+    m->out.pitch = V * 4;
+  } else {
+    m->out.w = B + off_out;
+  }
+  for (int l = 0; l < m->L; l++) {
+    Layer& y = m->layers[l];
+    LOff& z = lo[l];
+    y.attn_norm = (const float*)(B + z.an);
+    y.ffn_norm = (const float*)(B + z.fn);
+    y.wq.w = B + z.q;
+    y.wk.w = B + z.k;
+    y.wv.w = B + z.v;
+    y.wo.w = B + z.o;
+    y.wg.w = B + z.g;
+    y.wu.w = B + z.u;
+    y.wd.w = B + z.dn;
+  }
+  // ---- KV page pool ----
+  m->max_sessions = opt.max_sessions;
+  m->max_pages = (opt.max_context + m->page - 1) / m->page;
+  m->n_pages = m->max_sessions * m->max_pages;
+  m->kv_bytes = (size_t)m->L * 2 * m->n_pages * m->page * m->kvdl * sizeof(__half);
+  WL_CUDA_TRY(cudaMalloc(&m->kvbuf, m->kv_bytes));
+  WL_CUDA_TRY(cudaMemsetAsync(m->kvbuf, 0, m->kv_bytes, m->st));
+  m->free_pages.resize(m->n_pages);
+  for (int i = 0; i < m->n_pages; i++) m->free_pages[i] = m->n_pages - 1 - i;
+  m->h_tables.assign((size_t)m->max_sessions * m->max_pages, 0);
+  WL_TRY(dalloc(&m->d_tables, m->h_tables.size()));
+  WL_CUDA_TRY(cudaMemsetAsync(m->d_tables, 0, m->h_tables.size() * sizeof(int), m->st));
+  m->slots.assign(m->max_sessions, nullptr);
+  // ---- scratch ----
+  const int MR = m->MR = std::max(opt.max_batch, opt.max_prefill);
+  WL_TRY(dalloc(&m->h, (size_t)MR * d));
+  WL_TRY(dalloc(&m->xn, (size_t)MR * d));
+  WL_TRY(dalloc(&m->q, (size_t)MR * m->Hl * m->hd));
+  WL_TRY(dalloc(&m->att, (size_t)MR * m->Hl * m->hd));
+  WL_TRY(dalloc(&m->act, (size_t)MR * m->ffl));
+  WL_TRY(dalloc(&m->logits, (size_t)MR * V));
+  int max_groups = std::max({(m->Hl * m->hd + 2 * m->kvdl + 255) / 256 + 3, 2 * ((m->ffl + 255) / 256),
+                             (V + 255) / 256, (d + 255) / 256});
+  m->n_counters = std::max(max_groups, 1024);
+  m->ws_floats = (size_t)(2 * m->sms + max_groups + 2) * 32 * 256;
+  WL_TRY(dalloc(&m->ws, m->ws_floats));
+  WL_TRY(dalloc(&m->counters, (size_t)m->n_counters));
+  WL_CUDA_TRY(cudaMemsetAsync(m->counters, 0, (size_t)m->n_counters * sizeof(unsigned), m->st));
+  m->part_rows = (size_t)2 * m->sms + MR;
+  WL_TRY(dalloc(&m->part_o, m->part_rows * m->Hl * m->hd));
+  WL_TRY(dalloc(&m->part_ml, m->part_rows * m->Hl * 2));
+  WL_TRY(dalloc(&m->row_pos, (size_t)MR));
+  WL_TRY(dalloc(&m->row_sess, (size_t)MR));
+  WL_TRY(dalloc(&m->ids, (size_t)MR));
+  WL_TRY(dalloc(&m->err, 1));
+  WL_CUDA_TRY(cudaMemsetAsync(m->err, 0, sizeof(int), m->st));
+  WL_CUDA_TRY(cudaMallocHost(&m->h_meta, (size_t)3 * MR * sizeof(int)));
+  WL_CUDA_TRY(cudaStreamSynchronize(m->st));
+  *out = m.release();
+  return WL_OK;
+}
+
+void model_free(wl_model* m) {
+  if (!m) return;
+  cudaSetDevice(m->dev);
+  cudaStreamSynchronize(m->st);
+  for (auto& kv : m->graphs) cudaGraphExecDestroy(kv.second);
+  for (wl_session* s : m->slots)
+    if (s) s->m = nullptr;
+  cudaFree(m->dweights);
+  cudaFree(m->kvbuf);
+  cudaFree(m->d_tables);
+  cudaFree(m->h);
+  cudaFree(m->xn);
+  cudaFree(m->q);
+  cudaFree(m->att);
+  cudaFree(m->act);
+  cudaFree(m->logits);
+  cudaFree(m->ws);
+  cudaFree(m->counters);
+  cudaFree(m->part_o);
+  cudaFree(m->part_ml);
+  cudaFree(m->row_pos);
+  cudaFree(m->row_sess);
+  cudaFree(m->ids);
+  cudaFree(m->err);
+  cudaFreeHost(m->h_meta);
+  delete m;
+}
+
+int session_create(wl_model* m, wl_session** out) {
+  *out = nullptr;
+  WL_CHECK_ARG(m, "null model");
+  std::lock_guard<std::mutex> lk(m->mu);
+  for (int i = 0; i < m->max_sessions; i++)
+    if (!m->slots[i]) {
+      auto* s = new wl_session();
+      s->m = m;
+      s->slot = i;
+      m->slots[i] = s;
+      *out = s;
+      return WL_OK;
+    }
+  return fail(WL_ERR_OUT_OF_MEMORY, "all " + std::to_string(m->max_sessions) + " session slots in use");
+}
+
+int session_reset(wl_session* s) {
+  WL_CHECK_ARG(s, "null session");
+  wl_model* m = s->m;
+  if (m) {
+    std::lock_guard<std::mutex> lk(m->mu);
+    for (int pg : s->pages) m->free_pages.push_back(pg);
+  }
+  s->pages.clear();
+  s->len = 0;
+  return WL_OK;
+}
+
+void session_free(wl_session* s) {
+  if (!s) return;
+  session_reset(s);
+  if (s->m) {
+    std::lock_guard<std::mutex> lk(s->m->mu);
+    s->m->slots[s->slot] = nullptr;
+  }
+  delete s;
+}
+
+int forward(wl_model* m, wl_session* const* ss, int n, const uint32_t* ids, const int* n_ids,
+            float* logits, int mode) {
+  WL_CHECK_ARG(m && ids && n_ids && logits, "null argument");
+  WL_TRY(check_sessions(m, ss, n));
+  WL_CHECK_ARG(mode == WL_LOGITS_LAST || mode == WL_LOGITS_ALL, "bad logits mode");
+  std::lock_guard<std::mutex> lk(m->mu);
+  WL_CUDA_TRY(cudaSetDevice(m->dev));
+  size_t total = 0;
+  bool all_one = true;
+  for (int i = 0; i < n; i++) {
+    WL_CHECK_ARG(n_ids[i] >= 1, "each session needs at least one token");
+    all_one &= n_ids[i] == 1;
+    total += (size_t)n_ids[i];
+  }
+  for (size_t i = 0; i < total; i++)
+    if (ids[i] >= (uint32_t)m->V)
+      return fail(WL_ERR_TOKEN_OUT_OF_RANGE, "Token ID " + std::to_string(ids[i]) +
+                                                 " exceeds vocabulary size " + std::to_string(m->V));
+  const size_t V = (size_t)m->V;
+  if (all_one && n <= m->opt.max_batch) {
+    for (int i = 0; i < n; i++) WL_TRY(ensure_pages(m, ss[i], ss[i]->len + 1));
+    for (int i = 0; i < n; i++) {
+      m->h_meta[i] = (int)ids[i];
+      m->h_meta[m->MR + i] = ss[i]->len;
+      m->h_meta[2 * m->MR + i] = ss[i]->slot;
+    }
+    WL_TRY(upload_meta(m, n));
+    WL_TRY(decode_launch(m, n));
+    WL_CUDA_TRY(cudaMemcpyAsync(logits, m->logits, (size_t)n * V * 4, cudaMemcpyDeviceToHost, m->st));
+    WL_CUDA_TRY(cudaStreamSynchronize(m->st));
+    for (int i = 0; i < n; i++) ss[i]->len += 1;
+    return WL_OK;
+  }
+  // per-session prefill, chunked by max_prefill rows
+  size_t id_off = 0, lg_off = 0;
+  for (int i = 0; i < n; i++) {
+    wl_session* s = ss[i];
+    const int cnt = n_ids[i];
+    for (int c0 = 0; c0 < cnt; c0 += m->opt.max_prefill) {
+      const int c = std::min(m->opt.max_prefill, cnt - c0);
+      WL_TRY(ensure_pages(m, s, s->len + c));
+      for (int r = 0; r < c; r++) {
+        m->h_meta[r] = (int)ids[id_off + c0 + r];
+        m->h_meta[m->MR + r] = s->len + r;
+        m->h_meta[2 * m->MR + r] = s->slot;
+      }
+      WL_TRY(upload_meta(m, c));
+      const bool last_chunk = c0 + c == cnt;
+      int lfirst = mode == WL_LOGITS_ALL ? 0 : (last_chunk ? c - 1 : c);
+      const int nsplit = attention_plan_splits(c, m->KVHl, s->len + c, m->sms);
+      WL_TRY(run_rows(m, c, nsplit, lfirst));
+      if (c - lfirst > 0) {
+        WL_CUDA_TRY(cudaMemcpyAsync(logits + lg_off, m->logits, (size_t)(c - lfirst) * V * 4,
+                                    cudaMemcpyDeviceToHost, m->st));
+        lg_off += (size_t)(c - lfirst) * V;
+      }
+      WL_CUDA_TRY(cudaStreamSynchronize(m->st));
+      s->len += c;
+    }
+    id_off += (size_t)cnt;
+  }
+  return WL_OK;
+}
+
+int decode_step_device(wl_model* m, wl_session* const* ss, int n, const uint32_t* d_ids,
+                       float* d_logits, cudaStream_t user) {
+  WL_CHECK_ARG(m && d_ids && d_logits, "null argument");
+  WL_TRY(check_sessions(m, ss, n));
+  WL_CHECK_ARG(n <= m->opt.max_batch, "n_sess exceeds max_batch");
+  std::lock_guard<std::mutex> lk(m->mu);
+  WL_CUDA_TRY(cudaSetDevice(m->dev));
+  cudaEvent_t ev = nullptr;
+  if (user && user != m->st) {  // order after the caller's work
+    WL_CUDA_TRY(cudaEventCreateWithFlags(&ev, cudaEventDisableTiming));
+    cudaEventRecord(ev, user);
+    cudaStreamWaitEvent(m->st, ev, 0);
+  }
+  for (int i = 0; i < n; i++) WL_TRY(ensure_pages(m, ss[i], ss[i]->len + 1));
+  for (int i = 0; i < n; i++) {
+    m->h_meta[m->MR + i] = ss[i]->len;
+    m->h_meta[2 * m->MR + i] = ss[i]->slot;
+  }
+  WL_CUDA_TRY(cudaMemcpyAsync(m->ids, d_ids, (size_t)n * 4, cudaMemcpyDeviceToDevice, m->st));
+  WL_CUDA_TRY(cudaMemcpyAsync(m->row_pos, m->h_meta + m->MR, (size_t)n * 4, cudaMemcpyHostToDevice, m->st));
+  WL_CUDA_TRY(cudaMemcpyAsync(m->row_sess, m->h_meta + 2 * m->MR, (size_t)n * 4, cudaMemcpyHostToDevice, m->st));
+  WL_TRY(decode_launch(m, n));
+  WL_CUDA_TRY(cudaMemcpyAsync(d_logits, m->logits, (size_t)n * m->V * 4, cudaMemcpyDeviceToDevice, m->st));
+  if (ev) {
+    cudaEventRecord(ev, m->st);
+    cudaStreamWaitEvent(user, ev, 0);
+    cudaEventDestroy(ev);
+  }
+  for (int i = 0; i < n; i++) ss[i]->len += 1;
+  return WL_OK;
+}
+
+// kernels per decode step: embed + L*(norm, qkv, attn[, combine], o, norm, gateup, down) + norm + head
+int decode_kernel_count(const wl_model* m, int n) {
+  const int nsplit = attention_plan_splits(n, m->KVHl, m->opt.max_context, m->sms);
+  int chunks = (n + 31) / 32;
+  int per_layer = 2 + chunks * 4 + 1 + (nsplit > 1 ? 1 : 0);
+  return 1 + m->L * per_layer + 1 + chunks;
+}
+
+}  // namespace wl

@@ -1,0 +1,104 @@
+// Model runtime internals: weights in HBM, paged KV sessions, scratch, graphs.
+#pragma once
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <map>
+#include <memory>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "../../include/woolly_cuda.h"
+#include "gguf.h"
+#include "kernels.cuh"
+#include "qgemv.cuh"
+
+struct wl_ctx {
+  int device = 0;
+  int num_sms = 0;
+  cudaStream_t stream = nullptr;
+};
+
+namespace wl {
+
+// A layout-B weight matrix [K][N] as GGUF blocks in HBM.
+struct QMat {
+  const uint8_t* w = nullptr;
+  uint32_t type = 0;
+  int K = 0, N = 0;
+  int pitch = 0;  // bytes per row
+};
+
+struct Layer {
+  const float* attn_norm = nullptr;
+  const float* ffn_norm = nullptr;
+  QMat wq, wk, wv, wo, wg, wu, wd;
+};
+
+}  // namespace wl
+
+struct wl_session;
+
+struct wl_model {
+  wl_ctx* ctx = nullptr;
+  int dev = 0, sms = 0;
+  cudaStream_t st = nullptr;
+  wl_model_options opt{};
+  wl_model_config cfg{};
+  // shapes (per shard under tensor parallelism)
+  int d = 0, L = 0, H = 0, KVH = 0, hd = 0, kvd = 0, ff = 0, V = 0;
+  int Hl = 0, KVHl = 0, kvdl = 0, ffl = 0;  // local heads / kv width / ffn width
+  float eps = 1e-5f, theta = 10000.f;
+  int window = 0, rope = 0;
+  // weights
+  uint8_t* dweights = nullptr;
+  size_t weight_bytes = 0;
+  const float* embd = nullptr;  // [d][V] f32
+  const float* out_norm = nullptr;
+  wl::QMat out;                 // [d][V] (a tied embedding is an F32 QMat)
+  std::vector<wl::Layer> layers;
+  // paged KV
+  int page = 16, n_pages = 0, max_pages = 0, max_sessions = 0;
+  uint8_t* kvbuf = nullptr;
+  size_t kv_bytes = 0;
+  std::vector<int> free_pages;
+  int* d_tables = nullptr;          // [max_sessions][max_pages]
+  std::vector<int> h_tables;
+  std::vector<wl_session*> slots;
+  // scratch (rows = max(max_batch, max_prefill))
+  int MR = 0;
+  float* h = nullptr;
+  __half* xn = nullptr;
+  float* q = nullptr;
+  __half* att = nullptr;
+  __half* act = nullptr;
+  float* logits = nullptr;
+  float* ws = nullptr;
+  size_t ws_floats = 0;
+  unsigned* counters = nullptr;
+  int n_counters = 0;
+  float* part_o = nullptr;
+  float* part_ml = nullptr;
+  size_t part_rows = 0;  // capacity in rows*nsplit
+  int* row_pos = nullptr;
+  int* row_sess = nullptr;
+  uint32_t* ids = nullptr;
+  int* err = nullptr;
+  // pinned staging for per-step metadata
+  int* h_meta = nullptr;  // [3][MR]: ids, pos, sess
+  // decode graphs keyed by batch size
+  std::map<int, cudaGraphExec_t> graphs;
+  std::map<int, int> graph_warm;
+  // tensor parallel
+  int tp_rank = 0, tp_size = 1;
+  void* nccl = nullptr;
+  std::mutex mu;
+};
+
+struct wl_session {
+  wl_model* m = nullptr;
+  int slot = -1;
+  int len = 0;
+  std::vector<int> pages;
+};

@@ -1,0 +1,209 @@
+// Row-wise and element-wise kernels: RMSNorm(+RoPE), embedding gather,
+// SwiGLU, RoPE, block dequantization.
+#include <cuda_fp16.h>
+
+#include <cmath>
+#include <string>
+
+#include "common.h"
+#include "kernels.cuh"
+
+namespace wl {
+namespace {
+
+constexpr int kNormThreads = 256;
+
+// rms_norm (woolly-core tensor_utils.rs:446-480): rms = sqrt(sum(x^2)/d + eps),
+// y = (x / rms) * w, with an optional NeoX rotation (RoPE::apply_f32,
+// woolly-tensor/src/ops/mod.rs:476-527) of the normalised row, head by head.
+__global__ void __launch_bounds__(kNormThreads)
+    k_rmsnorm(const float* x, const float* w, int dim, float eps, int rope, const int* pos,
+              int hd, float theta, void* y, int y_f16) {
+  extern __shared__ float srow[];  // normalised row when rope is on
+  __shared__ float sred[kNormThreads / 32];
+  const int r = blockIdx.x, tid = threadIdx.x;
+  const float* xr = x + (size_t)r * dim;
+  float ss = 0.f;
+  for (int i = tid; i < dim; i += kNormThreads) ss += xr[i] * xr[i];
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+  if ((tid & 31) == 0) sred[tid >> 5] = ss;
+  __syncthreads();
+  if (tid < 32) {
+    float v = tid < kNormThreads / 32 ? sred[tid] : 0.f;
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+    if (tid == 0) sred[0] = v;
+  }
+  __syncthreads();
+  const float rms = sqrtf(sred[0] / (float)dim + eps);
+  if (!rope) {
+    for (int i = tid; i < dim; i += kNormThreads) {
+      float v = __fdiv_rn(xr[i], rms) * w[i];
+      if (y_f16)
+        reinterpret_cast<__half*>(y)[(size_t)r * dim + i] = __float2half_rn(v);
+      else
+        reinterpret_cast<float*>(y)[(size_t)r * dim + i] = v;
+    }
+    return;
+  }
+  for (int i = tid; i < dim; i += kNormThreads) srow[i] = __fdiv_rn(xr[i], rms) * w[i];
+  __syncthreads();
+  const int half = hd / 2;
+  const float p = (float)pos[r];
+  for (int j = tid; j < dim / 2; j += kNormThreads) {
+    int h = j / half, ii = j % half;
+    int c1 = h * hd + ii, c2 = c1 + half;
+    float freq = 1.0f / powf(theta, 2.0f * (float)ii / (float)hd);
+    float sn, cs;
+    sincosf(p * freq, &sn, &cs);
+    float x1 = srow[c1], x2 = srow[c2];
+    float o1 = x1 * cs - x2 * sn, o2 = x1 * sn + x2 * cs;
+    if (y_f16) {
+      reinterpret_cast<__half*>(y)[(size_t)r * dim + c1] = __float2half_rn(o1);
+      reinterpret_cast<__half*>(y)[(size_t)r * dim + c2] = __float2half_rn(o2);
+    } else {
+      reinterpret_cast<float*>(y)[(size_t)r * dim + c1] = o1;
+      reinterpret_cast<float*>(y)[(size_t)r * dim + c2] = o2;
+    }
+  }
+}
+
+// h[r][j] = E[j*V + id]: token_embd is [d][V] in woolly's reading
+// (lazy_transformer.rs:1252-1262).  Out-of-range ids raise a flag and read id 0.
+__global__ void k_embed(const float* E, int d, int V, const uint32_t* ids, int rows, float* h,
+                        int* err) {
+  const int r = blockIdx.y;
+  const int j = blockIdx.x * blockDim.x + threadIdx.x;
+  if (j >= d || r >= rows) return;
+  uint32_t t = ids[r];
+  if (t >= (uint32_t)V) {
+    if (err && j == 0) atomicOr(err, 1);
+    t = 0;
+  }
+  h[(size_t)r * d + j] = __ldg(E + (size_t)j * V + t);
+}
+
+// swiglu (tensor_utils.rs:512-532): silu(g) * u with silu(g) = g * (1 / (1 + exp(-g)))
+__global__ void k_swiglu(const float* g, const float* u, size_t n, float* out) {
+  size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  float gi = g[i];
+  out[i] = gi * (1.0f / (1.0f + expf(-gi))) * u[i];
+}
+
+// RoPE::apply_f32 (woolly-tensor/src/ops/mod.rs:476-527)
+__global__ void k_rope(const float* x, float* out, const int* pos, float base, int batch, int seq,
+                       int heads, int hd) {
+  const int half = hd / 2;
+  size_t total = (size_t)batch * seq * heads * half;
+  size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
+  if (i >= total) return;
+  int ii = (int)(i % half);
+  size_t rowh = i / half;  // (batch, seq, head)
+  int s = (int)((rowh / heads) % seq);
+  float freq = 1.0f / powf(base, 2.0f * (float)ii / (float)hd);
+  float ang = (float)pos[s] * freq;
+  float sn, cs;
+  sincosf(ang, &sn, &cs);
+  size_t b1 = rowh * hd + ii, b2 = b1 + half;
+  float x1 = x[b1], x2 = x[b2];
+  out[b1] = x1 * cs - x2 * sn;
+  out[b2] = x1 * sn + x2 * cs;
+}
+
+// woolly_gguf::dequantize (dequantize.rs:286-327, :337-378, :553-586), one
+// thread per 32-value block; bit-exact: (q-8)*d, q*d then +m (two roundings,
+// no FMA), q*d with d widened exactly from f16.
+__global__ void k_dequant(int type, const uint8_t* blocks, size_t n, float* out) {
+  size_t b = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
+  size_t nb = (n + 31) / 32;
+  if (b >= nb) return;
+  const int S = type == WL_Q4_0 ? 18 : type == WL_Q4_1 ? 20 : 34;
+  const uint8_t* p = blocks + b * S;
+  float d = __half2float(__ushort_as_half((uint16_t)(p[0] | (p[1] << 8))));
+  size_t o0 = b * 32;
+  for (int i = 0; i < 32 && o0 + i < n; i++) {
+    float v;
+    if (type == WL_Q4_0) {
+      int q = i < 16 ? (p[2 + i] & 15) - 8 : ((p[2 + i - 16] >> 4) & 15) - 8;
+      v = __fmul_rn((float)q, d);
+    } else if (type == WL_Q4_1) {
+      float m = __half2float(__ushort_as_half((uint16_t)(p[2] | (p[3] << 8))));
+      int q = i < 16 ? (p[4 + i] & 15) : ((p[4 + i - 16] >> 4) & 15);
+      v = __fadd_rn(__fmul_rn((float)q, d), m);
+    } else {
+      v = __fmul_rn((float)(int8_t)p[2 + i], d);
+    }
+    out[o0 + i] = v;
+  }
+}
+
+__global__ void k_f16_to_f32(const uint8_t* src, size_t n, float* out) {
+  size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
+  if (i < n) out[i] = __half2float(__ushort_as_half((uint16_t)(src[2 * i] | (src[2 * i + 1] << 8))));
+}
+
+}  // namespace
+
+int launch_rmsnorm(const float* x, const float* w, int rows, int dim, float eps, int rope,
+                   const int* pos, int head_dim, float theta, void* y, int y_f16,
+                   cudaStream_t st) {
+  if (rows <= 0) return WL_OK;
+  size_t smem = rope ? (size_t)dim * sizeof(float) : 0;
+  if (rope && (head_dim <= 0 || dim % head_dim || head_dim % 2))
+    return fail(WL_ERR_INVALID_ARGUMENT, "rmsnorm_rope: dim must be a multiple of an even head_dim");
+  if (smem > 48 * 1024) {
+    WL_CUDA_TRY(cudaFuncSetAttribute(k_rmsnorm, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)smem));
+  }
+  k_rmsnorm<<<rows, kNormThreads, smem, st>>>(x, w, dim, eps, rope, pos, head_dim, theta, y, y_f16);
+  WL_CUDA_TRY(cudaGetLastError());
+  return WL_OK;
+}
+
+int launch_embed(const float* E, int d, int V, const uint32_t* ids, int rows, float* h,
+                 int* err_flag, cudaStream_t st) {
+  if (rows <= 0) return WL_OK;
+  dim3 grid((d + 255) / 256, rows);
+  k_embed<<<grid, 256, 0, st>>>(E, d, V, ids, rows, h, err_flag);
+  WL_CUDA_TRY(cudaGetLastError());
+  return WL_OK;
+}
+
+int launch_swiglu(const float* g, const float* u, size_t n, float* out, cudaStream_t st) {
+  if (!n) return WL_OK;
+  k_swiglu<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(g, u, n, out);
+  WL_CUDA_TRY(cudaGetLastError());
+  return WL_OK;
+}
+
+int launch_rope(const float* x, float* out, const int* pos, float base, int batch, int seq,
+                int heads, int hd, cudaStream_t st) {
+  size_t total = (size_t)batch * seq * heads * (hd / 2);
+  if (!total) return WL_OK;
+  k_rope<<<(unsigned)((total + 255) / 256), 256, 0, st>>>(x, out, pos, base, batch, seq, heads, hd);
+  WL_CUDA_TRY(cudaGetLastError());
+  return WL_OK;
+}
+
+int launch_dequant(int type, const void* blocks, size_t n, float* out, cudaStream_t st) {
+  if (!n) return WL_OK;
+  if (type == WL_F32) {
+    WL_CUDA_TRY(cudaMemcpyAsync(out, blocks, n * 4, cudaMemcpyDeviceToDevice, st));
+    return WL_OK;
+  }
+  if (type == WL_F16) {
+    k_f16_to_f32<<<(unsigned)((n + 255) / 256), 256, 0, st>>>((const uint8_t*)blocks, n, out);
+    WL_CUDA_TRY(cudaGetLastError());
+    return WL_OK;
+  }
+  if (!(type == WL_Q4_0 || type == WL_Q4_1 || type == WL_Q8_0))
+    return fail(WL_ERR_UNSUPPORTED, "dequantize: type " + std::to_string(type) + " not supported");
+  size_t nb = (n + 31) / 32;
+  k_dequant<<<(unsigned)((nb + 127) / 128), 128, 0, st>>>(type, (const uint8_t*)blocks, n, out);
+  WL_CUDA_TRY(cudaGetLastError());
+  return WL_OK;
+}
+
+}  // namespace wl

@@ -1,0 +1,198 @@
+"""Model-level API mirroring woolly-core: the Model trait (model/mod.rs:32-67),
+InferenceSession::infer / infer_batch (session.rs:193-277) and
+InferenceEngine (engine.rs:48-105), over the CUDA runtime in libwoolly_cuda.so.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+from typing import Sequence
+
+import numpy as np
+
+from . import _lib
+from ._lib import LOGITS_ALL, LOGITS_LAST, WoollyError, check, lib
+from .gguf import config_dict
+
+
+class Context:
+    """One CUDA device with its own stream (wl_init)."""
+
+    def __init__(self, device: int = 0):
+        self._h = C.c_void_p()
+        check(lib().wl_init(device, C.byref(self._h)))
+        self.device = device
+
+    def close(self):
+        if self._h:
+            lib().wl_ctx_free(self._h)
+            self._h = None
+
+
+def model_options(**kw) -> _lib.ModelOptions:
+    o = _lib.ModelOptions()
+    lib().wl_model_options_default(C.byref(o))
+    for k, v in kw.items():
+        if not hasattr(o, k):
+            raise TypeError(f"unknown model option {k}")
+        setattr(o, k, v)
+    return o
+
+
+class CudaTransformer:
+    """Drop-in for LazyTransformer behind woolly's Model trait.
+
+    forward(input_ids) follows LazyTransformer::forward (lazy_transformer.rs:
+    1155-1336): a full causal forward of the ids, returning seq_len * vocab
+    logits (all positions, row-major).  Sessions keep a device KV cache for
+    incremental decode.
+    """
+
+    def __init__(self, path: str, ctx: Context | None = None, **options):
+        self.ctx = ctx or Context(options.pop("device", 0))
+        self._own_ctx = ctx is None
+        self._opts = model_options(**options)
+        self._h = C.c_void_p()
+        check(lib().wl_model_load_gguf(self.ctx._h, str(path).encode(), C.byref(self._opts),
+                                       C.byref(self._h)))
+        c = _lib.ModelConfig()
+        check(lib().wl_model_get_config(self._h, C.byref(c)))
+        self.config = config_dict(c)
+        self._name = os.path.splitext(os.path.basename(path))[0]
+        self._default: Session | None = None
+
+    @classmethod
+    def from_gguf(cls, path: str, **options) -> "CudaTransformer":
+        return cls(path, **options)
+
+    def close(self):
+        if self._default is not None:
+            self._default.close()
+            self._default = None
+        if self._h:
+            lib().wl_model_free(self._h)
+            self._h = None
+        if self._own_ctx:
+            self.ctx.close()
+
+    # --- Model trait (model/mod.rs:32-67) ---
+    def name(self) -> str:
+        return self._name
+
+    def model_type(self) -> str:
+        return self.config["architecture"]
+
+    def vocab_size(self) -> int:
+        return self.config["vocab_size"]
+
+    def context_length(self) -> int:
+        return self.config["context_length"]
+
+    def hidden_size(self) -> int:
+        return self.config["hidden_size"]
+
+    def num_layers(self) -> int:
+        return self.config["num_layers"]
+
+    def num_heads(self) -> int:
+        return self.config["num_heads"]
+
+    def forward(self, input_ids: Sequence[int]) -> np.ndarray:
+        if len(input_ids) == 0:
+            raise WoollyError(_lib.WL_ERR_INVALID_ARGUMENT, "Empty input tokens")
+        if self._default is None:
+            self._default = Session(self)
+        self._default.reset()
+        return self._default.infer(input_ids)
+
+    def memory(self) -> tuple[int, int]:
+        w, k = C.c_uint64(), C.c_uint64()
+        check(lib().wl_model_memory(self._h, C.byref(w), C.byref(k)))
+        return w.value, k.value
+
+    def decode_kernel_count(self, n_sess: int) -> int:
+        return lib().wl_decode_kernel_count(self._h, n_sess)
+
+    # --- batched multi-session forward (wl_forward) ---
+    def forward_sessions(self, sessions: Sequence["Session"], ids: Sequence[Sequence[int]],
+                         all_logits: bool = False) -> list[np.ndarray]:
+        n = len(sessions)
+        counts = np.array([len(x) for x in ids], dtype=np.int32)
+        flat = np.ascontiguousarray(np.concatenate([np.asarray(x, dtype=np.uint32) for x in ids]))
+        V = self.vocab_size()
+        rows = int(counts.sum()) if all_logits else n
+        out = np.empty((rows, V), dtype=np.float32)
+        arr = (C.c_void_p * n)(*[s._h for s in sessions])
+        check(lib().wl_forward(self._h, arr, n, flat.ctypes.data, counts.ctypes.data,
+                               out.ctypes.data, LOGITS_ALL if all_logits else LOGITS_LAST))
+        if not all_logits:
+            return [out[i] for i in range(n)]
+        res, o = [], 0
+        for c in counts:
+            res.append(out[o:o + c])
+            o += c
+        return res
+
+    def decode_step_device(self, sessions: Sequence["Session"], d_ids: int, d_logits: int,
+                           stream: int = 0) -> None:
+        """One batched decode step with device-resident ids/logits (raw pointers)."""
+        arr = (C.c_void_p * len(sessions))(*[s._h for s in sessions])
+        check(lib().wl_decode_step_device(self._h, arr, len(sessions), d_ids, d_logits, stream))
+
+
+class Session:
+    """A device KV cache for one sequence (InferenceSession, session.rs:193-277)."""
+
+    def __init__(self, model: CudaTransformer):
+        self.model = model
+        self._h = C.c_void_p()
+        check(lib().wl_session_create(model._h, C.byref(self._h)))
+
+    def close(self):
+        if self._h:
+            lib().wl_session_free(self._h)
+            self._h = None
+
+    def reset(self):
+        check(lib().wl_session_reset(self._h))
+
+    def __len__(self) -> int:
+        return lib().wl_session_length(self._h)
+
+    def infer(self, tokens: Sequence[int]) -> np.ndarray:
+        """Appends tokens; returns their logits, flattened [len(tokens) * vocab]."""
+        if len(tokens) == 0:
+            raise WoollyError(_lib.WL_ERR_INVALID_ARGUMENT, "Empty input tokens")
+        return self.model.forward_sessions([self], [tokens], all_logits=True)[0].reshape(-1)
+
+    def infer_last(self, tokens: Sequence[int]) -> np.ndarray:
+        return self.model.forward_sessions([self], [tokens], all_logits=False)[0]
+
+    def infer_batch(self, batch: Sequence[Sequence[int]]) -> list[np.ndarray]:
+        return [self.infer(t) for t in batch]
+
+
+InferenceSession = Session
+
+
+class InferenceEngine:
+    """InferenceEngine (woolly-core/src/engine.rs:15-246): holds one model and
+    hands out sessions."""
+
+    def __init__(self):
+        self.model: CudaTransformer | None = None
+
+    def load_model(self, model: CudaTransformer) -> None:
+        self.model = model
+
+    def create_session(self) -> Session:
+        if self.model is None:
+            raise WoollyError(_lib.WL_ERR_INVALID_ARGUMENT, "No model loaded")
+        return Session(self.model)
+
+    def infer(self, tokens: Sequence[int]) -> np.ndarray:
+        s = self.create_session()
+        try:
+            return s.infer(tokens)
+        finally:
+            s.close()
