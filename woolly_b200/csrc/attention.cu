@@ -7,13 +7,16 @@
 // The optional window W keeps keys j in (pos - W, pos] (Mistral shape; no
 // reference counterpart).
 //
-// Flash-decoding: one CTA per (KV head, query row, context split).  The CTA
-// streams K/V rows of its split once for all G = H/KVH query heads of the
-// group (GQA reuse), keeps an online softmax per head, and writes either the
-// final row (one split) or an unnormalised partial (o, m, l) that
-// k_attn_combine merges with the log-sum-exp rule.  K/V rows are 16-byte
-// vector loads of a paged f16 cache (pages of `page` tokens, per-session page
-// table), coalesced across the lanes that share a token.
+// Paged path (flash-decoding): one CTA per (KV head, query row, context
+// split).  The KV cache is paged as [page][kv_head][16 tokens][head_dim] f16,
+// so a (page, head) pair is one contiguous 2-8 KB chunk; the CTA streams the K
+// and V chunks of its pages with 1-D bulk copies (cp.async.bulk, completion
+// on an mbarrier) through a 4-stage shared-memory ring, scores all G = H/KVH
+// query heads of the group from shared memory (GQA reuse), keeps an online
+// softmax per head and writes either the final row (one split) or an
+// unnormalised partial (o, m, l) that k_attn_combine merges with the
+// log-sum-exp rule.  Every mbarrier wait is bounded; on expiry the kernel
+// raises an error flag instead of spinning.
 #include <cuda_fp16.h>
 
 #include <cmath>
@@ -26,87 +29,102 @@ namespace wl {
 namespace {
 
 constexpr int kAttnThreads = 128;
-constexpr int kTile = 64;  // tokens per softmax tile
+constexpr int kPage = 16;    // tokens per KV page
+constexpr int kStagesA = 4;  // pages in flight per CTA
+constexpr int kTile = 64;    // tokens per softmax tile (f32 path)
 
-struct PagedKV {
-  const __half* k;
-  const __half* v;
-  const int* table;
-  int maxp, page, kvd;
-  __device__ __forceinline__ size_t row(int sess, int j) const {
-    int pg = __ldg(table + (size_t)sess * maxp + j / page);
-    return ((size_t)pg * page + (j % page)) * kvd;
+// ---------------------------------------------------------------- mbarrier / bulk copy
+__device__ __forceinline__ void mbar_init(uint64_t* bar, unsigned count) {
+  const unsigned a = (unsigned)__cvta_generic_to_shared(bar);
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(a), "r"(count));
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, unsigned bytes) {
+  const unsigned a = (unsigned)__cvta_generic_to_shared(bar);
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(a), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, unsigned bytes, uint64_t* bar) {
+  const unsigned d = (unsigned)__cvta_generic_to_shared(dst);
+  const unsigned b = (unsigned)__cvta_generic_to_shared(bar);
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::"r"(d),
+      "l"(src), "r"(bytes), "r"(b)
+      : "memory");
+}
+// bounded wait for the given phase parity; false if the bound expired
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, unsigned parity) {
+  const unsigned a = (unsigned)__cvta_generic_to_shared(bar);
+  for (int it = 0; it < (1 << 22); it++) {
+    unsigned done;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+        " selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(done)
+        : "r"(a), "r"(parity)
+        : "memory");
+    if (done) return true;
   }
-  __device__ __forceinline__ void k8(int sess, int j, int off, float* f) const {
-    uint4 u = __ldg(reinterpret_cast<const uint4*>(k + row(sess, j) + off));
-    const __half2* h = reinterpret_cast<const __half2*>(&u);
-#pragma unroll
-    for (int i = 0; i < 4; i++) {
-      float2 t = __half22float2(h[i]);
-      f[2 * i] = t.x, f[2 * i + 1] = t.y;
-    }
-  }
-  __device__ __forceinline__ float2 v2(int sess, int j, int off) const {
-    return __half22float2(__ldg(reinterpret_cast<const __half2*>(v + row(sess, j) + off)));
-  }
-};
+  return false;
+}
 
-struct F32KV {
-  const float* k;
-  const float* v;
-  int kvd;
-  __device__ __forceinline__ void k8(int, int j, int off, float* f) const {
-    const float4* p = reinterpret_cast<const float4*>(k + (size_t)j * kvd + off);
-    float4 a = __ldg(p), b = __ldg(p + 1);
-    f[0] = a.x, f[1] = a.y, f[2] = a.z, f[3] = a.w, f[4] = b.x, f[5] = b.y, f[6] = b.z, f[7] = b.w;
+// f32 output, or f16 hi/lo planes (lo plane `plane` elements after hi) when plane != 0
+__device__ __forceinline__ void put_out(void* out, size_t plane, size_t i, float v) {
+  if (!plane) {
+    reinterpret_cast<float*>(out)[i] = v;
+  } else {
+    const __half hi = __float2half_rn(v);
+    reinterpret_cast<__half*>(out)[i] = hi;
+    reinterpret_cast<__half*>(out)[i + plane] = __float2half_rn(v - __half2float(hi));
   }
-  __device__ __forceinline__ float2 v2(int, int j, int off) const {
-    return __ldg(reinterpret_cast<const float2*>(v + (size_t)j * kvd + off));
-  }
-};
+}
 
-struct RowInfo {
-  const int* pos;   // nullptr: pos = past + row
-  const int* sess;  // nullptr: session 0
-  int past;
-};
-
-template <class KV>
-struct Params {
-  KV kv;
-  RowInfo ri;
-  const float* q;
-  int ldq;
-  int heads, kv_heads, window, nsplit;
-  float scale;
-  float* part_o;
-  float* part_ml;
-  void* out;
-  int ldo, out_f16;
-};
-
-template <int HD, int G, class KV>
-__global__ void __launch_bounds__(kAttnThreads) k_attn(const Params<KV> a) {
-  constexpr int LPT = HD / 8;  // lanes per token in the score phase
-  constexpr int TPW = 32 / LPT;
+// ---------------------------------------------------------------- paged kernel
+template <int HD, int G>
+__global__ void __launch_bounds__(kAttnThreads) k_attn_paged(const AttnArgs a, float scale) {
+  constexpr int CHUNK = kPage * HD;        // halves per (page, head) chunk
+  constexpr int LPT = HD / 8;              // lanes per token in the score phase
+  constexpr int TPP = kAttnThreads / LPT;  // tokens per pass
   constexpr int NW = kAttnThreads / 32;
-  constexpr int DP = HD / 2;   // dim pairs in the V phase
+  constexpr int DP = HD / 2;
   constexpr int NS = kAttnThreads / DP;  // token streams in the V phase
-  __shared__ float s_p[G][kTile];
+  extern __shared__ __align__(128) __half kvs[];  // [kStagesA][2][CHUNK]
+  __shared__ __align__(8) uint64_t bars[kStagesA];
+  __shared__ float s_p[G][kPage];
   __shared__ float s_m[G], s_l[G], s_alpha[G];
   __shared__ float s_red[NS][G][HD];
+  __shared__ int s_fail;
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int kvh = blockIdx.x, r = blockIdx.y, sp = blockIdx.z;
-  const int pos = a.ri.pos ? a.ri.pos[r] : a.ri.past + r;
-  const int sess = a.ri.sess ? a.ri.sess[r] : 0;
+  const int pos = a.row_pos[r];
+  const int sess = a.row_sess[r];
   const int j0 = (a.window > 0 && pos - a.window + 1 > 0) ? pos - a.window + 1 : 0;
-  const int len = pos + 1 - j0;
-  const int chunk = (len + a.nsplit - 1) / a.nsplit;
-  const int ja = j0 + sp * chunk;
-  const int jb = min(pos + 1, ja + chunk);
+  const int P0 = j0 / kPage, P1 = pos / kPage;
+  const int npg = P1 - P0 + 1;
+  const int pc = (npg + a.nsplit - 1) / a.nsplit;
+  const int pa = P0 + sp * pc;
+  const int pb = min(P1 + 1, pa + pc);
+  const int mine = pb > pa ? pb - pa : 0;
+  const int* table = a.kv.page_table + (size_t)sess * a.kv.max_pages;
 
-  const int sub = lane / LPT, li = lane % LPT;
+  auto issue = [&](int i) {  // page pa+i into stage i % kStagesA (thread 0 only)
+    const int st = i % kStagesA;
+    const int pg = table[pa + i];
+    const size_t off = ((size_t)pg * a.kv.kv_heads + kvh) * CHUNK;
+    mbar_expect_tx(&bars[st], 2 * CHUNK * 2);
+    bulk_g2s(kvs + (size_t)st * 2 * CHUNK, a.kv.k + off, CHUNK * 2, &bars[st]);
+    bulk_g2s(kvs + (size_t)st * 2 * CHUNK + CHUNK, a.kv.v + off, CHUNK * 2, &bars[st]);
+  };
+  if (tid == 0) {
+    for (int s = 0; s < kStagesA; s++) mbar_init(&bars[s], 1);
+    asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+    s_fail = 0;
+  }
+  __syncthreads();
+  if (tid == 0)
+    for (int i = 0; i < kStagesA && i < mine; i++) issue(i);
+
+  const int sub = tid / LPT, li = tid % LPT;
   float qr[G][8];
 #pragma unroll
   for (int h = 0; h < G; h++) {
@@ -121,46 +139,56 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn(const Params<KV> a) {
   for (int h = 0; h < G; h++) o[h][0] = o[h][1] = 0.f;
   __syncthreads();
 
-  for (int t0 = ja; t0 < jb; t0 += kTile) {
-    const int n = min(kTile, jb - t0);
-    for (int base = warp * TPW; base < n; base += NW * TPW) {
-      const int tok = base + sub;
-      const bool ok = tok < n;
-      float kf[8];
-      if (ok)
-        a.kv.k8(sess, t0 + tok, kvh * HD + li * 8, kf);
-      else
+  for (int i = 0; i < mine; i++) {
+    const int st = i % kStagesA;
+    if (!mbar_wait(&bars[st], (unsigned)((i / kStagesA) & 1))) {
+      if (a.err) atomicOr(a.err, 2);
+      s_fail = 1;
+    }
+    __syncthreads();
+    if (s_fail) break;
+    const __half* Ks = kvs + (size_t)st * 2 * CHUNK;
+    const __half* Vs = Ks + CHUNK;
+    const int tok0 = (pa + i) * kPage;
 #pragma unroll
-        for (int i = 0; i < 8; i++) kf[i] = 0.f;
+    for (int pass = 0; pass < kPage / TPP; pass++) {
+      const int tk = pass * TPP + sub;
+      const int j = tok0 + tk;
+      const bool ok = j >= j0 && j <= pos;
+      const uint4 u = *reinterpret_cast<const uint4*>(Ks + tk * HD + li * 8);
+      const __half2* hh = reinterpret_cast<const __half2*>(&u);
+      float kf[8];
+#pragma unroll
+      for (int q = 0; q < 4; q++) {
+        const float2 f = __half22float2(hh[q]);
+        kf[2 * q] = f.x, kf[2 * q + 1] = f.y;
+      }
 #pragma unroll
       for (int h = 0; h < G; h++) {
         float s = 0.f;
 #pragma unroll
-        for (int i = 0; i < 8; i++) s += qr[h][i] * kf[i];
+        for (int q = 0; q < 8; q++) s += qr[h][q] * kf[q];
 #pragma unroll
         for (int off = LPT / 2; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
-        if (ok && li == 0) s_p[h][tok] = s * a.scale;
+        if (li == 0) s_p[h][tk] = ok ? s * scale : -INFINITY;
       }
     }
     __syncthreads();
     for (int h = warp; h < G; h += NW) {
-      float mx = -INFINITY;
-      for (int i = lane; i < n; i += 32) mx = fmaxf(mx, s_p[h][i]);
+      const float sv = lane < kPage ? s_p[h][lane] : -INFINITY;
+      float mx = sv;
 #pragma unroll
       for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
       const float m_old = s_m[h];
       const float m_new = fmaxf(m_old, mx);
-      float sum = 0.f;
-      for (int i = lane; i < n; i += 32) {
-        float p = expf(s_p[h][i] - m_new);
-        s_p[h][i] = p;
-        sum += p;
-      }
+      const float p = sv == -INFINITY ? 0.f : expf(sv - m_new);
+      float sum = p;
 #pragma unroll
       for (int off = 16; off > 0; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
+      if (lane < kPage) s_p[h][lane] = p;
       __syncwarp();
       if (lane == 0) {
-        float alpha = m_old == -INFINITY ? 0.f : expf(m_old - m_new);
+        const float alpha = m_old == -INFINITY ? 0.f : expf(m_old - m_new);
         s_alpha[h] = alpha;
         s_l[h] = s_l[h] * alpha + sum;
         s_m[h] = m_new;
@@ -169,19 +197,21 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn(const Params<KV> a) {
     __syncthreads();
 #pragma unroll
     for (int h = 0; h < G; h++) {
-      float al = s_alpha[h];
+      const float al = s_alpha[h];
       o[h][0] *= al, o[h][1] *= al;
     }
-    for (int tok = stream; tok < n; tok += NS) {
-      float2 vv = a.kv.v2(sess, t0 + tok, kvh * HD + 2 * dp);
+#pragma unroll
+    for (int tk = stream; tk < kPage; tk += NS) {
+      const float2 vv = __half22float2(*reinterpret_cast<const __half2*>(Vs + tk * HD + 2 * dp));
 #pragma unroll
       for (int h = 0; h < G; h++) {
-        float p = s_p[h][tok];
+        const float p = s_p[h][tk];
         o[h][0] += p * vv.x;
         o[h][1] += p * vv.y;
       }
     }
-    __syncthreads();
+    __syncthreads();  // stage st fully consumed
+    if (tid == 0 && i + kStagesA < mine) issue(i + kStagesA);
   }
 #pragma unroll
   for (int h = 0; h < G; h++) {
@@ -197,12 +227,8 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn(const Params<KV> a) {
     const int qh = kvh * G + h;
     if (a.nsplit == 1) {
       const float l = s_l[h];
-      const float v = l > 0.f ? acc * (1.0f / l) : 0.f;
-      const size_t oi = (size_t)r * a.ldo + (size_t)qh * HD + d;
-      if (a.out_f16)
-        reinterpret_cast<__half*>(a.out)[oi] = __float2half_rn(v);
-      else
-        reinterpret_cast<float*>(a.out)[oi] = v;
+      put_out(a.out, a.out_plane, (size_t)r * a.ldo + (size_t)qh * HD + d,
+              l > 0.f ? acc * (1.0f / l) : 0.f);
     } else {
       const size_t pi = ((size_t)r * a.heads + qh) * a.nsplit + sp;
       a.part_o[pi * HD + d] = acc;
@@ -216,111 +242,214 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn(const Params<KV> a) {
 
 template <int HD>
 __global__ void k_attn_combine(const float* part_o, const float* part_ml, int heads, int nsplit,
-                               void* out, int ldo, int out_f16) {
+                               void* out, int ldo, size_t out_plane) {
   const int r = blockIdx.x, h = blockIdx.y, d = threadIdx.x;
   const size_t base = ((size_t)r * heads + h) * nsplit;
   float M = -INFINITY;
   for (int s = 0; s < nsplit; s++) M = fmaxf(M, part_ml[(base + s) * 2]);
   float L = 0.f, acc = 0.f;
   for (int s = 0; s < nsplit; s++) {
-    float m = part_ml[(base + s) * 2];
+    const float m = part_ml[(base + s) * 2];
     if (m == -INFINITY) continue;
-    float w = expf(m - M);
+    const float w = expf(m - M);
     L += part_ml[(base + s) * 2 + 1] * w;
     acc += part_o[(base + s) * HD + d] * w;
   }
-  float v = L > 0.f ? acc * (1.0f / L) : 0.f;
-  size_t oi = (size_t)r * ldo + (size_t)h * HD + d;
-  if (out_f16)
-    reinterpret_cast<__half*>(out)[oi] = __float2half_rn(v);
-  else
-    reinterpret_cast<float*>(out)[oi] = v;
+  put_out(out, out_plane, (size_t)r * ldo + (size_t)h * HD + d, L > 0.f ? acc * (1.0f / L) : 0.f);
 }
 
-template <int HD, class KV>
-int launch_g(const Params<KV>& p, int rows, int G, cudaStream_t st) {
-  dim3 grid(p.kv_heads, rows, p.nsplit);
+template <int HD, int G>
+int launch_paged_g(const AttnArgs& a, float scale, cudaStream_t st) {
+  static unsigned done = 0;
+  const size_t smem = (size_t)kStagesA * 2 * kPage * HD * sizeof(__half);
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!(done >> (dev & 31) & 1u)) {
+    WL_CUDA_TRY(cudaFuncSetAttribute(k_attn_paged<HD, G>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)smem));
+    done |= 1u << (dev & 31);
+  }
+  k_attn_paged<HD, G><<<dim3(a.kv_heads, a.rows, a.nsplit), kAttnThreads, smem, st>>>(a, scale);
+  WL_CUDA_TRY(cudaGetLastError());
+  return WL_OK;
+}
+
+template <int HD>
+int launch_paged_hd(const AttnArgs& a, int G, float scale, cudaStream_t st) {
+  int s;
   switch (G) {
-    case 1: k_attn<HD, 1, KV><<<grid, kAttnThreads, 0, st>>>(p); break;
-    case 2: k_attn<HD, 2, KV><<<grid, kAttnThreads, 0, st>>>(p); break;
-    case 4: k_attn<HD, 4, KV><<<grid, kAttnThreads, 0, st>>>(p); break;
-    case 8: k_attn<HD, 8, KV><<<grid, kAttnThreads, 0, st>>>(p); break;
+    case 1: s = launch_paged_g<HD, 1>(a, scale, st); break;
+    case 2: s = launch_paged_g<HD, 2>(a, scale, st); break;
+    case 4: s = launch_paged_g<HD, 4>(a, scale, st); break;
+    case 8: s = launch_paged_g<HD, 8>(a, scale, st); break;
     default:
       return fail(WL_ERR_UNSUPPORTED,
                   "attention: heads per KV head must be 1, 2, 4 or 8 (got " + std::to_string(G) + ")");
   }
-  WL_CUDA_TRY(cudaGetLastError());
-  if (p.nsplit > 1) {
-    k_attn_combine<HD><<<dim3(rows, p.heads), HD, 0, st>>>(p.part_o, p.part_ml, p.heads,
-                                                            p.nsplit, p.out, p.ldo, p.out_f16);
+  if (s) return s;
+  if (a.nsplit > 1) {
+    k_attn_combine<HD><<<dim3(a.rows, a.heads), HD, 0, st>>>(a.part_o, a.part_ml, a.heads,
+                                                             a.nsplit, a.out, a.ldo, a.out_plane);
     WL_CUDA_TRY(cudaGetLastError());
   }
   return WL_OK;
 }
 
-template <class KV>
-int launch_any(const Params<KV>& p, int rows, int hd, cudaStream_t st) {
-  if (p.heads % p.kv_heads) return fail(WL_ERR_INVALID_ARGUMENT, "attention: heads % kv_heads != 0");
-  int G = p.heads / p.kv_heads;
-  switch (hd) {
-    case 32: return launch_g<32>(p, rows, G, st);
-    case 64: return launch_g<64>(p, rows, G, st);
-    case 128: return launch_g<128>(p, rows, G, st);
-    case 256: return launch_g<256>(p, rows, G, st);
+// ---------------------------------------------------------------- contiguous f32 KV (op API)
+template <int HD, int G>
+__global__ void __launch_bounds__(kAttnThreads)
+    k_attn_f32(const float* q, const float* k, const float* v, int past, int heads, int kvd,
+               int window, float scale, float* out) {
+  constexpr int LPT = HD / 8;
+  constexpr int TPW = 32 / LPT;
+  constexpr int NW = kAttnThreads / 32;
+  constexpr int DP = HD / 2;
+  constexpr int NS = kAttnThreads / DP;
+  __shared__ float s_p[G][kTile];
+  __shared__ float s_m[G], s_l[G], s_alpha[G];
+  __shared__ float s_red[NS][G][HD];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int kvh = blockIdx.x, r = blockIdx.y;
+  const int ldq = heads * HD;
+  const int pos = past + r;
+  const int j0 = (window > 0 && pos - window + 1 > 0) ? pos - window + 1 : 0;
+  const int sub = lane / LPT, li = lane % LPT;
+  float qr[G][8];
+#pragma unroll
+  for (int h = 0; h < G; h++)
+#pragma unroll
+    for (int i = 0; i < 8; i++) qr[h][i] = q[(size_t)r * ldq + (size_t)(kvh * G + h) * HD + li * 8 + i];
+  if (tid < G) s_m[tid] = -INFINITY, s_l[tid] = 0.f;
+  const int stream = tid / DP, dp = tid % DP;
+  float o[G][2];
+#pragma unroll
+  for (int h = 0; h < G; h++) o[h][0] = o[h][1] = 0.f;
+  __syncthreads();
+  for (int t0 = j0; t0 <= pos; t0 += kTile) {
+    const int n = min(kTile, pos + 1 - t0);
+    for (int base = warp * TPW; base < n; base += NW * TPW) {
+      const int tok = base + sub;
+      const bool ok = tok < n;
+      float kf[8];
+#pragma unroll
+      for (int i = 0; i < 8; i++) kf[i] = ok ? k[(size_t)(t0 + tok) * kvd + kvh * HD + li * 8 + i] : 0.f;
+#pragma unroll
+      for (int h = 0; h < G; h++) {
+        float s = 0.f;
+#pragma unroll
+        for (int i = 0; i < 8; i++) s += qr[h][i] * kf[i];
+#pragma unroll
+        for (int off = LPT / 2; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
+        if (ok && li == 0) s_p[h][tok] = s * scale;
+      }
+    }
+    __syncthreads();
+    for (int h = warp; h < G; h += NW) {
+      float mx = -INFINITY;
+      for (int i = lane; i < n; i += 32) mx = fmaxf(mx, s_p[h][i]);
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+      const float m_old = s_m[h];
+      const float m_new = fmaxf(m_old, mx);
+      float sum = 0.f;
+      for (int i = lane; i < n; i += 32) {
+        const float p = expf(s_p[h][i] - m_new);
+        s_p[h][i] = p;
+        sum += p;
+      }
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
+      __syncwarp();
+      if (lane == 0) {
+        const float alpha = m_old == -INFINITY ? 0.f : expf(m_old - m_new);
+        s_alpha[h] = alpha;
+        s_l[h] = s_l[h] * alpha + sum;
+        s_m[h] = m_new;
+      }
+    }
+    __syncthreads();
+#pragma unroll
+    for (int h = 0; h < G; h++) o[h][0] *= s_alpha[h], o[h][1] *= s_alpha[h];
+    for (int tok = stream; tok < n; tok += NS) {
+      const float2 vv = *reinterpret_cast<const float2*>(v + (size_t)(t0 + tok) * kvd + kvh * HD + 2 * dp);
+#pragma unroll
+      for (int h = 0; h < G; h++) {
+        o[h][0] += s_p[h][tok] * vv.x;
+        o[h][1] += s_p[h][tok] * vv.y;
+      }
+    }
+    __syncthreads();
   }
-  return fail(WL_ERR_UNSUPPORTED, "attention: head_dim must be 32, 64, 128 or 256");
+#pragma unroll
+  for (int h = 0; h < G; h++) {
+    s_red[stream][h][2 * dp] = o[h][0];
+    s_red[stream][h][2 * dp + 1] = o[h][1];
+  }
+  __syncthreads();
+  for (int i = tid; i < G * HD; i += kAttnThreads) {
+    const int h = i / HD, d = i % HD;
+    float acc = 0.f;
+#pragma unroll
+    for (int s = 0; s < NS; s++) acc += s_red[s][h][d];
+    const float l = s_l[h];
+    out[(size_t)r * ldq + (size_t)(kvh * G + h) * HD + d] = l > 0.f ? acc * (1.0f / l) : 0.f;
+  }
+}
+
+template <int HD>
+int launch_f32_hd(const float* q, const float* k, const float* v, int rows, int past, int heads,
+                  int kv_heads, int window, float* out, cudaStream_t st) {
+  const dim3 grid(kv_heads, rows);
+  const float scale = 1.0f / sqrtf((float)HD);
+  const int kvd = kv_heads * HD;
+  switch (heads / kv_heads) {
+    case 1: k_attn_f32<HD, 1><<<grid, kAttnThreads, 0, st>>>(q, k, v, past, heads, kvd, window, scale, out); break;
+    case 2: k_attn_f32<HD, 2><<<grid, kAttnThreads, 0, st>>>(q, k, v, past, heads, kvd, window, scale, out); break;
+    case 4: k_attn_f32<HD, 4><<<grid, kAttnThreads, 0, st>>>(q, k, v, past, heads, kvd, window, scale, out); break;
+    case 8: k_attn_f32<HD, 8><<<grid, kAttnThreads, 0, st>>>(q, k, v, past, heads, kvd, window, scale, out); break;
+    default: return fail(WL_ERR_UNSUPPORTED, "attention: heads per KV head must be 1, 2, 4 or 8");
+  }
+  WL_CUDA_TRY(cudaGetLastError());
+  return WL_OK;
 }
 
 }  // namespace
 
 int attention_plan_splits(int rows, int kv_heads, int max_len, int num_sms) {
-  int ctas = rows * kv_heads;
-  int target = 2 * num_sms;
+  const int ctas = rows * kv_heads;
+  const int target = 2 * num_sms;
   int ns = (target + ctas - 1) / ctas;
-  int by_len = (max_len + kTile - 1) / kTile;  // at least one tile per split
+  const int pages = (max_len + kPage - 1) / kPage;
+  const int by_len = (pages + 3) / 4;  // at least ~4 pages per split
   ns = ns < by_len ? ns : by_len;
   if (ns > 64) ns = 64;
   return ns < 1 ? 1 : ns;
 }
 
 int launch_attention_paged(const AttnArgs& a, cudaStream_t st) {
-  Params<PagedKV> p;
-  p.kv = PagedKV{a.kv.k, a.kv.v, a.kv.page_table, a.kv.max_pages, a.kv.page, a.kv.kvd};
-  p.ri = RowInfo{a.row_pos, a.row_sess, 0};
-  p.q = a.q;
-  p.ldq = a.ldq;
-  p.heads = a.heads;
-  p.kv_heads = a.kv_heads;
-  p.window = a.window;
-  p.nsplit = a.nsplit;
-  p.scale = 1.0f / sqrtf((float)a.head_dim);
-  p.part_o = a.part_o;
-  p.part_ml = a.part_ml;
-  p.out = a.out;
-  p.ldo = a.ldo;
-  p.out_f16 = a.out_f16;
-  return launch_any(p, a.rows, a.head_dim, st);
+  if (a.kv.page != kPage) return fail(WL_ERR_UNSUPPORTED, "attention: KV page must be 16 tokens");
+  if (a.heads % a.kv_heads) return fail(WL_ERR_INVALID_ARGUMENT, "attention: heads % kv_heads != 0");
+  const int G = a.heads / a.kv_heads;
+  const float scale = 1.0f / sqrtf((float)a.head_dim);
+  switch (a.head_dim) {
+    case 64: return launch_paged_hd<64>(a, G, scale, st);
+    case 128: return launch_paged_hd<128>(a, G, scale, st);
+    case 256: return launch_paged_hd<256>(a, G, scale, st);
+  }
+  return fail(WL_ERR_UNSUPPORTED, "attention: head_dim must be 64, 128 or 256");
 }
 
 int launch_attention_f32(const float* q, const float* k, const float* v, int rows, int past,
                          int heads, int kv_heads, int hd, int window, float* out,
                          cudaStream_t st) {
-  Params<F32KV> p;
-  p.kv = F32KV{k, v, kv_heads * hd};
-  p.ri = RowInfo{nullptr, nullptr, past};
-  p.q = q;
-  p.ldq = heads * hd;
-  p.heads = heads;
-  p.kv_heads = kv_heads;
-  p.window = window;
-  p.nsplit = 1;
-  p.scale = 1.0f / sqrtf((float)hd);
-  p.part_o = nullptr;
-  p.part_ml = nullptr;
-  p.out = out;
-  p.ldo = heads * hd;
-  p.out_f16 = 0;
-  return launch_any(p, rows, hd, st);
+  if (heads % kv_heads) return fail(WL_ERR_INVALID_ARGUMENT, "attention: heads % kv_heads != 0");
+  switch (hd) {
+    case 32: return launch_f32_hd<32>(q, k, v, rows, past, heads, kv_heads, window, out, st);
+    case 64: return launch_f32_hd<64>(q, k, v, rows, past, heads, kv_heads, window, out, st);
+    case 128: return launch_f32_hd<128>(q, k, v, rows, past, heads, kv_heads, window, out, st);
+    case 256: return launch_f32_hd<256>(q, k, v, rows, past, heads, kv_heads, window, out, st);
+  }
+  return fail(WL_ERR_UNSUPPORTED, "attention: head_dim must be 32, 64, 128 or 256");
 }
 
 }  // namespace wl

@@ -41,63 +41,51 @@ int sm_count() {
   return n > 0 ? n : 148;
 }
 
-// stream-ordered scratch for op-level calls
-struct Scratch {
-  void* p = nullptr;
-  cudaStream_t st;
-  explicit Scratch(cudaStream_t s) : st(s) {}
-  int alloc(size_t bytes) {
-    WL_CUDA_TRY(cudaMallocAsync(&p, std::max<size_t>(bytes, 16), st));
-    return WL_OK;
-  }
-  ~Scratch() {
-    if (p) cudaFreeAsync(p, st);
-  }
-};
-
-// y[b][n] = sum_k x[b][k] W(k, n) through the tensor-core GEMV, rows in chunks of 32
+// y[b][n] = sum_k x[b][k] W(k, n) through the tensor-core GEMV, rows in chunks of 32.
+// Layout B takes its activations as f16 hi/lo planes, made here in a
+// stream-ordered temporary.
 int qgemv_op(int type, int layout, const uint8_t* W, int K, int N, const float* x, int B, float* y,
              cudaStream_t st) {
   const int S = bb(type);
   const int pitch = layout == WL_LAYOUT_B ? N / 32 * S : K / 32 * S;
-  Scratch xh(st);
-  WL_TRY(xh.alloc((size_t)B * K * sizeof(__half)));
-  WL_TRY(launch_f32_to_f16(x, (__half*)xh.p, (size_t)B * K, st));
   const bool fast = layout == WL_LAYOUT_B ? qgemv_b_fast_ok(type, K, N, pitch, W)
                                           : qgemv_a_fast_ok(type, K, N, pitch, W);
-  if (!fast)
-    return launch_qgemv_generic(type, layout, W, K, N, pitch, (const __half*)xh.p, K, B, y, N,
-                                false, st);
+  if (!fast) return launch_qgemv_generic(type, layout, W, K, N, pitch, x, 0, K, B, y, N, false, st);
+  __half* planes = nullptr;
+  const size_t n = (size_t)B * K;
+  if (layout == WL_LAYOUT_B) {
+    WL_CUDA_TRY(cudaMallocAsync((void**)&planes, 2 * n * sizeof(__half), st));
+    const int s = launch_split_planes(x, planes, n, n, st);
+    if (s) {
+      cudaFreeAsync(planes, st);
+      return s;
+    }
+  }
   const int gcols = qgemv_group_cols(layout);
-  const int groups = (N + gcols - 1) / gcols;
   GemvArgs a;
   a.type = type;
   a.nseg = 1;
   a.seg[0].W = W;
   a.seg[0].N = N;
   a.seg[0].pitch = pitch;
-  a.seg[0].groups = groups;
+  a.seg[0].groups = (N + gcols - 1) / gcols;
   a.K = K;
-  a.total_cols = groups * gcols;
-  a.B = std::min(B, 32);
-  qgemv_plan(a, layout, sm_count(), &a.ksplit, &a.kchunk);
-  Scratch ws(st);
-  size_t wsf = qgemv_ws_floats(a.ksplit, std::min(B, 32), a.total_cols);
-  size_t cnt_bytes = (size_t)groups * sizeof(unsigned);
-  WL_TRY(ws.alloc(wsf * sizeof(float) + cnt_bytes + 256));
-  a.ws = (float*)ws.p;
-  a.counters = (unsigned*)((uint8_t*)ws.p + (wsf * sizeof(float) + 255) / 256 * 256);
-  WL_CUDA_TRY(cudaMemsetAsync(a.counters, 0, cnt_bytes, st));
-  for (int r0 = 0; r0 < B; r0 += 32) {
+  a.ldx = K;
+  a.xkind = layout == WL_LAYOUT_B ? X_PLANES : X_F32;
+  a.x_plane = n;
+  a.epi.kind = EPI_F32;
+  a.epi.ldy[0] = N;
+  int s = WL_OK;
+  for (int r0 = 0; r0 < B && s == WL_OK; r0 += 32) {
     a.B = std::min(32, B - r0);
-    a.x = (const __half*)xh.p + (size_t)r0 * K;
-    a.ldx = K;
-    a.epi.kind = EPI_F32;
-    a.epi.y = y + (size_t)r0 * N;
-    a.epi.ldy = N;
-    WL_TRY(layout == WL_LAYOUT_B ? launch_qgemv_b(a, st) : launch_qgemv_a(a, st));
+    a.x = layout == WL_LAYOUT_B ? (const void*)(planes + (size_t)r0 * K)
+                                : (const void*)(x + (size_t)r0 * K);
+    a.epi.y[0] = y + (size_t)r0 * N;
+    qgemv_plan(a, layout, sm_count());
+    s = layout == WL_LAYOUT_B ? launch_qgemv_b(a, st) : launch_qgemv_a(a, st);
   }
-  return WL_OK;
+  if (planes) cudaFreeAsync(planes, st);
+  return s;
 }
 
 }  // namespace
@@ -281,7 +269,7 @@ int wl_rmsnorm_rope(const float* x, const float* w, int rows, int dim, float eps
   if (!x || !w || !y || rows < 0 || dim <= 0) return fail(WL_ERR_INVALID_ARGUMENT, "bad argument");
   if (rope_mode == WL_ROPE_NEOX && !pos) return fail(WL_ERR_INVALID_ARGUMENT, "rope needs positions");
   return launch_rmsnorm(x, w, rows, dim, eps, rope_mode == WL_ROPE_NEOX, pos, head_dim, theta, y,
-                        y_f16, (cudaStream_t)stream);
+                        y_f16 ? 1 : 0, 0, (cudaStream_t)stream);
 }
 
 int wl_swiglu(const float* gate, const float* up, size_t n, float* out, void* stream) {

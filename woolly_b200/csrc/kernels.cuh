@@ -13,17 +13,18 @@ namespace wl {
 struct AttnArgs {
   const float* q = nullptr;  // [rows][H*hd] f32
   int ldq = 0;
-  KvPages kv{};
+  KvPages kv{};                   // page size must be 16 tokens
   const int* row_pos = nullptr;   // [rows]
   const int* row_sess = nullptr;  // [rows]
   int rows = 0, heads = 0, kv_heads = 0, head_dim = 0;
   int window = 0;   // 0 = full causal prefix
   int nsplit = 1;
-  float* part_o = nullptr;   // [rows][H][nsplit][hd]
+  float* part_o = nullptr;   // [rows][H][nsplit][hd]   (nsplit > 1)
   float* part_ml = nullptr;  // [rows][H][nsplit][2]
-  void* out = nullptr;       // [rows][H*hd], f16 (out_f16) or f32
+  void* out = nullptr;       // [rows][ldo]: f32, or f16 hi/lo planes when out_plane != 0
   int ldo = 0;
-  int out_f16 = 1;
+  size_t out_plane = 0;      // planes: offset of the lo plane (elements)
+  int* err = nullptr;        // set (bit 1) if a bounded wait gave up
 };
 int launch_attention_paged(const AttnArgs& a, cudaStream_t st);
 
@@ -36,9 +37,10 @@ int launch_attention_f32(const float* q, const float* k, const float* v, int row
 int attention_plan_splits(int rows, int kv_heads, int max_len, int num_sms);
 
 // y = x / sqrt(mean(x^2) + eps) * w per row; optional NeoX rope per head.
+// y_mode: 0 f32, 1 f16, 2 f16 hi/lo planes (lo plane y_plane elements after hi).
 int launch_rmsnorm(const float* x, const float* w, int rows, int dim, float eps, int rope,
-                   const int* pos, int head_dim, float theta, void* y, int y_f16,
-                   cudaStream_t st);
+                   const int* pos, int head_dim, float theta, void* y, int y_mode,
+                   size_t y_plane, cudaStream_t st);
 
 // h[r][j] = E[j*V + ids[r]] (token_embd stored [d][V], lazy_transformer.rs:1252-1262)
 int launch_embed(const float* E, int d, int V, const uint32_t* ids, int rows, float* h,

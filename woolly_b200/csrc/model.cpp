@@ -273,28 +273,33 @@ static int allreduce_sum(wl_model* m, float* buf, size_t count) {
 }
 
 // ------------------------------------------------------------------ GEMV dispatch
-// y rows r in [0, R): up to 32 rows per launch.
-static int gemv(wl_model* m, int nseg, const QMat* mats, int R, const __half* x, int ldx,
-                Epilogue epi, int ldy_elems, size_t y_elem_bytes) {
+// rows r in [0, R) of x (f16 hi/lo planes, lo plane x_plane elements after
+// hi), up to 32 rows per launch.
+static int gemv(wl_model* m, int nseg, const QMat* mats, int R, const __half* x, size_t x_plane,
+                int ldx, Epilogue epi) {
   for (int s = 0; s < nseg; s++)
     if (mats[s].type != mats[0].type)
       return fail(WL_ERR_UNSUPPORTED, "fused GEMV segments must share a quantization type");
-  const bool quant = block_bytes(mats[0].type) != 0;
+  bool fast = block_bytes(mats[0].type) != 0;
+  for (int s = 0; s < nseg && fast; s++)
+    fast = qgemv_b_fast_ok(mats[s].type, mats[s].K, mats[s].N, mats[s].pitch, mats[s].w);
+  if (!fast && (nseg != 1 || !(epi.kind == EPI_F32 || epi.kind == EPI_ADD)))
+    return fail(WL_ERR_UNSUPPORTED, "GEMV: unaligned or F32 weights only support plain outputs");
+  const bool sw = epi.kind == EPI_SWIGLU;
+  if (sw && (nseg != 2 || mats[0].N != mats[1].N))
+    return fail(WL_ERR_INVALID_ARGUMENT, "SwiGLU GEMV needs gate and up of equal width");
   for (int r0 = 0; r0 < R; r0 += 32) {
     const int b = std::min(32, R - r0);
     Epilogue e = epi;
-    if (e.y) e.y = (uint8_t*)e.y + (size_t)r0 * ldy_elems * y_elem_bytes;
+    for (int s = 0; s < 3; s++)
+      if (e.y[s])
+        e.y[s] = (uint8_t*)e.y[s] + (size_t)r0 * e.ldy[s] * (sw ? sizeof(__half) : sizeof(float));
     if (e.row_pos) e.row_pos += r0;
     if (e.row_sess) e.row_sess += r0;
     const __half* xr = x + (size_t)r0 * ldx;
-    bool fast = quant;
-    for (int s = 0; s < nseg && fast; s++)
-      fast = qgemv_b_fast_ok(mats[s].type, mats[s].K, mats[s].N, mats[s].pitch, mats[s].w);
     if (!fast) {
-      if (nseg != 1 || !(e.kind == EPI_F32 || e.kind == EPI_ADD))
-        return fail(WL_ERR_UNSUPPORTED, "GEMV: unaligned or F32 weights only support plain outputs");
       WL_TRY(launch_qgemv_generic(mats[0].type, WL_LAYOUT_B, mats[0].w, mats[0].K, mats[0].N,
-                                  mats[0].pitch, xr, ldx, b, (float*)e.y, e.ldy,
+                                  mats[0].pitch, xr, x_plane, ldx, b, (float*)e.y[0], e.ldy[0],
                                   e.kind == EPI_ADD, m->st));
       continue;
     }
@@ -312,15 +317,12 @@ static int gemv(wl_model* m, int nseg, const QMat* mats, int R, const __half* x,
     }
     a.K = mats[0].K;
     a.B = b;
+    a.xkind = X_PLANES;
     a.x = xr;
+    a.x_plane = x_plane;
     a.ldx = ldx;
-    a.total_cols = gb * 256;
     a.epi = e;
-    qgemv_plan(a, WL_LAYOUT_B, m->sms, &a.ksplit, &a.kchunk);
-    if (qgemv_ws_floats(a.ksplit, b, a.total_cols) > m->ws_floats || gb > m->n_counters)
-      return fail(WL_ERR_INVALID_ARGUMENT, "GEMV workspace too small");
-    a.ws = m->ws;
-    a.counters = m->counters;
+    qgemv_plan(a, WL_LAYOUT_B, m->sms);
     WL_TRY(launch_qgemv_b(a, m->st));
   }
   return WL_OK;
@@ -331,22 +333,28 @@ static int gemv(wl_model* m, int nseg, const QMat* mats, int R, const __half* x,
 static int run_rows(wl_model* m, int R, int nsplit, int lfirst) {
   cudaStream_t st = m->st;
   const bool tp = m->tp_size > 1;
+  const int qd = m->Hl * m->hd;
+  const size_t xpl = (size_t)m->MR * m->d;  // lo-plane offsets
+  const size_t apl = (size_t)m->MR * qd;
+  const size_t fpl = (size_t)m->MR * m->ffl;
   WL_TRY(launch_embed(m->embd, m->d, m->V, m->ids, R, m->h, m->err, st));
   for (int l = 0; l < m->L; l++) {
     const Layer& y = m->layers[l];
-    WL_TRY(launch_rmsnorm(m->h, y.attn_norm, R, m->d, m->eps, 0, nullptr, 0, 0.f, m->xn, 1, st));
+    WL_TRY(launch_rmsnorm(m->h, y.attn_norm, R, m->d, m->eps, 0, nullptr, 0, 0.f, m->xn, 2, xpl, st));
     KvPages kv;
-    kv.k = reinterpret_cast<__half*>(m->kvbuf + (size_t)l * 2 * m->n_pages * m->page * m->kvdl * 2);
-    kv.v = kv.k + (size_t)m->n_pages * m->page * m->kvdl;
+    const size_t layer_halves = (size_t)m->n_pages * m->page * m->kvdl;
+    kv.k = reinterpret_cast<__half*>(m->kvbuf) + (size_t)l * 2 * layer_halves;
+    kv.v = kv.k + layer_halves;
     kv.page_table = m->d_tables;
     kv.max_pages = m->max_pages;
     kv.page = m->page;
-    kv.kvd = m->kvdl;
+    kv.kv_heads = m->KVHl;
+    kv.head_dim = m->hd;
     {
       Epilogue e;
       e.kind = EPI_QKV;
-      e.y = m->q;
-      e.ldy = m->Hl * m->hd;
+      e.y[0] = m->q;
+      e.ldy[0] = qd;
       e.rope = m->rope;
       e.head_dim = m->hd;
       e.theta = m->theta;
@@ -354,12 +362,12 @@ static int run_rows(wl_model* m, int R, int nsplit, int lfirst) {
       e.row_sess = m->row_sess;
       e.kv = kv;
       QMat segs[3] = {y.wq, y.wk, y.wv};
-      WL_TRY(gemv(m, 3, segs, R, m->xn, m->d, e, e.ldy, 4));
+      WL_TRY(gemv(m, 3, segs, R, m->xn, xpl, m->d, e));
     }
     {
       AttnArgs a;
       a.q = m->q;
-      a.ldq = m->Hl * m->hd;
+      a.ldq = qd;
       a.kv = kv;
       a.row_pos = m->row_pos;
       a.row_sess = m->row_sess;
@@ -372,45 +380,47 @@ static int run_rows(wl_model* m, int R, int nsplit, int lfirst) {
       a.part_o = m->part_o;
       a.part_ml = m->part_ml;
       a.out = m->att;
-      a.ldo = m->Hl * m->hd;
-      a.out_f16 = 1;
+      a.ldo = qd;
+      a.out_plane = apl;
+      a.err = m->err;
       WL_TRY(launch_attention_paged(a, st));
     }
     {
       Epilogue e;
       e.kind = (tp && m->tp_rank != 0) ? EPI_F32 : EPI_ADD;  // rank 0 carries the residual
-      e.y = m->h;
-      e.ldy = m->d;
-      WL_TRY(gemv(m, 1, &y.wo, R, m->att, m->Hl * m->hd, e, m->d, 4));
+      e.y[0] = m->h;
+      e.ldy[0] = m->d;
+      WL_TRY(gemv(m, 1, &y.wo, R, m->att, apl, qd, e));
       if (tp) WL_TRY(allreduce_sum(m, m->h, (size_t)R * m->d));
     }
-    WL_TRY(launch_rmsnorm(m->h, y.ffn_norm, R, m->d, m->eps, 0, nullptr, 0, 0.f, m->xn, 1, st));
+    WL_TRY(launch_rmsnorm(m->h, y.ffn_norm, R, m->d, m->eps, 0, nullptr, 0, 0.f, m->xn, 2, xpl, st));
     {
       Epilogue e;
       e.kind = EPI_SWIGLU;
-      e.y = m->act;
-      e.ldy = m->ffl;
+      e.y[0] = m->act;
+      e.ldy[0] = m->ffl;
+      e.y_plane = fpl;
       QMat segs[2] = {y.wg, y.wu};
-      WL_TRY(gemv(m, 2, segs, R, m->xn, m->d, e, m->ffl, 2));
+      WL_TRY(gemv(m, 2, segs, R, m->xn, xpl, m->d, e));
     }
     {
       Epilogue e;
       e.kind = (tp && m->tp_rank != 0) ? EPI_F32 : EPI_ADD;
-      e.y = m->h;
-      e.ldy = m->d;
-      WL_TRY(gemv(m, 1, &y.wd, R, m->act, m->ffl, e, m->d, 4));
+      e.y[0] = m->h;
+      e.ldy[0] = m->d;
+      WL_TRY(gemv(m, 1, &y.wd, R, m->act, fpl, m->ffl, e));
       if (tp) WL_TRY(allreduce_sum(m, m->h, (size_t)R * m->d));
     }
   }
   const int nl = R - lfirst;
   if (nl > 0) {
     WL_TRY(launch_rmsnorm(m->h + (size_t)lfirst * m->d, m->out_norm, nl, m->d, m->eps, 0, nullptr,
-                          0, 0.f, m->xn, 1, st));
+                          0, 0.f, m->xn, 2, xpl, st));
     Epilogue e;
     e.kind = EPI_F32;
-    e.y = m->logits;
-    e.ldy = m->V;
-    WL_TRY(gemv(m, 1, &m->out, nl, m->xn, m->d, e, m->V, 4));
+    e.y[0] = m->logits;
+    e.ldy[0] = m->V;
+    WL_TRY(gemv(m, 1, &m->out, nl, m->xn, xpl, m->d, e));
   }
   return WL_OK;
 }
@@ -561,8 +571,8 @@ int model_load(wl_ctx* ctx, const char* path, const wl_model_options* o, wl_mode
   m->ffl = m->ff / T;
   if ((m->hd % 32) || (m->Hl * m->hd) % 32 || m->kvdl % 32)
     return fail(WL_ERR_UNSUPPORTED, "head_dim must be a multiple of 32");
-  if (m->rope && 256 % m->hd)
-    return fail(WL_ERR_UNSUPPORTED, "fused RoPE needs head_dim dividing 256");
+  if (m->hd != 64 && m->hd != 128 && m->hd != 256)
+    return fail(WL_ERR_UNSUPPORTED, "head_dim must be 64, 128 or 256");
 
   // ---- plan the weight buffer ----
   Loader ld{g, m.get()};
@@ -639,18 +649,11 @@ int model_load(wl_ctx* ctx, const char* path, const wl_model_options* o, wl_mode
   // ---- scratch ----
   const int MR = m->MR = std::max(opt.max_batch, opt.max_prefill);
   WL_TRY(dalloc(&m->h, (size_t)MR * d));
-  WL_TRY(dalloc(&m->xn, (size_t)MR * d));
+  WL_TRY(dalloc(&m->xn, (size_t)2 * MR * d));
   WL_TRY(dalloc(&m->q, (size_t)MR * m->Hl * m->hd));
-  WL_TRY(dalloc(&m->att, (size_t)MR * m->Hl * m->hd));
-  WL_TRY(dalloc(&m->act, (size_t)MR * m->ffl));
+  WL_TRY(dalloc(&m->att, (size_t)2 * MR * m->Hl * m->hd));
+  WL_TRY(dalloc(&m->act, (size_t)2 * MR * m->ffl));
   WL_TRY(dalloc(&m->logits, (size_t)MR * V));
-  int max_groups = std::max({(m->Hl * m->hd + 2 * m->kvdl + 255) / 256 + 3, 2 * ((m->ffl + 255) / 256),
-                             (V + 255) / 256, (d + 255) / 256});
-  m->n_counters = std::max(max_groups, 1024);
-  m->ws_floats = (size_t)(2 * m->sms + max_groups + 2) * 32 * 256;
-  WL_TRY(dalloc(&m->ws, m->ws_floats));
-  WL_TRY(dalloc(&m->counters, (size_t)m->n_counters));
-  WL_CUDA_TRY(cudaMemsetAsync(m->counters, 0, (size_t)m->n_counters * sizeof(unsigned), m->st));
   m->part_rows = (size_t)2 * m->sms + MR;
   WL_TRY(dalloc(&m->part_o, m->part_rows * m->Hl * m->hd));
   WL_TRY(dalloc(&m->part_ml, m->part_rows * m->Hl * 2));
@@ -681,8 +684,6 @@ void model_free(wl_model* m) {
   cudaFree(m->att);
   cudaFree(m->act);
   cudaFree(m->logits);
-  cudaFree(m->ws);
-  cudaFree(m->counters);
   cudaFree(m->part_o);
   cudaFree(m->part_ml);
   cudaFree(m->row_pos);
@@ -803,7 +804,7 @@ int decode_step_device(wl_model* m, wl_session* const* ss, int n, const uint32_t
   std::lock_guard<std::mutex> lk(m->mu);
   WL_CUDA_TRY(cudaSetDevice(m->dev));
   cudaEvent_t ev = nullptr;
-  if (user && user != m->st) {  // order after the caller's work
+  if (user != m->st) {  // order after the caller's work (0 = the legacy default stream)
     WL_CUDA_TRY(cudaEventCreateWithFlags(&ev, cudaEventDisableTiming));
     cudaEventRecord(ev, user);
     cudaStreamWaitEvent(m->st, ev, 0);

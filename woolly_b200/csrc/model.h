@@ -68,19 +68,15 @@ struct wl_model {
   std::vector<wl_session*> slots;
   // scratch (rows = max(max_batch, max_prefill))
   int MR = 0;
-  float* h = nullptr;
-  __half* xn = nullptr;
-  float* q = nullptr;
-  __half* att = nullptr;
-  __half* act = nullptr;
-  float* logits = nullptr;
-  float* ws = nullptr;
-  size_t ws_floats = 0;
-  unsigned* counters = nullptr;
-  int n_counters = 0;
-  float* part_o = nullptr;
+  float* h = nullptr;       // residual stream [MR][d]
+  __half* xn = nullptr;     // normalised rows as f16 hi/lo planes [2][MR][d]
+  float* q = nullptr;       // queries [MR][Hl*hd]
+  __half* att = nullptr;    // attention output planes [2][MR][Hl*hd]
+  __half* act = nullptr;    // SwiGLU output planes [2][MR][ffl]
+  float* logits = nullptr;  // [MR][V]
+  float* part_o = nullptr;  // attention split partials
   float* part_ml = nullptr;
-  size_t part_rows = 0;  // capacity in rows*nsplit
+  size_t part_rows = 0;     // capacity in rows*nsplit
   int* row_pos = nullptr;
   int* row_sess = nullptr;
   uint32_t* ids = nullptr;

@@ -16,9 +16,19 @@ constexpr int kNormThreads = 256;
 // rms_norm (woolly-core tensor_utils.rs:446-480): rms = sqrt(sum(x^2)/d + eps),
 // y = (x / rms) * w, with an optional NeoX rotation (RoPE::apply_f32,
 // woolly-tensor/src/ops/mod.rs:476-527) of the normalised row, head by head.
+__device__ __forceinline__ void put_y(void* y, int mode, size_t plane, size_t i, float v) {
+  if (mode == 0) {
+    reinterpret_cast<float*>(y)[i] = v;
+  } else {
+    const __half hi = __float2half_rn(v);
+    reinterpret_cast<__half*>(y)[i] = hi;
+    if (mode == 2) reinterpret_cast<__half*>(y)[i + plane] = __float2half_rn(v - __half2float(hi));
+  }
+}
+
 __global__ void __launch_bounds__(kNormThreads)
     k_rmsnorm(const float* x, const float* w, int dim, float eps, int rope, const int* pos,
-              int hd, float theta, void* y, int y_f16) {
+              int hd, float theta, void* y, int y_mode, size_t y_plane) {
   extern __shared__ float srow[];  // normalised row when rope is on
   __shared__ float sred[kNormThreads / 32];
   const int r = blockIdx.x, tid = threadIdx.x;
@@ -38,13 +48,8 @@ __global__ void __launch_bounds__(kNormThreads)
   __syncthreads();
   const float rms = sqrtf(sred[0] / (float)dim + eps);
   if (!rope) {
-    for (int i = tid; i < dim; i += kNormThreads) {
-      float v = __fdiv_rn(xr[i], rms) * w[i];
-      if (y_f16)
-        reinterpret_cast<__half*>(y)[(size_t)r * dim + i] = __float2half_rn(v);
-      else
-        reinterpret_cast<float*>(y)[(size_t)r * dim + i] = v;
-    }
+    for (int i = tid; i < dim; i += kNormThreads)
+      put_y(y, y_mode, y_plane, (size_t)r * dim + i, __fdiv_rn(xr[i], rms) * w[i]);
     return;
   }
   for (int i = tid; i < dim; i += kNormThreads) srow[i] = __fdiv_rn(xr[i], rms) * w[i];
@@ -58,14 +63,8 @@ __global__ void __launch_bounds__(kNormThreads)
     float sn, cs;
     sincosf(p * freq, &sn, &cs);
     float x1 = srow[c1], x2 = srow[c2];
-    float o1 = x1 * cs - x2 * sn, o2 = x1 * sn + x2 * cs;
-    if (y_f16) {
-      reinterpret_cast<__half*>(y)[(size_t)r * dim + c1] = __float2half_rn(o1);
-      reinterpret_cast<__half*>(y)[(size_t)r * dim + c2] = __float2half_rn(o2);
-    } else {
-      reinterpret_cast<float*>(y)[(size_t)r * dim + c1] = o1;
-      reinterpret_cast<float*>(y)[(size_t)r * dim + c2] = o2;
-    }
+    put_y(y, y_mode, y_plane, (size_t)r * dim + c1, x1 * cs - x2 * sn);
+    put_y(y, y_mode, y_plane, (size_t)r * dim + c2, x1 * sn + x2 * cs);
   }
 }
 
@@ -147,8 +146,8 @@ __global__ void k_f16_to_f32(const uint8_t* src, size_t n, float* out) {
 }  // namespace
 
 int launch_rmsnorm(const float* x, const float* w, int rows, int dim, float eps, int rope,
-                   const int* pos, int head_dim, float theta, void* y, int y_f16,
-                   cudaStream_t st) {
+                   const int* pos, int head_dim, float theta, void* y, int y_mode,
+                   size_t y_plane, cudaStream_t st) {
   if (rows <= 0) return WL_OK;
   size_t smem = rope ? (size_t)dim * sizeof(float) : 0;
   if (rope && (head_dim <= 0 || dim % head_dim || head_dim % 2))
@@ -157,7 +156,8 @@ int launch_rmsnorm(const float* x, const float* w, int rows, int dim, float eps,
     WL_CUDA_TRY(cudaFuncSetAttribute(k_rmsnorm, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      (int)smem));
   }
-  k_rmsnorm<<<rows, kNormThreads, smem, st>>>(x, w, dim, eps, rope, pos, head_dim, theta, y, y_f16);
+  k_rmsnorm<<<rows, kNormThreads, smem, st>>>(x, w, dim, eps, rope, pos, head_dim, theta, y, y_mode,
+                                             y_plane);
   WL_CUDA_TRY(cudaGetLastError());
   return WL_OK;
 }

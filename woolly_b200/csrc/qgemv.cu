@@ -8,20 +8,24 @@
 //    y[b, r] = sum_k W[r*K + k] * x[b, k] (blocks run along K).
 //
 // Design (HBM-bound):
-//  * A CTA streams a [rows x 8 blocks] byte tile of the weight matrix through
-//    a 4-stage cp.async.cg (16-byte, L1-bypassing) pipeline: every global load
-//    is a full, aligned 16-byte vector of the block stream, uploaded unchanged.
-//  * Each warp dequantizes straight from the staged bytes into mma.sync
-//    m16n8k16 A-fragments in registers (LOP3 nibble -> f16 exponent trick,
-//    exact q and q-8 in f16, one f16 rounding of q*d or q*d+m); the rows of x
-//    (f16) are the B operand, so one dequant feeds every row of the batch.
-//    The dequantized weights never touch shared memory.
-//  * The output index each A-fragment row maps to is permuted so that every
-//    thread reads whole 16-bit words of the block payload.
-//  * K is split across CTAs to fill all 148 SMs; partial sums go to a
-//    workspace and the last-arriving CTA of each column group reduces them in
-//    split order (deterministic) and runs the fused epilogue (residual add,
-//    QKV split with RoPE and paged-KV append, SiLU(gate)*up, f16 cast).
+//  * One CTA owns a tile of 8 quant blocks along a matrix row (256 columns in
+//    layout B, 256 K-values in layout A) and streams its K-slice of rows
+//    through a 4-stage cp.async.cg (16-byte, L1-bypassing) pipeline together
+//    with the matching activation tile, so every global load is an aligned
+//    16-byte vector of the block stream, uploaded unchanged.
+//  * The MMA sees exact operands: A = the integer codes (q-8 for Q4_0, q for
+//    Q4_1 / Q8_0, exact in f16; built with PRMT + LOP3 from the staged bytes
+//    and the f16 exponent trick, never written back to shared memory), and
+//    B = the activation times the block scale carried as an f16 hi/lo pair
+//    ((x*d)_hi + (x*d)_lo, ~22 bits) built with HMUL2/HFMA2 from the hi/lo
+//    activation planes.  Q4_1's min term sum_k x*m rides on an extra MMA with
+//    an all-ones A.  m16n8k16 mma.sync with f32 accumulation.
+//  * K is split across the CTAs of a thread-block cluster (up to 16); the
+//    partial tiles are reduced through distributed shared memory in rank order
+//    (deterministic), each CTA finishing a strided slice of the outputs and
+//    applying the fused epilogue (residual add, QKV split with RoPE and
+//    paged-KV append, SiLU(gate)*up with gate and up in one cluster).
+#include <cooperative_groups.h>
 #include <cuda_fp16.h>
 
 #include <algorithm>
@@ -29,6 +33,8 @@
 
 #include "common.h"
 #include "qgemv.cuh"
+
+namespace cg = cooperative_groups;
 
 namespace wl {
 namespace {
@@ -51,9 +57,10 @@ struct QT<WL_Q8_0> {
 constexpr int kThreads = 128;
 constexpr int kRows = 64;  // matrix rows per pipeline stage
 constexpr int kStages = 4;
-constexpr int kGroupBlocks = 8;  // quant blocks per row in one stage tile
+constexpr int kGroupBlocks = 8;  // quant blocks per tile row
 constexpr int kColsB = 256;      // output columns per CTA, layout B
 constexpr int kColsA = 64;       // output rows per CTA, layout A
+constexpr int kMaxCluster = 16;
 
 __device__ __forceinline__ void cp_async16(void* smem, const void* gmem, int src_bytes) {
   unsigned s = (unsigned)__cvta_generic_to_shared(smem);
@@ -87,262 +94,328 @@ __device__ __forceinline__ uint32_t as_u(__half2 h) {
 __device__ __forceinline__ uint32_t ld16(const uint8_t* p) {
   return *reinterpret_cast<const uint16_t*>(p);
 }
-
-// f16 magic: 0x6400 | q is the half 1024 + q (exact for q < 1024).
-constexpr uint32_t kMagic = 0x64006400u;
-
-// Two 4-bit codes in f16 lanes (1024+q) -> weights.  Q4_0: (q-8)*d, Q4_1: q*d+m.
-template <int T>
-__device__ __forceinline__ uint32_t q4w(uint32_t h, uint32_t d, uint32_t m) {
-  if constexpr (T == WL_Q4_0) {
-    return as_u(__hmul2(__hsub2(as_h2(h), as_h2(0x64086408u)), as_h2(d)));  // 1032 = 1024+8
-  } else {
-    return as_u(__hfma2(__hsub2(as_h2(h), as_h2(kMagic)), as_h2(d), as_h2(m)));
-  }
+__device__ __forceinline__ uint32_t hsub2u(uint32_t a, uint32_t b) {
+  return as_u(__hsub2(as_h2(a), as_h2(b)));
 }
-// Two int8 codes (bytes 0 and 2 of v) -> weights q*d.
-__device__ __forceinline__ uint32_t q8w(uint32_t v, uint32_t d) {
-  uint32_t h = ((v & 0x00FF00FFu) ^ 0x00800080u) | kMagic;             // 1024 + q + 128
-  return as_u(__hmul2(__hsub2(as_h2(h), as_h2(0x64806480u)), as_h2(d)));  // - 1152
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
+  return __byte_perm(a, b, sel);
+}
+
+// 0x6400 | c is the f16 value 1024 + c (exact for c < 1024).
+constexpr uint32_t kMagic = 0x64006400u;
+constexpr uint32_t kOnes = 0x3C003C00u;  // half2(1, 1)
+
+// low-nibble codes in f16 lanes (1024+q) -> exact q-8 (Q4_0) or q (Q4_1)
+template <int T>
+__device__ __forceinline__ uint32_t q4a(uint32_t h) {
+  return hsub2u(h, T == WL_Q4_0 ? 0x64086408u : kMagic);
+}
+// high-nibble codes in f16 lanes (1024+16q) -> exact 16(q-8) (Q4_0) or 16q (Q4_1)
+template <int T>
+__device__ __forceinline__ uint32_t q4a_hi(uint32_t h) {
+  return hsub2u(h, T == WL_Q4_0 ? 0x64806480u : kMagic);
+}
+// int8 codes in bytes 0 and 2 of v (bytes 1 and 3 zero) -> exact q in f16 lanes
+__device__ __forceinline__ uint32_t q8a(uint32_t v) {
+  return hsub2u((v ^ 0x00800080u) | kMagic, 0x64806480u);  // 1024 + q + 128 - 1152
+}
+
+// (d*x) as an f16 pair hi + lo: hi = f16(d*xh), lo = f16(d*xl + (d*xh - hi));
+// the residual d*xh - hi is exact in f16, so hi + lo carries ~22 bits.
+__device__ __forceinline__ void scale_split(uint32_t d, uint32_t xh, uint32_t xl, uint32_t& hi,
+                                            uint32_t& lo) {
+  __half2 hh = __hmul2(as_h2(d), as_h2(xh));
+  __half2 r = __hfma2(as_h2(d), as_h2(xh), as_h2(as_u(hh) ^ 0x80008000u));
+  hi = as_u(hh);
+  lo = as_u(__hfma2(as_h2(d), as_h2(xl), r));
 }
 
 __device__ __forceinline__ float silu(float g) { return g * (1.0f / (1.0f + expf(-g))); }
 
-// ------------------------------------------------------------------ epilogue
-// `tile` holds the final sums [b][c] (row pitch tp) for this CTA's columns:
-// segment `seg`, segment-local first column col0, `nc` valid columns.
-__device__ void apply_epilogue(const GemvArgs& a, int seg, int col0, int nc, float* tile, int tp) {
-  const Epilogue& e = a.epi;
-  const int B = a.B;
-  const int tid = threadIdx.x;
-  if (e.kind == EPI_QKV && e.rope && seg < 2) {
-    // NeoX rotation of (i, i + hd/2) inside each head (RoPE::apply_f32,
-    // woolly-tensor/src/ops/mod.rs:476-527); col0 is a multiple of head_dim.
-    const int hd = e.head_dim, half = hd / 2;
-    const int npairs = nc / 2;
-    for (int i = tid; i < B * npairs; i += blockDim.x) {
-      int b = i / npairs, j = i % npairs;
-      int h = j / half, ii = j % half;
-      int c1 = h * hd + ii, c2 = c1 + half;
-      float freq = 1.0f / powf(e.theta, 2.0f * (float)ii / (float)hd);
-      float ang = (float)e.row_pos[b] * freq;
-      float sn, cs;
-      sincosf(ang, &sn, &cs);
-      float x1 = tile[b * tp + c1], x2 = tile[b * tp + c2];
-      tile[b * tp + c1] = x1 * cs - x2 * sn;
-      tile[b * tp + c2] = x1 * sn + x2 * cs;
-    }
-    __syncthreads();
-  }
-  for (int i = tid; i < B * nc; i += blockDim.x) {
-    int b = i / nc, c = i % nc;
-    float v = tile[b * tp + c];
-    int col = col0 + c;
-    switch (e.kind) {
-      case EPI_F32:
-        reinterpret_cast<float*>(e.y)[(size_t)b * e.ldy + col] = v;
-        break;
-      case EPI_ADD:
-        reinterpret_cast<float*>(e.y)[(size_t)b * e.ldy + col] += v;
-        break;
-      case EPI_F16:
-      case EPI_SWIGLU:
-        reinterpret_cast<__half*>(e.y)[(size_t)b * e.ldy + col] = __float2half_rn(v);
-        break;
-      case EPI_QKV: {
-        if (seg == 0) {
-          reinterpret_cast<float*>(e.y)[(size_t)b * e.ldy + col] = v;
-        } else {
-          int p = e.row_pos[b];
-          int pg = e.kv.page_table[(size_t)e.row_sess[b] * e.kv.max_pages + p / e.kv.page];
-          size_t off = ((size_t)pg * e.kv.page + (p % e.kv.page)) * e.kv.kvd + col;
-          (seg == 1 ? e.kv.k : e.kv.v)[off] = __float2half_rn(v);
-        }
-        break;
-      }
-    }
+// Layout A: cp.async copies of one stage's f32 activation tile [BP][KC]; rows
+// >= B and columns >= k1 are zero-filled.
+__device__ __forceinline__ void load_x_f32(const GemvArgs& a, float* dst, int BP, int KC, int kk0,
+                                           int k1) {
+  const int nch = KC / 4;
+  const float* x = reinterpret_cast<const float*>(a.x);
+  for (int i = threadIdx.x; i < BP * nch; i += blockDim.x) {
+    const int b = i / nch, c = i - b * nch;
+    const int k = kk0 + c * 4;
+    const bool ok = b < a.B && k < k1;
+    cp_async16(dst + b * KC + c * 4, x + (ok ? (size_t)b * a.ldx + k : 0), ok ? 16 : 0);
   }
 }
 
-// Split-K completion: returns true in the CTA that must run the epilogue; in
-// that CTA `tile` then holds the reduced sums.  `unit` indexes counters.
-template <int TC>
-__device__ bool splitk_finish(const GemvArgs& a, int split, int gcol0, int unit, int ncols_valid,
-                              float* tile, int tp, bool swiglu, int up_gcol0) {
-  const int tid = threadIdx.x;
+// f32 tile [BP][KC] -> hi/lo planes [2][BP][XP]
+__device__ __forceinline__ void split_tile(const float* src, __half* xs, int BP, int KC, int XP) {
+  for (int i = threadIdx.x; i < BP * KC; i += blockDim.x) {
+    const int b = i / KC, k = i - b * KC;
+    const float v = src[i];
+    const __half hi = __float2half_rn(v);
+    xs[b * XP + k] = hi;
+    xs[BP * XP + b * XP + k] = __float2half_rn(v - __half2float(hi));
+  }
+}
+
+// ------------------------------------------------------------------ epilogue
+__device__ __forceinline__ void store_out(const GemvArgs& a, int seg, int b, int col, float v) {
+  const Epilogue& e = a.epi;
+  switch (e.kind) {
+    case EPI_F32:
+      reinterpret_cast<float*>(e.y[seg])[(size_t)b * e.ldy[seg] + col] = v;
+      break;
+    case EPI_ADD:
+      reinterpret_cast<float*>(e.y[seg])[(size_t)b * e.ldy[seg] + col] += v;
+      break;
+    case EPI_QKV:
+      if (seg == 0) {
+        reinterpret_cast<float*>(e.y[0])[(size_t)b * e.ldy[0] + col] = v;
+      } else {
+        const int p = e.row_pos[b];
+        const int pg = e.kv.page_table[(size_t)e.row_sess[b] * e.kv.max_pages + p / e.kv.page];
+        const size_t off =
+            kv_offset(e.kv, pg, p % e.kv.page, col / e.kv.head_dim, col % e.kv.head_dim);
+        (seg == 1 ? e.kv.k : e.kv.v)[off] = __float2half_rn(v);
+      }
+      break;
+  }
+}
+
+// Cluster reduction of the partial tiles (row pitch tp, `cols` per row) and
+// the epilogue for segment `seg`, segment-local first column col0.  Each CTA
+// of the cluster finishes every C-th element; partials are summed in rank
+// order (deterministic).  RoPE pairs (i, i + hd/2) are finished together.
+// For EPI_SWIGLU the cluster holds gate tiles at even ranks and the matching
+// up tiles at odd ranks.
+__device__ void cluster_finish(const GemvArgs& a, float* tile, int tp, int cols, int ncv, int seg,
+                               int col0) {
+  cg::cluster_group cl = cg::this_cluster();
+  const int C = (int)cl.num_blocks();
+  const int r = (int)cl.block_rank();
   const int B = a.B;
-  float* wsp = a.ws + (size_t)split * B * a.total_cols;
-  for (int i = tid; i < B * TC; i += blockDim.x) {
-    int b = i / TC, c = i % TC;
-    if (c < ncols_valid) wsp[(size_t)b * a.total_cols + gcol0 + c] = tile[b * tp + c];
-  }
-  __threadfence();
-  __syncthreads();
-  __shared__ unsigned s_last;
-  if (tid == 0) {
-    unsigned target = (unsigned)a.ksplit * (swiglu ? 2u : 1u);
-    unsigned prev = atomicAdd(&a.counters[unit], 1u);
-    s_last = prev == target - 1;
-    if (s_last) a.counters[unit] = 0;  // ready for the next launch
-  }
-  __syncthreads();
-  if (!s_last) return false;
-  __threadfence();
-  const size_t sstride = (size_t)B * a.total_cols;
-  for (int i = tid; i < B * TC; i += blockDim.x) {
-    int b = i / TC, c = i % TC;
-    if (c >= ncols_valid) continue;
-    if (swiglu) {
-      // gate columns live at [unit*TC], up columns at [up_gcol0]
-      const float* pg = a.ws + (size_t)b * a.total_cols + (size_t)unit * TC + c;
-      const float* pu = a.ws + (size_t)b * a.total_cols + up_gcol0 + c;
-      float g = 0.f, u = 0.f;
-      for (int s = 0; s < a.ksplit; s++) g += __ldcg(pg + s * sstride), u += __ldcg(pu + s * sstride);
-      tile[b * tp + c] = silu(g) * u;
-    } else {
-      const float* p = a.ws + (size_t)b * a.total_cols + gcol0 + c;
-      float acc = 0.f;
-      for (int s = 0; s < a.ksplit; s++) acc += __ldcg(p + s * sstride);
-      tile[b * tp + c] = acc;
+  const float* rt[kMaxCluster];
+#pragma unroll
+  for (int q = 0; q < kMaxCluster; q++) rt[q] = q < C ? cl.map_shared_rank(tile, q) : nullptr;
+  cl.sync();  // every partial tile is complete
+  const Epilogue& e = a.epi;
+  if (e.kind == EPI_SWIGLU) {
+    __half* out = reinterpret_cast<__half*>(e.y[0]);
+    for (int i = r + C * threadIdx.x; i < B * cols; i += C * blockDim.x) {
+      const int b = i / cols, c = i - b * cols;
+      if (c >= ncv) continue;
+      float gs = 0.f, us = 0.f;
+      for (int q = 0; q < C; q += 2) gs += rt[q][b * tp + c], us += rt[q + 1][b * tp + c];
+      const float v = silu(gs) * us;  // swiglu, tensor_utils.rs:512-532
+      const __half hi = __float2half_rn(v);
+      const size_t o = (size_t)b * e.ldy[0] + col0 + c;
+      out[o] = hi;
+      out[o + e.y_plane] = __float2half_rn(v - __half2float(hi));
+    }
+  } else if (e.kind == EPI_QKV && e.rope && seg < 2) {
+    // NeoX rotation inside each head (RoPE::apply_f32, woolly-tensor/src/ops/mod.rs:476-527);
+    // col0 is a multiple of head_dim.
+    const int hd = e.head_dim, half = hd / 2;
+    const int np = ncv / 2;
+    for (int i = r + C * threadIdx.x; i < B * np; i += C * blockDim.x) {
+      const int b = i / np, j = i - b * np;
+      const int h = j / half, ii = j - h * half;
+      const int c1 = h * hd + ii, c2 = c1 + half;
+      float x1 = 0.f, x2 = 0.f;
+      for (int q = 0; q < C; q++) x1 += rt[q][b * tp + c1], x2 += rt[q][b * tp + c2];
+      const float freq = 1.0f / powf(e.theta, 2.0f * (float)ii / (float)hd);
+      float sn, cs;
+      sincosf((float)e.row_pos[b] * freq, &sn, &cs);
+      store_out(a, seg, b, col0 + c1, x1 * cs - x2 * sn);
+      store_out(a, seg, b, col0 + c2, x1 * sn + x2 * cs);
+    }
+  } else {
+    for (int i = r + C * threadIdx.x; i < B * cols; i += C * blockDim.x) {
+      const int b = i / cols, c = i - b * cols;
+      if (c >= ncv) continue;
+      float v = 0.f;
+      for (int q = 0; q < C; q++) v += rt[q][b * tp + c];
+      store_out(a, seg, b, col0 + c, v);
     }
   }
-  __syncthreads();
-  return true;
+  cl.sync();  // keep this CTA's tile alive until every rank has read it
 }
 
 // ------------------------------------------------------------------ layout B
 template <int T, int NT>
 __global__ void __launch_bounds__(kThreads) k_qgemv_b(const GemvArgs a) {
   using Q = QT<T>;
-  constexpr int BP = NT * 8;        // padded batch rows
-  constexpr int XP = kRows + 8;     // halves per x row in a stage (bank-conflict pad)
+  constexpr int BP = NT * 8;  // padded batch rows
   constexpr int RAW = kRows * Q::SP;
-  constexpr int XST = BP * XP;      // halves per x stage
+  constexpr int XP = kRows + 8;               // halves per staged x row (bank-conflict pad)
+  constexpr int SST = RAW + 2 * BP * XP * 2;  // stage: weight tile + hi/lo x planes
   constexpr int CH = kGroupBlocks * Q::S / 16;  // 16-byte chunks per tile row
+  constexpr int XCH = 2 * BP * (kRows / 8);     // 16-byte chunks of x per stage
   extern __shared__ __align__(16) uint8_t smem[];
   uint8_t* raw = smem;
-  __half* xs = reinterpret_cast<__half*>(smem + kStages * RAW);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int g = lane >> 2, t = lane & 3;
   const int gx = blockIdx.x, split = blockIdx.y;
-  int seg = 0;
+  int seg = 0, lg;
+  if (a.epi.kind == EPI_SWIGLU) {  // x = 2*group + (0 gate | 1 up)
+    seg = gx & 1;
+    lg = gx >> 1;
+  } else {
 #pragma unroll
-  for (int s = 1; s < 3; s++)
-    if (s < a.nseg && gx >= a.seg[s].group_base) seg = s;
-  const GemvSeg& S = a.seg[seg];
-  const int lg = gx - S.group_base;  // group index within segment
-  const uint8_t* W = S.W + (size_t)lg * kGroupBlocks * Q::S;
+    for (int s = 1; s < 3; s++)
+      if (s < a.nseg && gx >= a.seg[s].group_base) seg = s;
+    lg = gx - a.seg[seg].group_base;
+  }
+  const int Nseg = a.seg[seg].N, pitch = a.seg[seg].pitch;
+  const uint8_t* W = a.seg[seg].W + (size_t)lg * kGroupBlocks * Q::S;
   const int k0 = split * a.kchunk;
   const int k1 = min(a.K, k0 + a.kchunk);
-  const int nstage = (k1 - k0 + kRows - 1) / kRows;
-
+  const int nstage = k1 > k0 ? (k1 - k0 + kRows - 1) / kRows : 0;
   // valid payload bytes of this group's tile row (the last group may be partial)
-  const int vbytes = min(kGroupBlocks, S.N / 32 - lg * kGroupBlocks) * Q::S;
+  const int vbytes = min(kGroupBlocks, Nseg / 32 - lg * kGroupBlocks) * Q::S;
+
+  // this thread's 16-byte chunks of a stage (fixed across stages)
+  constexpr int NWC = (kRows * CH + kThreads - 1) / kThreads;
+  constexpr int NXC = (XCH + kThreads - 1) / kThreads;
+  int wr[NWC], wc[NWC];
+#pragma unroll
+  for (int j = 0; j < NWC; j++) {
+    const int i = tid + j * kThreads;
+    wr[j] = i < kRows * CH ? i / CH : -1;
+    wc[j] = i - (i / CH) * CH;
+  }
+  const __half* xg = reinterpret_cast<const __half*>(a.x);
+  int xc[NXC], xo[NXC];
+  size_t xsrc[NXC];
+#pragma unroll
+  for (int j = 0; j < NXC; j++) {
+    const int i = tid + j * kThreads;
+    const int p = i / (BP * (kRows / 8)), rem = i - p * BP * (kRows / 8);
+    const int b = rem / (kRows / 8), c = rem - b * (kRows / 8);
+    const bool live = i < XCH && b < a.B;
+    xc[j] = live ? c * 8 : -1;
+    xo[j] = (p * BP * XP + b * XP + c * 8) * 2;
+    xsrc[j] = live ? p * a.x_plane + (size_t)b * a.ldx + c * 8 : 0;
+  }
   auto load_stage = [&](int st, int buf) {
     const int r0 = k0 + st * kRows;
-    uint8_t* dst = raw + buf * RAW;
-    for (int i = tid; i < kRows * CH; i += kThreads) {
-      int r = i / CH, c = i - r * CH;
-      int row = r0 + r;
-      bool ok = row < k1 && c * 16 < vbytes;
-      const uint8_t* src = W + (size_t)(ok ? row : k0) * S.pitch + c * 16;
-      cp_async16(dst + r * Q::SP + c * 16, src, ok ? 16 : 0);
+    uint8_t* dst = raw + buf * SST;
+#pragma unroll
+    for (int j = 0; j < NWC; j++) {
+      if (wr[j] < 0) continue;
+      const int row = r0 + wr[j];
+      const bool ok = row < k1 && wc[j] * 16 < vbytes;
+      cp_async16(dst + wr[j] * Q::SP + wc[j] * 16,
+                 W + (ok ? (size_t)row * pitch + wc[j] * 16 : 0), ok ? 16 : 0);
     }
-    __half* xd = xs + buf * XST;
-    for (int i = tid; i < BP * (kRows / 8); i += kThreads) {
-      int b = i / (kRows / 8), c = i % (kRows / 8);
-      int row = r0 + c * 8;
-      bool ok = b < a.B && row < k1;
-      const __half* src = a.x + (size_t)(ok ? b : 0) * a.ldx + (ok ? row : k0);
-      cp_async16(xd + b * XP + c * 8, src, ok ? 16 : 0);
+#pragma unroll
+    for (int j = 0; j < NXC; j++) {
+      if (tid + j * kThreads >= XCH) continue;
+      const bool ok = xc[j] >= 0 && r0 + xc[j] < k1;
+      cp_async16(dst + RAW + xo[j], xg + (ok ? xsrc[j] + r0 : 0), ok ? 16 : 0);
     }
   };
-
-  float acc[2][2][NT][4];
-#pragma unroll
-  for (int i = 0; i < 2; i++)
-#pragma unroll
-    for (int j = 0; j < 2; j++)
-#pragma unroll
-      for (int n = 0; n < NT; n++)
-#pragma unroll
-        for (int q = 0; q < 4; q++) acc[i][j][n][q] = 0.f;
 
 #pragma unroll
   for (int s = 0; s < kStages - 1; s++) {
     if (s < nstage) load_stage(s, s);
     cp_commit();
   }
+
+  float acc[2][2][NT][4];
+  float accm[2][NT][4];  // Q4_1: sum_k x*m per block (same for all rows of the block)
+#pragma unroll
+  for (int i = 0; i < 2; i++)
+#pragma unroll
+    for (int n = 0; n < NT; n++)
+#pragma unroll
+      for (int q = 0; q < 4; q++) acc[i][0][n][q] = acc[i][1][n][q] = accm[i][n][q] = 0.f;
+
   for (int st = 0; st < nstage; st++) {
     cp_wait<kStages - 2>();
     __syncthreads();
     {
-      int nx = st + kStages - 1;
+      const int nx = st + kStages - 1;
       if (nx < nstage) load_stage(nx, nx % kStages);
       cp_commit();
     }
-    const int buf = st % kStages;
-    const uint8_t* rs = raw + buf * RAW;
-    const __half* xb = xs + buf * XST;
-    const int rows_here = min(kRows, k1 - (k0 + st * kRows));
-    const int nks = rows_here >> 4;
-    for (int ks = 0; ks < nks; ks++) {
-      uint32_t bf[NT][2];
+    const uint8_t* rs = raw + (st % kStages) * SST;
+    const __half* xs = reinterpret_cast<const __half*>(rs + RAW);
+    // rows past the end of this split are zero-filled and contribute exactly 0
+#pragma unroll
+    for (int ks = 0; ks < kRows / 16; ks++) {
+      uint32_t xh[NT][2], xl[NT][2];
 #pragma unroll
       for (int n = 0; n < NT; n++) {
-        const __half* xp = xb + (n * 8 + g) * XP + ks * 16 + 2 * t;
-        bf[n][0] = *reinterpret_cast<const uint32_t*>(xp);
-        bf[n][1] = *reinterpret_cast<const uint32_t*>(xp + 8);
+        const __half* xp = xs + (n * 8 + g) * XP + ks * 16 + 2 * t;
+        xh[n][0] = *reinterpret_cast<const uint32_t*>(xp);
+        xh[n][1] = *reinterpret_cast<const uint32_t*>(xp + 8);
+        xl[n][0] = *reinterpret_cast<const uint32_t*>(xp + BP * XP);
+        xl[n][1] = *reinterpret_cast<const uint32_t*>(xp + BP * XP + 8);
       }
-      const int r0 = ks * 16 + 2 * t;
+      const uint8_t* p0b = rs + (ks * 16 + 2 * t) * Q::SP + warp * 2 * Q::S;
 #pragma unroll
       for (int blk = 0; blk < 2; blk++) {
-        const uint8_t* rb = rs + (warp * 2 + blk) * Q::S;
-        const uint8_t* p0 = rb + r0 * Q::SP;
+        const uint8_t* p0 = p0b + blk * Q::S;
         const uint8_t* p1 = p0 + Q::SP;
         const uint8_t* p2 = p0 + 8 * Q::SP;
         const uint8_t* p3 = p2 + Q::SP;
-        uint32_t d01 = ld16(p0) | (ld16(p1) << 16);
-        uint32_t d23 = ld16(p2) | (ld16(p3) << 16);
+        const uint32_t d01 = prmt(ld16(p0), ld16(p1), 0x5410);
+        const uint32_t d23 = prmt(ld16(p2), ld16(p3), 0x5410);
         uint32_t af[2][4];
+        const int o = Q::QOFF + 2 * g;
+        // byte 0 (sel 0x6420) or byte 1 (sel 0x6521) of the 16-bit payload words of
+        // rows (r0, r0+1) and (r0+8, r0+9), one per f16 lane
+        const uint32_t q0 = ld16(p0 + o), q1 = ld16(p1 + o), q2 = ld16(p2 + o), q3 = ld16(p3 + o);
+        const uint32_t x00 = prmt(q0, q1, 0x6420), x01 = prmt(q0, q1, 0x6521);
+        const uint32_t x20 = prmt(q2, q3, 0x6420), x21 = prmt(q2, q3, 0x6521);
         if constexpr (T == WL_Q8_0) {
-          const int o = Q::QOFF + 2 * g;
-          uint32_t v01 = ld16(p0 + o) | (ld16(p1 + o) << 16);
-          uint32_t v23 = ld16(p2 + o) | (ld16(p3 + o) << 16);
-          uint32_t w01 = ld16(p0 + o + 16) | (ld16(p1 + o + 16) << 16);
-          uint32_t w23 = ld16(p2 + o + 16) | (ld16(p3 + o + 16) << 16);
-          af[0][0] = q8w(v01, d01);
-          af[0][1] = q8w(v01 >> 8, d01);
-          af[0][2] = q8w(v23, d23);
-          af[0][3] = q8w(v23 >> 8, d23);
-          af[1][0] = q8w(w01, d01);
-          af[1][1] = q8w(w01 >> 8, d01);
-          af[1][2] = q8w(w23, d23);
-          af[1][3] = q8w(w23 >> 8, d23);
+          // A-row g <-> output 2g, row g+8 <-> 2g+1; m-tile 1 = outputs +16
+          const uint32_t s0 = ld16(p0 + o + 16), s1 = ld16(p1 + o + 16);
+          const uint32_t s2 = ld16(p2 + o + 16), s3 = ld16(p3 + o + 16);
+          af[0][0] = q8a(x00);
+          af[0][1] = q8a(x01);
+          af[0][2] = q8a(x20);
+          af[0][3] = q8a(x21);
+          af[1][0] = q8a(prmt(s0, s1, 0x6420));
+          af[1][1] = q8a(prmt(s0, s1, 0x6521));
+          af[1][2] = q8a(prmt(s2, s3, 0x6420));
+          af[1][3] = q8a(prmt(s2, s3, 0x6521));
         } else {
-          uint32_t m01 = 0, m23 = 0;
-          if constexpr (T == WL_Q4_1) {
-            m01 = ld16(p0 + 2) | (ld16(p1 + 2) << 16);
-            m23 = ld16(p2 + 2) | (ld16(p3 + 2) << 16);
-          }
-          const int o = Q::QOFF + 2 * g;
-          uint32_t v01 = ld16(p0 + o) | (ld16(p1 + o) << 16);
-          uint32_t v23 = ld16(p2 + o) | (ld16(p3 + o) << 16);
-          const uint32_t M = 0x000F000Fu;
-          af[0][0] = q4w<T>((v01 & M) | kMagic, d01, m01);
-          af[0][1] = q4w<T>(((v01 >> 8) & M) | kMagic, d01, m01);
-          af[0][2] = q4w<T>((v23 & M) | kMagic, d23, m23);
-          af[0][3] = q4w<T>(((v23 >> 8) & M) | kMagic, d23, m23);
-          af[1][0] = q4w<T>(((v01 >> 4) & M) | kMagic, d01, m01);
-          af[1][1] = q4w<T>(((v01 >> 12) & M) | kMagic, d01, m01);
-          af[1][2] = q4w<T>(((v23 >> 4) & M) | kMagic, d23, m23);
-          af[1][3] = q4w<T>(((v23 >> 12) & M) | kMagic, d23, m23);
+          // A-row g <-> output 2g, row g+8 <-> 2g+1 (m-tile 0: low nibbles); m-tile 1
+          // (outputs +16, high nibbles) holds 16x the codes and is rescaled at the end
+          const uint32_t ML = 0x000F000Fu, MH = 0x00F000F0u;
+          af[0][0] = q4a<T>((x00 & ML) | kMagic);
+          af[0][1] = q4a<T>((x01 & ML) | kMagic);
+          af[0][2] = q4a<T>((x20 & ML) | kMagic);
+          af[0][3] = q4a<T>((x21 & ML) | kMagic);
+          af[1][0] = q4a_hi<T>((x00 & MH) | kMagic);
+          af[1][1] = q4a_hi<T>((x01 & MH) | kMagic);
+          af[1][2] = q4a_hi<T>((x20 & MH) | kMagic);
+          af[1][3] = q4a_hi<T>((x21 & MH) | kMagic);
+        }
+        uint32_t m01 = 0, m23 = 0;
+        if constexpr (T == WL_Q4_1) {
+          m01 = prmt(ld16(p0 + 2), ld16(p1 + 2), 0x5410);
+          m23 = prmt(ld16(p2 + 2), ld16(p3 + 2), 0x5410);
         }
 #pragma unroll
         for (int n = 0; n < NT; n++) {
-          mma16816(acc[blk][0][n], af[0], bf[n][0], bf[n][1]);
-          mma16816(acc[blk][1][n], af[1], bf[n][0], bf[n][1]);
+          uint32_t bh0, bl0, bh1, bl1;
+          scale_split(d01, xh[n][0], xl[n][0], bh0, bl0);
+          scale_split(d23, xh[n][1], xl[n][1], bh1, bl1);
+          mma16816(acc[blk][0][n], af[0], bh0, bh1);
+          mma16816(acc[blk][1][n], af[1], bh0, bh1);
+          mma16816(acc[blk][0][n], af[0], bl0, bl1);
+          mma16816(acc[blk][1][n], af[1], bl0, bl1);
+          if constexpr (T == WL_Q4_1) {
+            const uint32_t ones[4] = {kOnes, kOnes, kOnes, kOnes};
+            uint32_t mh0, ml0, mh1, ml1;
+            scale_split(m01, xh[n][0], xl[n][0], mh0, ml0);
+            scale_split(m23, xh[n][1], xl[n][1], mh1, ml1);
+            mma16816(accm[blk][n], ones, mh0, mh1);
+            mma16816(accm[blk][n], ones, ml0, ml1);
+          }
         }
       }
     }
@@ -350,7 +423,7 @@ __global__ void __launch_bounds__(kThreads) k_qgemv_b(const GemvArgs a) {
   cp_wait<0>();
   __syncthreads();
 
-  // accumulators -> tile[b][c]; A-row g <-> output 2g, row g+8 <-> 2g+1, +16 for m-tile 1
+  // accumulators -> tile[b][c] (reuses the pipeline buffers)
   constexpr int TP = kColsB + 4;
   float* tile = reinterpret_cast<float*>(smem);
 #pragma unroll
@@ -361,23 +434,15 @@ __global__ void __launch_bounds__(kThreads) k_qgemv_b(const GemvArgs a) {
       for (int n = 0; n < NT; n++)
 #pragma unroll
         for (int q = 0; q < 4; q++) {
-          int b = n * 8 + 2 * t + (q & 1);
-          int c = (warp * 2 + blk) * 32 + 16 * mt + 2 * g + (q >> 1);
-          tile[b * TP + c] = acc[blk][mt][n][q];
+          const int b = n * 8 + 2 * t + (q & 1);
+          const int c = (warp * 2 + blk) * 32 + 16 * mt + 2 * g + (q >> 1);
+          // m-tile 1 of the 4-bit types accumulated 16x the codes (exact power of two)
+          const float sc = (T != WL_Q8_0 && mt == 1) ? 0.0625f : 1.0f;
+          tile[b * TP + c] = acc[blk][mt][n][q] * sc + accm[blk][n][q];
         }
   __syncthreads();
-  const int ncv = min(kColsB, S.N - lg * kColsB);
-  const bool swiglu = a.epi.kind == EPI_SWIGLU;
-  if (a.ksplit > 1 || swiglu) {
-    const int unit = swiglu ? lg : gx;
-    const int up_g0 = swiglu ? (a.seg[1].group_base + lg) * kColsB : 0;
-    if (!splitk_finish<kColsB>(a, split, gx * kColsB, unit, ncv, tile, TP, swiglu, up_g0)) return;
-    if (swiglu) {
-      apply_epilogue(a, 0, lg * kColsB, ncv, tile, TP);
-      return;
-    }
-  }
-  apply_epilogue(a, seg, lg * kColsB, ncv, tile, TP);
+  const int ncv = min(kColsB, Nseg - lg * kColsB);
+  cluster_finish(a, tile, TP, kColsB, ncv, seg, lg * kColsB);
 }
 
 // ------------------------------------------------------------------ layout A
@@ -386,13 +451,16 @@ __global__ void __launch_bounds__(kThreads) k_qgemv_a(const GemvArgs a) {
   using Q = QT<T>;
   constexpr int BP = NT * 8;
   constexpr int KS = kGroupBlocks * 32;  // k values per stage (256)
-  constexpr int XP = KS + 8;
   constexpr int RAW = kColsA * Q::SP;
-  constexpr int XST = BP * XP;
   constexpr int CH = kGroupBlocks * Q::S / 16;
+  constexpr int STG = NT <= 2 ? kStages : 2;  // pipeline depth (large batch tiles use 2)
+  constexpr int SST = RAW + BP * KS * 4;      // weight tile + f32 activation tile per stage
+  constexpr int XP = KS + 8;
+  constexpr int PIPE = STG * SST > BP * (kColsA + 4) * 4 ? STG * SST : BP * (kColsA + 4) * 4;
   extern __shared__ __align__(16) uint8_t smem[];
   uint8_t* raw = smem;
-  __half* xs = reinterpret_cast<__half*>(smem + kStages * RAW);
+  __half* xs = reinterpret_cast<__half*>(smem + PIPE);
+  const __half* xl_base = xs + BP * XP;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int g = lane >> 2, t = lane & 3;
@@ -401,27 +469,26 @@ __global__ void __launch_bounds__(kThreads) k_qgemv_a(const GemvArgs a) {
   const int n0 = gx * kColsA;
   const int k0 = split * a.kchunk;
   const int k1 = min(a.K, k0 + a.kchunk);
-  const int nstage = (k1 - k0) / KS;
+  const int nstage = k1 > k0 ? (k1 - k0) / KS : 0;
 
   auto load_stage = [&](int st, int buf) {
-    const int kk = k0 + st * KS;
-    const size_t byte0 = (size_t)(kk / 32) * Q::S;
-    uint8_t* dst = raw + buf * RAW;
+    const size_t byte0 = (size_t)((k0 + st * KS) / 32) * Q::S;
+    uint8_t* dst = raw + buf * SST;
     for (int i = tid; i < kColsA * CH; i += kThreads) {
-      int r = i / CH, c = i - r * CH;
-      int row = n0 + r;
-      bool ok = row < S.N;
-      const uint8_t* src = S.W + (size_t)(ok ? row : 0) * S.pitch + byte0 + c * 16;
-      cp_async16(dst + r * Q::SP + c * 16, src, ok ? 16 : 0);
+      const int r = i / CH, c = i - r * CH;
+      const int row = n0 + r;
+      const bool ok = row < S.N;
+      cp_async16(dst + r * Q::SP + c * 16, S.W + (size_t)(ok ? row : 0) * S.pitch + byte0 + c * 16,
+                 ok ? 16 : 0);
     }
-    __half* xd = xs + buf * XST;
-    for (int i = tid; i < BP * (KS / 8); i += kThreads) {
-      int b = i / (KS / 8), c = i % (KS / 8);
-      bool ok = b < a.B;
-      const __half* src = a.x + (size_t)(ok ? b : 0) * a.ldx + kk + c * 8;
-      cp_async16(xd + b * XP + c * 8, src, ok ? 16 : 0);
-    }
+    load_x_f32(a, reinterpret_cast<float*>(dst + RAW), BP, KS, k0 + st * KS, k1);
   };
+
+#pragma unroll
+  for (int s = 0; s < STG - 1; s++) {
+    if (s < nstage) load_stage(s, s);
+    cp_commit();
+  }
 
   float acc[NT][4];
 #pragma unroll
@@ -429,72 +496,86 @@ __global__ void __launch_bounds__(kThreads) k_qgemv_a(const GemvArgs a) {
 #pragma unroll
     for (int q = 0; q < 4; q++) acc[n][q] = 0.f;
 
-#pragma unroll
-  for (int s = 0; s < kStages - 1; s++) {
-    if (s < nstage) load_stage(s, s);
-    cp_commit();
-  }
   for (int st = 0; st < nstage; st++) {
-    cp_wait<kStages - 2>();
+    cp_wait<STG - 2>();
     __syncthreads();
     {
-      int nx = st + kStages - 1;
-      if (nx < nstage) load_stage(nx, nx % kStages);
+      const int nx = st + STG - 1;
+      if (nx < nstage) load_stage(nx, nx % STG);
       cp_commit();
     }
-    const int buf = st % kStages;
-    const uint8_t* rA0 = raw + buf * RAW + (warp * 16 + g) * Q::SP;
+    split_tile(reinterpret_cast<const float*>(raw + (st % STG) * SST + RAW), xs, BP, KS, XP);
+    __syncthreads();
+    const uint8_t* rA0 = raw + (st % STG) * SST + (warp * 16 + g) * Q::SP;
     const uint8_t* rB0 = rA0 + 8 * Q::SP;
-    const __half* xb = xs + buf * XST;
 #pragma unroll 2
     for (int bi = 0; bi < kGroupBlocks; bi++) {
       const uint8_t* rA = rA0 + bi * Q::S;
       const uint8_t* rB = rB0 + bi * Q::S;
-      uint32_t dA = ld16(rA), dB = ld16(rB);
-      dA |= dA << 16;
-      dB |= dB << 16;
+      const float dA = __half2float(__ushort_as_half((unsigned short)ld16(rA)));
+      const float dB = __half2float(__ushort_as_half((unsigned short)ld16(rB)));
       uint32_t af[2][4];
       if constexpr (T == WL_Q8_0) {
-        // byte j of the payload is k = j; k-step 0 covers k 0..15, k-step 1 k 16..31
+        // payload byte j is k = j: k-step 0 covers k 0..15, k-step 1 k 16..31
 #pragma unroll
         for (int s = 0; s < 2; s++) {
           const int o = Q::QOFF + 16 * s + 2 * t;
-          af[s][0] = q8w(__byte_perm(ld16(rA + o), 0, 0x4140), dA);
-          af[s][1] = q8w(__byte_perm(ld16(rB + o), 0, 0x4140), dB);
-          af[s][2] = q8w(__byte_perm(ld16(rA + o + 8), 0, 0x4140), dA);
-          af[s][3] = q8w(__byte_perm(ld16(rB + o + 8), 0, 0x4140), dB);
+          af[s][0] = q8a(__byte_perm(ld16(rA + o), 0, 0x4140));
+          af[s][1] = q8a(__byte_perm(ld16(rB + o), 0, 0x4140));
+          af[s][2] = q8a(__byte_perm(ld16(rA + o + 8), 0, 0x4140));
+          af[s][3] = q8a(__byte_perm(ld16(rB + o + 8), 0, 0x4140));
         }
       } else {
-        uint32_t mA = 0, mB = 0;
-        if constexpr (T == WL_Q4_1) {
-          mA = ld16(rA + 2), mB = ld16(rB + 2);
-          mA |= mA << 16;
-          mB |= mB << 16;
-        }
         const int o = Q::QOFF + 2 * t;
         // low nibble of byte j is k = j, high nibble is k = j + 16
-        uint32_t xA0 = __byte_perm(ld16(rA + o), 0, 0x4140);
-        uint32_t xA1 = __byte_perm(ld16(rA + o + 8), 0, 0x4140);
-        uint32_t xB0 = __byte_perm(ld16(rB + o), 0, 0x4140);
-        uint32_t xB1 = __byte_perm(ld16(rB + o + 8), 0, 0x4140);
+        const uint32_t xA0 = __byte_perm(ld16(rA + o), 0, 0x4140);
+        const uint32_t xA1 = __byte_perm(ld16(rA + o + 8), 0, 0x4140);
+        const uint32_t xB0 = __byte_perm(ld16(rB + o), 0, 0x4140);
+        const uint32_t xB1 = __byte_perm(ld16(rB + o + 8), 0, 0x4140);
         const uint32_t M = 0x000F000Fu;
-        af[0][0] = q4w<T>((xA0 & M) | kMagic, dA, mA);
-        af[0][1] = q4w<T>((xB0 & M) | kMagic, dB, mB);
-        af[0][2] = q4w<T>((xA1 & M) | kMagic, dA, mA);
-        af[0][3] = q4w<T>((xB1 & M) | kMagic, dB, mB);
-        af[1][0] = q4w<T>(((xA0 >> 4) & M) | kMagic, dA, mA);
-        af[1][1] = q4w<T>(((xB0 >> 4) & M) | kMagic, dB, mB);
-        af[1][2] = q4w<T>(((xA1 >> 4) & M) | kMagic, dA, mA);
-        af[1][3] = q4w<T>(((xB1 >> 4) & M) | kMagic, dB, mB);
+        af[0][0] = q4a<T>((xA0 & M) | kMagic);
+        af[0][1] = q4a<T>((xB0 & M) | kMagic);
+        af[0][2] = q4a<T>((xA1 & M) | kMagic);
+        af[0][3] = q4a<T>((xB1 & M) | kMagic);
+        af[1][0] = q4a<T>(((xA0 >> 4) & M) | kMagic);
+        af[1][1] = q4a<T>(((xB0 >> 4) & M) | kMagic);
+        af[1][2] = q4a<T>(((xA1 >> 4) & M) | kMagic);
+        af[1][3] = q4a<T>(((xB1 >> 4) & M) | kMagic);
       }
+      const uint32_t ones[4] = {kOnes, kOnes, kOnes, kOnes};
 #pragma unroll
-      for (int s = 0; s < 2; s++)
+      for (int n = 0; n < NT; n++) {
+        float c[4] = {0.f, 0.f, 0.f, 0.f}, cm[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-        for (int n = 0; n < NT; n++) {
-          const __half* xp = xb + (n * 8 + g) * XP + bi * 32 + s * 16 + 2 * t;
-          mma16816(acc[n], af[s], *reinterpret_cast<const uint32_t*>(xp),
-                   *reinterpret_cast<const uint32_t*>(xp + 8));
+        for (int s = 0; s < 2; s++) {
+          const int kk = bi * 32 + s * 16 + 2 * t;
+          const __half* xp = xs + (n * 8 + g) * XP + kk;
+          const __half* lp = xl_base + (n * 8 + g) * XP + kk;
+          const uint32_t h0 = *reinterpret_cast<const uint32_t*>(xp);
+          const uint32_t h1 = *reinterpret_cast<const uint32_t*>(xp + 8);
+          const uint32_t l0 = *reinterpret_cast<const uint32_t*>(lp);
+          const uint32_t l1 = *reinterpret_cast<const uint32_t*>(lp + 8);
+          mma16816(c, af[s], h0, h1);
+          mma16816(c, af[s], l0, l1);
+          if constexpr (T == WL_Q4_1) {
+            mma16816(cm, ones, h0, h1);
+            mma16816(cm, ones, l0, l1);
+          }
         }
+        // block scale per A row: c0,c1 belong to row g, c2,c3 to row g+8
+        acc[n][0] += dA * c[0];
+        acc[n][1] += dA * c[1];
+        acc[n][2] += dB * c[2];
+        acc[n][3] += dB * c[3];
+        if constexpr (T == WL_Q4_1) {
+          const float mA = __half2float(__ushort_as_half((unsigned short)ld16(rA + 2)));
+          const float mB = __half2float(__ushort_as_half((unsigned short)ld16(rB + 2)));
+          acc[n][0] += mA * cm[0];
+          acc[n][1] += mA * cm[1];
+          acc[n][2] += mB * cm[2];
+          acc[n][3] += mB * cm[3];
+        }
+      }
     }
   }
   cp_wait<0>();
@@ -505,39 +586,38 @@ __global__ void __launch_bounds__(kThreads) k_qgemv_a(const GemvArgs a) {
   for (int n = 0; n < NT; n++)
 #pragma unroll
     for (int q = 0; q < 4; q++) {
-      int b = n * 8 + 2 * t + (q & 1);
-      int c = warp * 16 + g + 8 * (q >> 1);
+      const int b = n * 8 + 2 * t + (q & 1);
+      const int c = warp * 16 + g + 8 * (q >> 1);
       tile[b * TP + c] = acc[n][q];
     }
   __syncthreads();
-  const int ncv = min(kColsA, S.N - n0);
-  if (a.ksplit > 1) {
-    if (!splitk_finish<kColsA>(a, split, n0, gx, ncv, tile, TP, false, 0)) return;
-  }
-  apply_epilogue(a, 0, n0, ncv, tile, TP);
+  cluster_finish(a, tile, TP, kColsA, min(kColsA, S.N - n0), 0, n0);
 }
 
 // ------------------------------------------------------------------ generic fallback
 __device__ __forceinline__ float deq1(int type, const uint8_t* blk, int j) {
-  float d = __half2float(__ushort_as_half(*reinterpret_cast<const uint16_t*>(blk)));
+  const float d = __half2float(__ushort_as_half(*reinterpret_cast<const uint16_t*>(blk)));
   if (type == WL_Q4_0) {
-    int q = j < 16 ? (blk[2 + j] & 15) - 8 : (blk[2 + j - 16] >> 4) - 8;
+    const int q = j < 16 ? (blk[2 + j] & 15) - 8 : (blk[2 + j - 16] >> 4) - 8;
     return (float)q * d;
   }
   if (type == WL_Q4_1) {
-    float m = __half2float(__ushort_as_half(*reinterpret_cast<const uint16_t*>(blk + 2)));
-    int q = j < 16 ? (blk[4 + j] & 15) : (blk[4 + j - 16] >> 4);
+    const float m = __half2float(__ushort_as_half(*reinterpret_cast<const uint16_t*>(blk + 2)));
+    const int q = j < 16 ? (blk[4 + j] & 15) : (blk[4 + j - 16] >> 4);
     return __fadd_rn(__fmul_rn((float)q, d), m);
   }
   return (float)(int8_t)blk[2 + j] * d;
 }
 
 __global__ void k_qgemv_generic(int type, int layout, const uint8_t* W, int K, int N, int pitch,
-                                const __half* x, int ldx, int B, float* y, int ldy, int add) {
-  int o = blockIdx.x * blockDim.x + threadIdx.x;
-  int b = blockIdx.y;
+                                const void* xv, size_t x_plane, int ldx, int B, float* y, int ldy,
+                                int add) {
+  const int o = blockIdx.x * blockDim.x + threadIdx.x;
+  const int b = blockIdx.y;
   if (o >= N || b >= B) return;
   const int S = type == WL_Q4_0 ? 18 : type == WL_Q4_1 ? 20 : 34;
+  const float* xf = reinterpret_cast<const float*>(xv);
+  const __half* xh = reinterpret_cast<const __half*>(xv);
   float acc = 0.f;
   for (int k = 0; k < K; k++) {
     float w;
@@ -547,7 +627,9 @@ __global__ void k_qgemv_generic(int type, int layout, const uint8_t* W, int K, i
     else
       w = layout == WL_LAYOUT_B ? deq1(type, W + (size_t)k * pitch + (o / 32) * S, o % 32)
                                 : deq1(type, W + (size_t)o * pitch + (k / 32) * S, k % 32);
-    acc += __half2float(x[(size_t)b * ldx + k]) * w;
+    const size_t xi = (size_t)b * ldx + k;
+    const float xk = x_plane ? __half2float(xh[xi]) + __half2float(xh[xi + x_plane]) : xf[xi];
+    acc += xk * w;
   }
   if (add)
     y[(size_t)b * ldy + o] += acc;
@@ -555,78 +637,83 @@ __global__ void k_qgemv_generic(int type, int layout, const uint8_t* W, int K, i
     y[(size_t)b * ldy + o] = acc;
 }
 
-__global__ void k_f32_to_f16(const float* x, __half* y, size_t n) {
-  size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
-  if (i < n) y[i] = __float2half_rn(x[i]);
+__global__ void k_split_planes(const float* x, __half* y, size_t n, size_t plane) {
+  const size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const float v = x[i];
+  const __half hi = __float2half_rn(v);
+  y[i] = hi;
+  y[i + plane] = __float2half_rn(v - __half2float(hi));
 }
 
+// ------------------------------------------------------------------ launch
 template <int T>
-constexpr int raw_bytes_b() {
-  return kStages * kRows * QT<T>::SP;
+size_t smem_b(int NT) {
+  const size_t BP = (size_t)NT * 8;
+  const size_t pipe = (size_t)kStages * (kRows * QT<T>::SP + 2 * BP * (kRows + 8) * 2);
+  const size_t tile = BP * (kColsB + 4) * 4;
+  return std::max(pipe, tile);
+}
+template <int T>
+size_t smem_a(int NT) {
+  const size_t BP = (size_t)NT * 8;
+  const int stg = NT <= 2 ? kStages : 2;
+  const size_t pipe = (size_t)stg * (kColsA * QT<T>::SP + BP * 256 * 4);
+  const size_t tile = BP * (kColsA + 4) * 4;
+  const size_t xs = 2 * BP * (256 + 8) * 2;
+  return std::max(pipe, tile) + xs;
+}
+
+template <class Kern>
+int launch_cluster(Kern kern, dim3 grid, size_t smem, int cx, int cy, const GemvArgs& a,
+                   cudaStream_t st, unsigned& attr_done) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!(attr_done >> (dev & 31) & 1u)) {
+    WL_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+    WL_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
+    attr_done |= 1u << (dev & 31);
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeClusterDimension;
+  at[0].val.clusterDim.x = cx;
+  at[0].val.clusterDim.y = cy;
+  at[0].val.clusterDim.z = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  WL_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, a));
+  return WL_OK;
 }
 
 template <int T, int NT>
 int launch_b_t(const GemvArgs& a, cudaStream_t st) {
-  constexpr int BP = NT * 8;
-  size_t pipe = (size_t)kStages * kRows * QT<T>::SP + (size_t)kStages * BP * (kRows + 8) * 2;
-  size_t epi = (size_t)BP * (kColsB + 4) * 4;
-  size_t smem = std::max(pipe, epi);
-  static unsigned attr_done = 0;  // one bit per device, per instantiation
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (!(attr_done >> (dev & 31) & 1u)) {
-    WL_CUDA_TRY(cudaFuncSetAttribute(k_qgemv_b<T, NT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     (int)smem));
-    attr_done |= 1u << (dev & 31);
-  }
+  static unsigned attr_done = 0;
   int groups = 0;
   for (int s = 0; s < a.nseg; s++) groups += a.seg[s].groups;
-  dim3 grid(groups, a.ksplit);
-  k_qgemv_b<T, NT><<<grid, kThreads, smem, st>>>(a);
-  WL_CUDA_TRY(cudaGetLastError());
-  return WL_OK;
+  const bool sw = a.epi.kind == EPI_SWIGLU;
+  return launch_cluster(k_qgemv_b<T, NT>, dim3(groups, a.csplit), smem_b<T>(NT), sw ? 2 : 1,
+                        a.csplit, a, st, attr_done);
 }
 
 template <int T, int NT>
 int launch_a_t(const GemvArgs& a, cudaStream_t st) {
-  constexpr int BP = NT * 8;
-  size_t pipe = (size_t)kStages * kColsA * QT<T>::SP + (size_t)kStages * BP * (256 + 8) * 2;
-  size_t epi = (size_t)BP * (kColsA + 4) * 4;
-  size_t smem = std::max(pipe, epi);
   static unsigned attr_done = 0;
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (!(attr_done >> (dev & 31) & 1u)) {
-    WL_CUDA_TRY(cudaFuncSetAttribute(k_qgemv_a<T, NT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     (int)smem));
-    attr_done |= 1u << (dev & 31);
-  }
-  dim3 grid(a.seg[0].groups, a.ksplit);
-  k_qgemv_a<T, NT><<<grid, kThreads, smem, st>>>(a);
-  WL_CUDA_TRY(cudaGetLastError());
-  return WL_OK;
+  return launch_cluster(k_qgemv_a<T, NT>, dim3(a.seg[0].groups, a.csplit), smem_a<T>(NT), 1,
+                        a.csplit, a, st, attr_done);
 }
 
-template <int T>
-int dispatch_b(const GemvArgs& a, cudaStream_t st) {
-  int nt = (a.B + 7) / 8;
-  switch (nt) {
-    case 1: return launch_b_t<T, 1>(a, st);
-    case 2: return launch_b_t<T, 2>(a, st);
-    case 3: return launch_b_t<T, 3>(a, st);
-    case 4: return launch_b_t<T, 4>(a, st);
-  }
-  return fail(WL_ERR_INVALID_ARGUMENT, "qgemv: B must be 1..32 per launch");
-}
-
-template <int T>
-int dispatch_a(const GemvArgs& a, cudaStream_t st) {
-  int nt = (a.B + 7) / 8;
-  switch (nt) {
-    case 1: return launch_a_t<T, 1>(a, st);
-    case 2: return launch_a_t<T, 2>(a, st);
-    case 3: return launch_a_t<T, 3>(a, st);
-    case 4: return launch_a_t<T, 4>(a, st);
+template <int T, bool LB>
+int dispatch(const GemvArgs& a, cudaStream_t st) {
+  switch ((a.B + 7) / 8) {
+    case 1: return LB ? launch_b_t<T, 1>(a, st) : launch_a_t<T, 1>(a, st);
+    case 2: return LB ? launch_b_t<T, 2>(a, st) : launch_a_t<T, 2>(a, st);
+    case 3: return LB ? launch_b_t<T, 3>(a, st) : launch_a_t<T, 3>(a, st);
+    case 4: return LB ? launch_b_t<T, 4>(a, st) : launch_a_t<T, 4>(a, st);
   }
   return fail(WL_ERR_INVALID_ARGUMENT, "qgemv: B must be 1..32 per launch");
 }
@@ -639,71 +726,67 @@ int qgemv_group_cols(int layout) { return layout == WL_LAYOUT_B ? kColsB : kCols
 
 // Layout B needs 16-byte aligned rows (pitch % 16 == 0, padding allowed) and
 // 16 readable bytes past the last row's payload (the tail chunk of a partial
-// group may straddle the end of the payload).
+// group may straddle the end of the payload); K a multiple of 16.
 bool qgemv_b_fast_ok(int type, int K, int N, int pitch, const void* W) {
-  int S = block_bytes(type);
+  const int S = block_bytes(type);
   if (!S) return false;
   return K % 16 == 0 && K > 0 && N % 32 == 0 && pitch % 16 == 0 && pitch >= N / 32 * S &&
          (reinterpret_cast<uintptr_t>(W) & 15) == 0;
 }
 
 bool qgemv_a_fast_ok(int type, int K, int N, int pitch, const void* W) {
-  int S = block_bytes(type);
+  const int S = block_bytes(type);
   if (!S) return false;
   (void)N;
   return K % 256 == 0 && pitch % 16 == 0 && pitch == K / 32 * S &&
          (reinterpret_cast<uintptr_t>(W) & 15) == 0;
 }
 
-void qgemv_plan(const GemvArgs& a, int layout, int num_sms, int* ksplit, int* kchunk) {
+void qgemv_plan(GemvArgs& a, int layout, int num_sms) {
   int groups = 0;
   for (int s = 0; s < a.nseg; s++) groups += a.seg[s].groups;
   const int gran = layout == WL_LAYOUT_B ? 16 : 256;
-  const int units = a.K / gran;
+  const int units = (a.K + gran - 1) / gran;
   const int target = 2 * num_sms;
-  int ks = (target + groups - 1) / std::max(groups, 1);
-  ks = std::max(1, std::min(ks, units));
-  int chunk = (units + ks - 1) / ks * gran;
-  ks = (a.K + chunk - 1) / chunk;
-  *ksplit = ks;
-  *kchunk = chunk;
-}
-
-size_t qgemv_ws_floats(int ksplit, int B, int total_cols) {
-  return (size_t)ksplit * B * total_cols;
+  const int cmax = a.epi.kind == EPI_SWIGLU ? kMaxCluster / 2 : kMaxCluster;
+  int c = (target + groups - 1) / std::max(groups, 1);
+  c = std::max(1, std::min({c, cmax, units}));
+  a.kchunk = (units + c - 1) / c * gran;
+  a.csplit = (a.K + a.kchunk - 1) / a.kchunk;
 }
 
 int launch_qgemv_b(const GemvArgs& a, cudaStream_t st) {
   switch (a.type) {
-    case WL_Q4_0: return dispatch_b<WL_Q4_0>(a, st);
-    case WL_Q4_1: return dispatch_b<WL_Q4_1>(a, st);
-    case WL_Q8_0: return dispatch_b<WL_Q8_0>(a, st);
+    case WL_Q4_0: return dispatch<WL_Q4_0, true>(a, st);
+    case WL_Q4_1: return dispatch<WL_Q4_1, true>(a, st);
+    case WL_Q8_0: return dispatch<WL_Q8_0, true>(a, st);
   }
   return fail(WL_ERR_UNSUPPORTED, "qgemv: unsupported type " + std::to_string(a.type));
 }
 
 int launch_qgemv_a(const GemvArgs& a, cudaStream_t st) {
   switch (a.type) {
-    case WL_Q4_0: return dispatch_a<WL_Q4_0>(a, st);
-    case WL_Q4_1: return dispatch_a<WL_Q4_1>(a, st);
-    case WL_Q8_0: return dispatch_a<WL_Q8_0>(a, st);
+    case WL_Q4_0: return dispatch<WL_Q4_0, false>(a, st);
+    case WL_Q4_1: return dispatch<WL_Q4_1, false>(a, st);
+    case WL_Q8_0: return dispatch<WL_Q8_0, false>(a, st);
   }
   return fail(WL_ERR_UNSUPPORTED, "qgemv: unsupported type " + std::to_string(a.type));
 }
 
 int launch_qgemv_generic(int type, int layout, const uint8_t* W, int K, int N, int pitch,
-                         const __half* x, int ldx, int B, float* y, int ldy, bool add,
-                         cudaStream_t st) {
+                         const void* x, size_t x_plane, int ldx, int B, float* y, int ldy,
+                         bool add, cudaStream_t st) {
   if (!block_bytes(type) && type != WL_F32) return fail(WL_ERR_UNSUPPORTED, "qgemv: unsupported type");
   dim3 grid((N + 127) / 128, B);
-  k_qgemv_generic<<<grid, 128, 0, st>>>(type, layout, W, K, N, pitch, x, ldx, B, y, ldy, add);
+  k_qgemv_generic<<<grid, 128, 0, st>>>(type, layout, W, K, N, pitch, x, x_plane, ldx, B, y, ldy,
+                                        add);
   WL_CUDA_TRY(cudaGetLastError());
   return WL_OK;
 }
 
-int launch_f32_to_f16(const float* x, __half* y, size_t n, cudaStream_t st) {
+int launch_split_planes(const float* x, __half* y, size_t n, size_t plane, cudaStream_t st) {
   if (!n) return WL_OK;
-  k_f32_to_f16<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(x, y, n);
+  k_split_planes<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(x, y, n, plane);
   WL_CUDA_TRY(cudaGetLastError());
   return WL_OK;
 }

@@ -7,29 +7,47 @@
 
 namespace wl {
 
-// Epilogue kinds for the layout-B GEMV (applied once the full K sum is known).
+// Epilogue kinds (applied once the full K sum of an output is known).
 enum EpiKind : int {
-  EPI_F32 = 0,     // y[b][col] = v                      (f32)
-  EPI_ADD = 1,     // y[b][col] += v                     (residual, f32)
-  EPI_F16 = 2,     // y[b][col] = half(v)
-  EPI_QKV = 3,     // seg0 -> q f32 (+rope), seg1 -> K pages f16 (+rope), seg2 -> V pages
-  EPI_SWIGLU = 4,  // seg0 = gate, seg1 = up: y[b][col] = half(silu(g) * u)
+  EPI_F32 = 0,     // segment s: y[s][b*ldy + col] = v
+  EPI_ADD = 1,     // segment s: y[s][b*ldy + col] += v (residual)
+  EPI_QKV = 2,     // seg0 -> q f32 (+rope), seg1 -> K pages f16 (+rope), seg2 -> V pages f16
+  EPI_SWIGLU = 3,  // seg0 = gate, seg1 = up (paired in one cluster): y[0] gets silu(g)*u as
+                   // f16 hi/lo planes (lo plane at y[0] + y_plane)
 };
 
-// Paged KV cache addressing for one layer.
-struct KvPages {
-  __half* k;              // [n_pages][page][kvd]
-  __half* v;
-  const int* page_table;  // [n_sessions_max][max_pages]
-  int max_pages;          // row stride of page_table
-  int page;               // tokens per page
-  int kvd;
+// Activation operand of the layout-B GEMV: f16 hi/lo planes, x = hi + lo with
+// lo = f16(x - hi) (~22 significant bits).  Element (b, k) of the hi plane is
+// x[b*ldx + k]; the lo plane starts x_plane elements later.  Layout A (the
+// op-level matvec) takes plain f32 activations instead.
+enum XKind : int {
+  X_PLANES = 0,
+  X_F32 = 1,
 };
+
+// Paged KV cache addressing for one layer: element (token j, kv head h, dim d)
+// of a session lives at page = table[sess][j / page], slot = j % page, in
+//   base[((page * kv_heads + h) * page_tokens + slot) * head_dim + d]
+// so one (page, head) is a contiguous page_tokens x head_dim f16 chunk.
+struct KvPages {
+  __half* k = nullptr;
+  __half* v = nullptr;
+  const int* page_table = nullptr;  // [n_sessions_max][max_pages]
+  int max_pages = 0;                // row stride of page_table
+  int page = 16;                    // tokens per page
+  int kv_heads = 0;
+  int head_dim = 0;
+};
+
+__host__ __device__ inline size_t kv_offset(const KvPages& kv, int pg, int slot, int head, int d) {
+  return (((size_t)pg * kv.kv_heads + head) * kv.page + slot) * kv.head_dim + d;
+}
 
 struct Epilogue {
   int kind = EPI_F32;
-  void* y = nullptr;  // output base (kind-dependent)
-  int ldy = 0;        // row stride of y (elements)
+  void* y[3] = {nullptr, nullptr, nullptr};  // per-segment outputs
+  int ldy[3] = {0, 0, 0};
+  size_t y_plane = 0;  // EPI_SWIGLU: offset of the lo plane (elements)
   // QKV / rope
   int rope = 0;
   int head_dim = 0;
@@ -41,9 +59,9 @@ struct Epilogue {
 
 struct GemvSeg {
   const uint8_t* W = nullptr;
-  int N = 0;         // columns (layout B) or rows (layout A)
-  int pitch = 0;     // bytes per matrix row
-  int groups = 0;    // column groups (tiles) in this segment
+  int N = 0;          // columns (layout B) or rows (layout A)
+  int pitch = 0;      // bytes per matrix row
+  int groups = 0;     // column groups (tiles) in this segment
   int group_base = 0;
 };
 
@@ -51,32 +69,31 @@ struct GemvArgs {
   int type = 2;  // WL_Q4_0 / WL_Q4_1 / WL_Q8_0
   int nseg = 1;
   GemvSeg seg[3];
-  int K = 0;            // reduction length
-  int B = 0;            // rows of x (<= 32 per launch)
-  const __half* x = nullptr;
+  int K = 0;     // reduction length
+  int B = 0;     // rows of x (<= 32 per launch)
+  int xkind = X_PLANES;
+  const void* x = nullptr;  // __half planes (X_PLANES) or float (X_F32)
+  size_t x_plane = 0;
   int ldx = 0;
-  int ksplit = 1;
-  int kchunk = 0;       // rows of K per split (multiple of 16)
-  float* ws = nullptr;  // [ksplit][B][total_cols] partial sums
-  unsigned* counters = nullptr;
-  int total_cols = 0;
+  int csplit = 1;  // CTAs per cluster splitting K (1..16)
+  int kchunk = 0;  // rows of K per CTA (multiple of 16; of 256 for layout A)
   Epilogue epi;
 };
 
 // Host launchers (stream-ordered).  Return a wl_status.
 int launch_qgemv_b(const GemvArgs& a, cudaStream_t st);
 int launch_qgemv_a(const GemvArgs& a, cudaStream_t st);
-// generic (any alignment) fallback, f32 math, plain loads; EPI_F32/EPI_ADD only
+// generic (any alignment / F32 weights) fallback, f32 math; EPI_F32/EPI_ADD;
+// x is f32 (x_plane == 0) or hi/lo f16 planes (x_plane = lo-plane offset)
 int launch_qgemv_generic(int type, int layout, const uint8_t* W, int K, int N, int pitch,
-                         const __half* x, int ldx, int B, float* y, int ldy, bool add,
-                         cudaStream_t st);
+                         const void* x, size_t x_plane, int ldx, int B, float* y, int ldy,
+                         bool add, cudaStream_t st);
+// f32 -> hi/lo f16 planes (lo plane `plane` elements after hi)
+int launch_split_planes(const float* x, __half* y, size_t n, size_t plane, cudaStream_t st);
 bool qgemv_b_fast_ok(int type, int K, int N, int pitch, const void* W);
 bool qgemv_a_fast_ok(int type, int K, int N, int pitch, const void* W);
-// scratch needs: floats of partial sums and counters for a launch
-void qgemv_plan(const GemvArgs& a, int layout, int num_sms, int* ksplit, int* kchunk);
-size_t qgemv_ws_floats(int ksplit, int B, int total_cols);
+// picks csplit / kchunk for a launch (fills the GPU)
+void qgemv_plan(GemvArgs& a, int layout, int num_sms);
 int qgemv_group_cols(int layout);
-
-int launch_f32_to_f16(const float* x, __half* y, size_t n, cudaStream_t st);
 
 }  // namespace wl
