@@ -153,6 +153,14 @@ int wl_dequantize(int ggml_type, const void* blocks, size_t nbytes, size_t n, fl
 int wl_qgemv(int ggml_type, int layout, const void* W, int K, int N, const float* x, int B,
              float* y, void* stream);
 
+/* Layout-B GEMV on activations already split into f16 hi/lo planes
+ * (x = hi + lo, lo = f16(x - hi); hi plane [B][K], lo plane x_plane elements
+ * later) — the operand format the model runtime uses between kernels.  Same
+ * math as wl_qgemv layout B (tensor_utils.rs:118-157); requires N % 32 == 0,
+ * K % 16 == 0 and 16-byte aligned rows (N/32 * block bytes % 16 == 0). */
+int wl_qgemv_planes(int ggml_type, const void* W, int K, int N, const void* x_planes,
+                    size_t x_plane, int B, float* y, void* stream);
+
 /* woolly_tensor quantization::simd::quantized_matvec(weights, input, output, m, k)
  * (quantization.rs:869): layout A, one input vector; Q4_0 and Q8_0 (Q4_1 ->
  * WL_ERR_UNSUPPORTED, as the reference). */

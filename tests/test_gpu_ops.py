@@ -132,6 +132,16 @@ def test_qgemv_sweep_shapes(qt, K, N):
             check_gemv(y.cpu().numpy(), ref)
 
 
+@pytest.mark.parametrize("qt", [Q4_0, Q4_1, Q8_0])
+def test_qgemv_planes_matches_f32_entry(qt):
+    K, N, B = 1024, 768, 20
+    raw = quant_matrix(qt, K, N, seed=77)
+    x = dev(np.random.default_rng(5).standard_normal((B, K)).astype(np.float32))
+    ref = ops.qgemv(dev(raw), qt, LAYOUT_B, x, N)
+    got = ops.qgemv_planes(dev(raw), qt, ops.split_planes(x), N)
+    assert torch.equal(ref, got)
+
+
 def test_matmul_2x2_kat_layout_b():
     """tensor_utils.rs:608-620 ([1,2;3,4] @ [5,6;7,8] = [19,22;43,50]) through the
     layout-B GEMV with Q8_0 blocks of scale 1: the K=2 case takes the generic

@@ -254,6 +254,36 @@ int wl_qgemv(int type, int layout, const void* W, int K, int N, const float* x, 
   return qgemv_op(type, layout, (const uint8_t*)W, K, N, x, B, y, (cudaStream_t)stream);
 }
 
+int wl_qgemv_planes(int type, const void* W, int K, int N, const void* xp, size_t x_plane, int B,
+                    float* y, void* stream) {
+  if (!W || !xp || !y || B <= 0) return fail(WL_ERR_INVALID_ARGUMENT, "bad argument");
+  if (!bb(type)) return fail(WL_ERR_UNSUPPORTED, "qgemv: type must be Q4_0, Q4_1 or Q8_0");
+  const int pitch = N / 32 * bb(type);
+  if (N % 32 || !qgemv_b_fast_ok(type, K, N, pitch, W))
+    return fail(WL_ERR_INVALID_ARGUMENT, "qgemv_planes: needs N % 32 == 0, K % 16 == 0, 16-byte rows");
+  GemvArgs a;
+  a.type = type;
+  a.nseg = 1;
+  a.seg[0].W = (const uint8_t*)W;
+  a.seg[0].N = N;
+  a.seg[0].pitch = pitch;
+  a.seg[0].groups = (N + 255) / 256;
+  a.K = K;
+  a.ldx = K;
+  a.xkind = X_PLANES;
+  a.x_plane = x_plane;
+  a.epi.kind = EPI_F32;
+  a.epi.ldy[0] = N;
+  for (int r0 = 0; r0 < B; r0 += 32) {
+    a.B = std::min(32, B - r0);
+    a.x = (const __half*)xp + (size_t)r0 * K;
+    a.epi.y[0] = y + (size_t)r0 * N;
+    qgemv_plan(a, WL_LAYOUT_B, sm_count());
+    WL_TRY(launch_qgemv_b(a, (cudaStream_t)stream));
+  }
+  return WL_OK;
+}
+
 // quantization::simd::quantized_matvec (woolly-tensor/src/quantization.rs:869-909)
 int wl_quantized_matvec(int type, const void* W, const float* input, float* output, int m, int k,
                         void* stream) {

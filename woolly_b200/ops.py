@@ -58,6 +58,25 @@ def qgemv(weights: torch.Tensor, ggml_type: int, layout: int, x: torch.Tensor, n
     return y.reshape(*x.shape[:-1], n)
 
 
+def split_planes(x: torch.Tensor) -> torch.Tensor:
+    """f32 [B, K] -> f16 [2, B, K]: hi = f16(x), lo = f16(x - hi)."""
+    hi = x.to(torch.float16)
+    return torch.stack([hi, (x - hi.float()).to(torch.float16)]).contiguous()
+
+
+def qgemv_planes(weights: torch.Tensor, ggml_type: int, planes: torch.Tensor, n: int,
+                 out: torch.Tensor | None = None) -> torch.Tensor:
+    """Layout-B GEMV on hi/lo activation planes [2, B, K] (no allocation
+    inside the library; capturable in a CUDA graph)."""
+    _dev(weights, torch.uint8, "weights")
+    _dev(planes, torch.float16, "planes")
+    _, B, K = planes.shape
+    y = out if out is not None else torch.empty(B, n, dtype=torch.float32, device=planes.device)
+    check(lib().wl_qgemv_planes(int(ggml_type), weights.data_ptr(), K, n, planes.data_ptr(), B * K,
+                                B, y.data_ptr(), _stream()))
+    return y
+
+
 def rmsnorm_rope(x: torch.Tensor, w: torch.Tensor, eps: float, *, rope: bool = False,
                  positions: torch.Tensor | None = None, head_dim: int = 0, theta: float = 10000.0,
                  out_dtype=torch.float32) -> torch.Tensor:
