@@ -161,6 +161,26 @@ int wl_qgemv(int ggml_type, int layout, const void* W, int K, int N, const float
 int wl_qgemv_planes(int ggml_type, const void* W, int K, int N, const void* x_planes,
                     size_t x_plane, int B, float* y, void* stream);
 
+/* Allocation-free variant of wl_qgemv for layout B.  No counterpart in the
+ * reference: it exists for callers that may not allocate device memory after
+ * start-up (fixed-budget serving processes, hosts whose allocator belongs to
+ * another framework, code paths where an allocation could stall the device).
+ * Same inputs, outputs and results as wl_qgemv(..., WL_LAYOUT_B, ...).
+ * Limits and behaviour:
+ *  - B*K <= 524288 (2^19); larger calls fail with WL_ERR_INVALID_ARGUMENT;
+ *  - the activations are staged in one fixed 2 MiB device array inside the
+ *    library, which every GPU that loads the library keeps until exit;
+ *  - all calls share that array: calls that overlap on the GPU (different
+ *    streams, or different threads on one device) race and must be ordered by
+ *    the caller; each call rewrites every element it reads, so nothing
+ *    carries over between calls;
+ *  - the first call on a device looks up the array's device address (once
+ *    per device, with that device current); make that first call before any
+ *    stream capture;
+ *  - N % 32 == 0, K % 16 == 0 and 16-byte aligned weight rows. */
+int wl_qgemv_noalloc(int ggml_type, const void* W, int K, int N, const float* x, int B,
+                     float* y, void* stream);
+
 /* woolly_tensor quantization::simd::quantized_matvec(weights, input, output, m, k)
  * (quantization.rs:869): layout A, one input vector; Q4_0 and Q8_0 (Q4_1 ->
  * WL_ERR_UNSUPPORTED, as the reference). */
