@@ -341,10 +341,13 @@ def run_gpu(args):
 
     # ---- dominant kernel: the layout-B Q4_0 GEMV ----
     achieved, per_shape = gemv_roofline(torch, dev)
-    traffic = None
+    traffic = None  # dram bytes per launch, scaled from the committed ncu capture
     try:
         with open(os.path.join(ROOT, "profiles", "qgemv_b_q4_0_7b_decode.json")) as f:
-            traffic = json.load(f).get("dram_bytes_per_launch")
+            ratio = json.load(f)["traffic_ratio"]
+        mean_alg = sum(K * N // 32 * 18 + 4 * BATCH * (K + N) for K, N in
+                       [(4096, 12288), (4096, 4096), (4096, 22016), (11008, 4096)]) / 4
+        traffic = ratio * mean_alg
     except Exception:
         pass
 
