@@ -181,60 +181,89 @@ __device__ __forceinline__ void store_out(const GemvArgs& a, int seg, int b, int
   }
 }
 
-// Cluster reduction of the partial tiles (row pitch tp, `cols` per row) and
-// the epilogue for segment `seg`, segment-local first column col0.  Each CTA
-// of the cluster finishes every C-th element; partials are summed in rank
-// order (deterministic).  RoPE pairs (i, i + hd/2) are finished together.
-// For EPI_SWIGLU the cluster holds gate tiles at even ranks and the matching
-// up tiles at odd ranks.
+// Cluster reduction of the partial tiles (row pitch tp, `cols` per row, both
+// multiples of 4) and the epilogue for segment `seg`, segment-local first
+// column col0.  Work is split into float4 groups of 4 columns; each CTA of the
+// cluster finishes every C-th group, reading the C partial tiles through
+// distributed shared memory (loads unrolled over ranks, summed in rank order:
+// deterministic).  RoPE pairs (i, i + hd/2) are finished together.  For
+// EPI_SWIGLU the cluster holds gate tiles at even ranks and the matching up
+// tiles at odd ranks.
+__device__ __forceinline__ float4 f4add(float4 a, float4 b) {
+  return make_float4(a.x + b.x, a.y + b.y, a.z + b.z, a.w + b.w);
+}
+
+template <int STEP>  // sum ranks r0, r0+STEP, ... < C
+__device__ __forceinline__ float4 rank_sum(cg::cluster_group& cl, float* tile, int off, int C, int r0) {
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  float4 v[kMaxCluster / STEP];
+#pragma unroll
+  for (int q = 0; q < kMaxCluster / STEP; q++) {
+    const int rk = r0 + q * STEP;
+    if (rk < C) v[q] = *reinterpret_cast<const float4*>(cl.map_shared_rank(tile + off, rk));
+  }
+#pragma unroll
+  for (int q = 0; q < kMaxCluster / STEP; q++)
+    if (r0 + q * STEP < C) acc = f4add(acc, v[q]);
+  return acc;
+}
+
 __device__ void cluster_finish(const GemvArgs& a, float* tile, int tp, int cols, int ncv, int seg,
                                int col0) {
   cg::cluster_group cl = cg::this_cluster();
   const int C = (int)cl.num_blocks();
   const int r = (int)cl.block_rank();
   const int B = a.B;
-  const float* rt[kMaxCluster];
-#pragma unroll
-  for (int q = 0; q < kMaxCluster; q++) rt[q] = q < C ? cl.map_shared_rank(tile, q) : nullptr;
   cl.sync();  // every partial tile is complete
   const Epilogue& e = a.epi;
+  const int g4 = cols / 4;
   if (e.kind == EPI_SWIGLU) {
     __half* out = reinterpret_cast<__half*>(e.y[0]);
-    for (int i = r + C * threadIdx.x; i < B * cols; i += C * blockDim.x) {
-      const int b = i / cols, c = i - b * cols;
+    for (int i = r + C * threadIdx.x; i < B * g4; i += C * blockDim.x) {
+      const int b = i / g4, c = (i - b * g4) * 4;
       if (c >= ncv) continue;
-      float gs = 0.f, us = 0.f;
-      for (int q = 0; q < C; q += 2) gs += rt[q][b * tp + c], us += rt[q + 1][b * tp + c];
-      const float v = silu(gs) * us;  // swiglu, tensor_utils.rs:512-532
-      const __half hi = __float2half_rn(v);
+      const float4 gs = rank_sum<2>(cl, tile, b * tp + c, C, 0);
+      const float4 us = rank_sum<2>(cl, tile, b * tp + c, C, 1);
+      const float gv[4] = {gs.x, gs.y, gs.z, gs.w}, uv[4] = {us.x, us.y, us.z, us.w};
       const size_t o = (size_t)b * e.ldy[0] + col0 + c;
-      out[o] = hi;
-      out[o + e.y_plane] = __float2half_rn(v - __half2float(hi));
+#pragma unroll
+      for (int j = 0; j < 4; j++) {
+        const float v = silu(gv[j]) * uv[j];  // swiglu, tensor_utils.rs:512-532
+        const __half hi = __float2half_rn(v);
+        out[o + j] = hi;
+        out[o + j + e.y_plane] = __float2half_rn(v - __half2float(hi));
+      }
     }
   } else if (e.kind == EPI_QKV && e.rope && seg < 2) {
     // NeoX rotation inside each head (RoPE::apply_f32, woolly-tensor/src/ops/mod.rs:476-527);
     // col0 is a multiple of head_dim.
     const int hd = e.head_dim, half = hd / 2;
-    const int np = ncv / 2;
-    for (int i = r + C * threadIdx.x; i < B * np; i += C * blockDim.x) {
-      const int b = i / np, j = i - b * np;
+    const int np4 = ncv / 8;  // groups of 4 pairs
+    for (int i = r + C * threadIdx.x; i < B * np4; i += C * blockDim.x) {
+      const int b = i / np4, j = (i - b * np4) * 4;
       const int h = j / half, ii = j - h * half;
       const int c1 = h * hd + ii, c2 = c1 + half;
-      float x1 = 0.f, x2 = 0.f;
-      for (int q = 0; q < C; q++) x1 += rt[q][b * tp + c1], x2 += rt[q][b * tp + c2];
-      const float freq = 1.0f / powf(e.theta, 2.0f * (float)ii / (float)hd);
-      float sn, cs;
-      sincosf((float)e.row_pos[b] * freq, &sn, &cs);
-      store_out(a, seg, b, col0 + c1, x1 * cs - x2 * sn);
-      store_out(a, seg, b, col0 + c2, x1 * sn + x2 * cs);
+      const float4 s1 = rank_sum<1>(cl, tile, b * tp + c1, C, 0);
+      const float4 s2 = rank_sum<1>(cl, tile, b * tp + c2, C, 0);
+      const float x1[4] = {s1.x, s1.y, s1.z, s1.w}, x2[4] = {s2.x, s2.y, s2.z, s2.w};
+#pragma unroll
+      for (int u = 0; u < 4; u++) {
+        const float freq = 1.0f / powf(e.theta, 2.0f * (float)(ii + u) / (float)hd);
+        float sn, cs;
+        sincosf((float)e.row_pos[b] * freq, &sn, &cs);
+        store_out(a, seg, b, col0 + c1 + u, x1[u] * cs - x2[u] * sn);
+        store_out(a, seg, b, col0 + c2 + u, x1[u] * sn + x2[u] * cs);
+      }
     }
   } else {
-    for (int i = r + C * threadIdx.x; i < B * cols; i += C * blockDim.x) {
-      const int b = i / cols, c = i - b * cols;
+    for (int i = r + C * threadIdx.x; i < B * g4; i += C * blockDim.x) {
+      const int b = i / g4, c = (i - b * g4) * 4;
       if (c >= ncv) continue;
-      float v = 0.f;
-      for (int q = 0; q < C; q++) v += rt[q][b * tp + c];
-      store_out(a, seg, b, col0 + c, v);
+      const float4 v = rank_sum<1>(cl, tile, b * tp + c, C, 0);
+      store_out(a, seg, b, col0 + c, v.x);
+      store_out(a, seg, b, col0 + c + 1, v.y);
+      store_out(a, seg, b, col0 + c + 2, v.z);
+      store_out(a, seg, b, col0 + c + 3, v.w);
     }
   }
   cl.sync();  // keep this CTA's tile alive until every rank has read it
