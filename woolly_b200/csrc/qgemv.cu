@@ -29,6 +29,7 @@
 #include <cuda_fp16.h>
 
 #include <algorithm>
+#include <cstdlib>
 #include <string>
 
 #include "common.h"
@@ -61,6 +62,10 @@ constexpr int kGroupBlocks = 8;  // quant blocks per tile row
 constexpr int kColsB = 256;      // output columns per CTA, layout B
 constexpr int kColsA = 64;       // output rows per CTA, layout A
 constexpr int kMaxCluster = 16;
+#ifndef WL_PLAN_CTAS_PER_SM
+#define WL_PLAN_CTAS_PER_SM 2
+#endif
+constexpr int kPlanCtasPerSm = WL_PLAN_CTAS_PER_SM;  // CTAs the K-split planner aims for
 
 __device__ __forceinline__ void cp_async16(void* smem, const void* gmem, int src_bytes) {
   unsigned s = (unsigned)__cvta_generic_to_shared(smem);
@@ -79,6 +84,15 @@ __device__ __forceinline__ void mma16816(float* c, const uint32_t* a, uint32_t b
       "{%8,%9}, {%0,%1,%2,%3};\n"
       : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// four 8x8 b16 matrices; lane l supplies the row address of matrix l/8, row l%8
+__device__ __forceinline__ void ldsm_x4(const void* row_addr, uint32_t& r0, uint32_t& r1,
+                                        uint32_t& r2, uint32_t& r3) {
+  const unsigned a = (unsigned)__cvta_generic_to_shared(row_addr);
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(a));
 }
 
 __device__ __forceinline__ __half2 as_h2(uint32_t u) {
@@ -125,7 +139,7 @@ __device__ __forceinline__ uint32_t q8a(uint32_t v) {
 __device__ __forceinline__ void scale_split(uint32_t d, uint32_t xh, uint32_t xl, uint32_t& hi,
                                             uint32_t& lo) {
   __half2 hh = __hmul2(as_h2(d), as_h2(xh));
-  __half2 r = __hfma2(as_h2(d), as_h2(xh), as_h2(as_u(hh) ^ 0x80008000u));
+  __half2 r = __hfma2(as_h2(d), as_h2(xh), __hneg2(hh));
   hi = as_u(hh);
   lo = as_u(__hfma2(as_h2(d), as_h2(xl), r));
 }
@@ -193,18 +207,21 @@ __device__ __forceinline__ float4 f4add(float4 a, float4 b) {
   return make_float4(a.x + b.x, a.y + b.y, a.z + b.z, a.w + b.w);
 }
 
-template <int STEP>  // sum ranks r0, r0+STEP, ... < C
+template <int STEP>  // sum ranks r0, r0+STEP, ... < C (4 remote loads in flight at a time)
 __device__ __forceinline__ float4 rank_sum(cg::cluster_group& cl, float* tile, int off, int C, int r0) {
   float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-  float4 v[kMaxCluster / STEP];
 #pragma unroll
-  for (int q = 0; q < kMaxCluster / STEP; q++) {
-    const int rk = r0 + q * STEP;
-    if (rk < C) v[q] = *reinterpret_cast<const float4*>(cl.map_shared_rank(tile + off, rk));
+  for (int q0 = 0; q0 < kMaxCluster / STEP; q0 += 4) {
+    float4 v[4];
+#pragma unroll
+    for (int q = 0; q < 4; q++) {
+      const int rk = r0 + (q0 + q) * STEP;
+      if (rk < C) v[q] = *reinterpret_cast<const float4*>(cl.map_shared_rank(tile + off, rk));
+    }
+#pragma unroll
+    for (int q = 0; q < 4; q++)
+      if (r0 + (q0 + q) * STEP < C) acc = f4add(acc, v[q]);
   }
-#pragma unroll
-  for (int q = 0; q < kMaxCluster / STEP; q++)
-    if (r0 + q * STEP < C) acc = f4add(acc, v[q]);
   return acc;
 }
 
@@ -373,14 +390,14 @@ __global__ void __launch_bounds__(kThreads) k_qgemv_b(const GemvArgs a) {
     // rows past the end of this split are zero-filled and contribute exactly 0
 #pragma unroll
     for (int ks = 0; ks < kRows / 16; ks++) {
+      // B fragments (session = n*8 + g, k = 2t..2t+1 | +8) of the hi and lo planes:
+      // matrices {hi k0-7, hi k8-15, lo k0-7, lo k8-15} of rows n*8..n*8+7
       uint32_t xh[NT][2], xl[NT][2];
 #pragma unroll
       for (int n = 0; n < NT; n++) {
-        const __half* xp = xs + (n * 8 + g) * XP + ks * 16 + 2 * t;
-        xh[n][0] = *reinterpret_cast<const uint32_t*>(xp);
-        xh[n][1] = *reinterpret_cast<const uint32_t*>(xp + 8);
-        xl[n][0] = *reinterpret_cast<const uint32_t*>(xp + BP * XP);
-        xl[n][1] = *reinterpret_cast<const uint32_t*>(xp + BP * XP + 8);
+        const int mi = lane >> 3;
+        const __half* ra = xs + (mi >> 1) * BP * XP + (n * 8 + (lane & 7)) * XP + ks * 16 + (mi & 1) * 8;
+        ldsm_x4(ra, xh[n][0], xh[n][1], xl[n][0], xl[n][1]);
       }
       const uint8_t* p0b = rs + (ks * 16 + 2 * t) * Q::SP + warp * 2 * Q::S;
 #pragma unroll
@@ -776,7 +793,8 @@ void qgemv_plan(GemvArgs& a, int layout, int num_sms) {
   for (int s = 0; s < a.nseg; s++) groups += a.seg[s].groups;
   const int gran = layout == WL_LAYOUT_B ? 16 : 256;
   const int units = (a.K + gran - 1) / gran;
-  const int target = 2 * num_sms;
+  static const int per_sm = getenv("WL_PLAN_CTAS") ? atoi(getenv("WL_PLAN_CTAS")) : kPlanCtasPerSm;
+  const int target = per_sm * num_sms;
   const int cmax = a.epi.kind == EPI_SWIGLU ? kMaxCluster / 2 : kMaxCluster;
   int c = (target + groups - 1) / std::max(groups, 1);
   c = std::max(1, std::min({c, cmax, units}));
