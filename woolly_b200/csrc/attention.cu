@@ -24,6 +24,7 @@
 
 #include "common.h"
 #include "kernels.cuh"
+#include "pdl.cuh"
 
 namespace wl {
 namespace {
@@ -96,6 +97,8 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_paged(const AttnArgs a, f
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int kvh = blockIdx.x, r = blockIdx.y, sp = blockIdx.z;
+  pdl_wait();
+  pdl_trigger();
   const int pos = a.row_pos[r];
   const int sess = a.row_sess[r];
   const int j0 = (a.window > 0 && pos - a.window + 1 > 0) ? pos - a.window + 1 : 0;
@@ -244,6 +247,8 @@ template <int HD>
 __global__ void k_attn_combine(const float* part_o, const float* part_ml, int heads, int nsplit,
                                void* out, int ldo, size_t out_plane) {
   const int r = blockIdx.x, h = blockIdx.y, d = threadIdx.x;
+  pdl_wait();
+  pdl_trigger();
   const size_t base = ((size_t)r * heads + h) * nsplit;
   float M = -INFINITY;
   for (int s = 0; s < nsplit; s++) M = fmaxf(M, part_ml[(base + s) * 2]);
@@ -269,9 +274,8 @@ int launch_paged_g(const AttnArgs& a, float scale, cudaStream_t st) {
                                      (int)smem));
     done |= 1u << (dev & 31);
   }
-  k_attn_paged<HD, G><<<dim3(a.kv_heads, a.rows, a.nsplit), kAttnThreads, smem, st>>>(a, scale);
-  WL_CUDA_TRY(cudaGetLastError());
-  return WL_OK;
+  return launch_k(k_attn_paged<HD, G>, dim3(a.kv_heads, a.rows, a.nsplit), dim3(kAttnThreads), smem,
+                  st, a, scale);
 }
 
 template <int HD>
@@ -288,9 +292,9 @@ int launch_paged_hd(const AttnArgs& a, int G, float scale, cudaStream_t st) {
   }
   if (s) return s;
   if (a.nsplit > 1) {
-    k_attn_combine<HD><<<dim3(a.rows, a.heads), HD, 0, st>>>(a.part_o, a.part_ml, a.heads,
-                                                             a.nsplit, a.out, a.ldo, a.out_plane);
-    WL_CUDA_TRY(cudaGetLastError());
+    WL_TRY(launch_k(k_attn_combine<HD>, dim3(a.rows, a.heads), dim3(HD), 0, st,
+                    (const float*)a.part_o, (const float*)a.part_ml, a.heads, a.nsplit, a.out, a.ldo,
+                    a.out_plane));
   }
   return WL_OK;
 }

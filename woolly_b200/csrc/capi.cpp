@@ -17,6 +17,9 @@ namespace wl {
 
 thread_local std::string g_err;
 void set_error(const std::string& m) { g_err = m; }
+thread_local bool g_pdl = false;
+bool pdl_enabled() { return g_pdl; }
+void set_pdl(bool on) { g_pdl = on; }
 
 int model_load(wl_ctx*, const char*, const wl_model_options*, wl_model**);
 void model_free(wl_model*);

@@ -10,6 +10,8 @@
 namespace wl {
 
 void set_error(const std::string& msg);
+// programmatic dependent launch for the kernels the calling thread enqueues
+void set_pdl(bool on);
 inline int fail(int code, const std::string& msg) {
   set_error(msg);
   return code;

@@ -15,6 +15,7 @@
 #include <dlfcn.h>
 
 #include <algorithm>
+#include <cstdlib>
 #include <cstring>
 #include <string>
 
@@ -330,7 +331,19 @@ static int gemv(wl_model* m, int nseg, const QMat* mats, int R, const __half* x,
 
 // The whole forward for R rows whose ids/positions/sessions are on device.
 // Logits are produced for rows [lfirst, R) into m->logits (row 0 = lfirst).
+static int run_rows_body(wl_model* m, int R, int nsplit, int lfirst);
+
+// The forward's kernels chain with programmatic dependent launch unless
+// WL_NO_PDL is set in the environment.
 static int run_rows(wl_model* m, int R, int nsplit, int lfirst) {
+  static const bool pdl = getenv("WL_NO_PDL") == nullptr;
+  set_pdl(pdl && m->tp_size == 1);
+  const int s = run_rows_body(m, R, nsplit, lfirst);
+  set_pdl(false);
+  return s;
+}
+
+static int run_rows_body(wl_model* m, int R, int nsplit, int lfirst) {
   cudaStream_t st = m->st;
   const bool tp = m->tp_size > 1;
   const int qd = m->Hl * m->hd;

@@ -7,6 +7,7 @@
 
 #include "common.h"
 #include "kernels.cuh"
+#include "pdl.cuh"
 
 namespace wl {
 namespace {
@@ -31,6 +32,8 @@ __global__ void __launch_bounds__(kNormThreads)
               int hd, float theta, void* y, int y_mode, size_t y_plane) {
   extern __shared__ float srow[];  // normalised row when rope is on
   __shared__ float sred[kNormThreads / 32];
+  pdl_wait();
+  pdl_trigger();
   const int r = blockIdx.x, tid = threadIdx.x;
   const float* xr = x + (size_t)r * dim;
   float ss = 0.f;
@@ -72,6 +75,8 @@ __global__ void __launch_bounds__(kNormThreads)
 // (lazy_transformer.rs:1252-1262).  Out-of-range ids raise a flag and read id 0.
 __global__ void k_embed(const float* E, int d, int V, const uint32_t* ids, int rows, float* h,
                         int* err) {
+  pdl_wait();
+  pdl_trigger();
   const int r = blockIdx.y;
   const int j = blockIdx.x * blockDim.x + threadIdx.x;
   if (j >= d || r >= rows) return;
@@ -156,19 +161,15 @@ int launch_rmsnorm(const float* x, const float* w, int rows, int dim, float eps,
     WL_CUDA_TRY(cudaFuncSetAttribute(k_rmsnorm, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      (int)smem));
   }
-  k_rmsnorm<<<rows, kNormThreads, smem, st>>>(x, w, dim, eps, rope, pos, head_dim, theta, y, y_mode,
-                                             y_plane);
-  WL_CUDA_TRY(cudaGetLastError());
-  return WL_OK;
+  return launch_k(k_rmsnorm, dim3(rows), dim3(kNormThreads), smem, st, x, w, dim, eps, rope, pos,
+                  head_dim, theta, y, y_mode, y_plane);
 }
 
 int launch_embed(const float* E, int d, int V, const uint32_t* ids, int rows, float* h,
                  int* err_flag, cudaStream_t st) {
   if (rows <= 0) return WL_OK;
   dim3 grid((d + 255) / 256, rows);
-  k_embed<<<grid, 256, 0, st>>>(E, d, V, ids, rows, h, err_flag);
-  WL_CUDA_TRY(cudaGetLastError());
-  return WL_OK;
+  return launch_k(k_embed, grid, dim3(256), 0, st, E, d, V, ids, rows, h, err_flag);
 }
 
 int launch_swiglu(const float* g, const float* u, size_t n, float* out, cudaStream_t st) {

@@ -34,6 +34,7 @@
 
 #include "common.h"
 #include "qgemv.cuh"
+#include "pdl.cuh"
 
 namespace cg = cooperative_groups;
 
@@ -55,9 +56,19 @@ struct QT<WL_Q8_0> {
   static constexpr int S = 34, QOFF = 2, SP = 272;
 };
 
-constexpr int kThreads = 128;
+constexpr int kThreads = 128;  // layout A
+#ifndef WL_GEMV_B_THREADS
+#define WL_GEMV_B_THREADS 128
+#endif
+constexpr int kThreadsB = WL_GEMV_B_THREADS;  // layout B: warps 4..7 take the second half of each stage's k-steps
+constexpr int kKParts = kThreadsB / 128;
 constexpr int kRows = 64;  // matrix rows per pipeline stage
-constexpr int kStages = 4;
+constexpr int kStages = 4;  // layout A
+#ifndef WL_GEMV_STAGES_B
+#define WL_GEMV_STAGES_B 4
+#endif
+// layout-B pipeline depth: batch tiles of up to 16 rows keep more stages in flight
+__host__ __device__ constexpr int stages_b(int NT) { return NT <= 2 ? WL_GEMV_STAGES_B : 4; }
 constexpr int kGroupBlocks = 8;  // quant blocks per tile row
 constexpr int kColsB = 256;      // output columns per CTA, layout B
 constexpr int kColsA = 64;       // output rows per CTA, layout A
@@ -79,7 +90,7 @@ __device__ __forceinline__ void cp_wait() {
 }
 
 __device__ __forceinline__ void mma16816(float* c, const uint32_t* a, uint32_t b0, uint32_t b1) {
-  asm volatile(
+  asm(
       "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
       "{%8,%9}, {%0,%1,%2,%3};\n"
       : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
@@ -171,6 +182,24 @@ __device__ __forceinline__ void split_tile(const float* src, __half* xs, int BP,
   }
 }
 
+// Compile-time phase timeline for kernel studies (off in normal builds): thread 0
+// of each CTA stores %globaltimer at entry, first stage, loop end, cluster
+// barrier and exit.
+#ifdef WL_EXP_TIMING
+__device__ unsigned long long g_tl[8192][5];
+__device__ __forceinline__ unsigned long long gtime() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+#define TL(i)                                                              \
+  if (threadIdx.x == 0) {                                                  \
+    const int cid = blockIdx.x + gridDim.x * blockIdx.y;                   \
+    if (cid < 8192) g_tl[cid][i] = gtime();                                \
+  }
+#else
+#define TL(i)
+#endif
 // ------------------------------------------------------------------ epilogue
 __device__ __forceinline__ void store_out(const GemvArgs& a, int seg, int b, int col, float v) {
   const Epilogue& e = a.epi;
@@ -195,73 +224,143 @@ __device__ __forceinline__ void store_out(const GemvArgs& a, int seg, int b, int
   }
 }
 
-// Cluster reduction of the partial tiles (row pitch tp, `cols` per row, both
-// multiples of 4) and the epilogue for segment `seg`, segment-local first
-// column col0.  Work is split into float4 groups of 4 columns; each CTA of the
-// cluster finishes every C-th group, reading the C partial tiles through
-// distributed shared memory (loads unrolled over ranks, summed in rank order:
-// deterministic).  RoPE pairs (i, i + hd/2) are finished together.  For
-// EPI_SWIGLU the cluster holds gate tiles at even ranks and the matching up
-// tiles at odd ranks.
+// Cluster split-K reduction by push.  The output tile of a CTA (B rows x
+// `cols` columns, ncv valid) is cut into float4 groups; group q of every CTA
+// is owned by rank item(q) % C.  Each CTA sends its partial of every group to
+// the owner's receive area with st.async (remote shared-memory stores that
+// count bytes on the owner's mbarrier), then waits until the C partials of its
+// own groups have arrived and sums them in rank order (deterministic).  One
+// cluster barrier, split into arrive (kernel start, after the mbarrier init)
+// and wait (before the first send), orders the init before any remote store;
+// no barrier is needed at the end because an owner only exits after its bytes
+// have landed.  RoPE items hold the pair of groups (i, i + hd/2); for
+// EPI_SWIGLU gate tiles sit at even ranks and the matching up tiles at odd
+// ranks.
 __device__ __forceinline__ float4 f4add(float4 a, float4 b) {
   return make_float4(a.x + b.x, a.y + b.y, a.z + b.z, a.w + b.w);
 }
 
-template <int STEP>  // sum ranks r0, r0+STEP, ... < C (4 remote loads in flight at a time)
-__device__ __forceinline__ float4 rank_sum(cg::cluster_group& cl, float* tile, int off, int C, int r0) {
-  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-  for (int q0 = 0; q0 < kMaxCluster / STEP; q0 += 4) {
-    float4 v[4];
-#pragma unroll
-    for (int q = 0; q < 4; q++) {
-      const int rk = r0 + (q0 + q) * STEP;
-      if (rk < C) v[q] = *reinterpret_cast<const float4*>(cl.map_shared_rank(tile + off, rk));
-    }
-#pragma unroll
-    for (int q = 0; q < 4; q++)
-      if (r0 + (q0 + q) * STEP < C) acc = f4add(acc, v[q]);
-  }
-  return acc;
+struct ClusterRed {
+  uint32_t bar = 0;  // shared address of the mbarrier
+  float4* recv = nullptr;
+  int C = 1, r = 0, nitems = 0, parts = 1, ipr = 0;
+};
+
+// receive area bytes for BP padded rows of `cols` columns
+__host__ __device__ constexpr size_t recv_bytes(int BP, int cols) {
+  return ((size_t)BP * cols / 4 + 2 * kMaxCluster) * 16;
 }
 
-__device__ void cluster_finish(const GemvArgs& a, float* tile, int tp, int cols, int ncv, int seg,
-                               int col0) {
+__device__ __forceinline__ bool red_rope(const GemvArgs& a, int seg) {
+  return a.epi.kind == EPI_QKV && a.epi.rope && seg < 2;
+}
+
+__device__ __forceinline__ void red_begin(ClusterRed& R, const GemvArgs& a, int seg, int ncv,
+                                          uint64_t* bar, void* recv) {
   cg::cluster_group cl = cg::this_cluster();
-  const int C = (int)cl.num_blocks();
-  const int r = (int)cl.block_rank();
+  R.C = (int)cl.num_blocks();
+  R.r = (int)cl.block_rank();
+  R.parts = red_rope(a, seg) ? 2 : 1;
+  R.nitems = a.B * (ncv / (4 * R.parts));
+  R.ipr = (R.nitems + R.C - 1) / R.C;
+  R.recv = reinterpret_cast<float4*>(recv);
+  R.bar = (uint32_t)__cvta_generic_to_shared(bar);
+  if (threadIdx.x == 0) {
+    const int mine = R.r < R.nitems ? (R.nitems - 1 - R.r) / R.C + 1 : 0;
+    const uint32_t bytes = (uint32_t)(mine * R.C * R.parts * 16);
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;\n" ::"r"(R.bar) : "memory");
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(R.bar), "r"(bytes)
+                 : "memory");
+    asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+  }
+  asm volatile("barrier.cluster.arrive.release.aligned;\n" ::: "memory");
+}
+
+__device__ __forceinline__ void st_async4(uint32_t dst, float4 v, uint32_t bar) {
+  asm volatile(
+      "st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.f32 [%0], {%1, %2, %3, %4}, [%5];\n" ::"r"(dst),
+      "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w), "r"(bar)
+      : "memory");
+}
+__device__ __forceinline__ uint32_t mapa(uint32_t addr, int rank) {
+  uint32_t out;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;\n" : "=r"(out) : "r"(addr), "r"(rank));
+  return out;
+}
+
+// bounded wait for phase 0 of the receive barrier; false when it gave up
+__device__ __forceinline__ bool red_wait(uint32_t bar) {
+  for (int it = 0; it < (1 << 22); it++) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], 0;\n"
+        " selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(bar)
+        : "memory");
+    if (ok) return true;
+  }
+  return false;
+}
+
+__device__ void cluster_finish(const GemvArgs& a, const ClusterRed& R, float* tile, int tp,
+                               int ncv, int seg, int col0) {
+  const int C = R.C, r = R.r, P = R.parts;
   const int B = a.B;
-  cl.sync();  // every partial tile is complete
   const Epilogue& e = a.epi;
-  const int g4 = cols / 4;
-  if (e.kind == EPI_SWIGLU) {
-    __half* out = reinterpret_cast<__half*>(e.y[0]);
-    for (int i = r + C * threadIdx.x; i < B * g4; i += C * blockDim.x) {
-      const int b = i / g4, c = (i - b * g4) * 4;
-      if (c >= ncv) continue;
-      const float4 gs = rank_sum<2>(cl, tile, b * tp + c, C, 0);
-      const float4 us = rank_sum<2>(cl, tile, b * tp + c, C, 1);
+  const int g4 = ncv / 4;
+  const int hd = e.head_dim, half = hd / 2;
+  asm volatile("barrier.cluster.wait.acquire.aligned;\n" ::: "memory");  // every mbarrier is set up
+  TL(3);
+  // send: group q = (b, c) of this CTA's tile to its owner
+  const uint32_t recv0 = (uint32_t)__cvta_generic_to_shared(R.recv);
+  for (int q = threadIdx.x; q < B * g4; q += blockDim.x) {
+    const int b = q / g4, c = (q - b * g4) * 4;
+    int item = q, part = 0;
+    if (P == 2) {
+      const int h = c / hd, w = c - h * hd;
+      part = w >= half;
+      item = b * (g4 / 2) + h * (half / 4) + (w - part * half) / 4;
+    }
+    const int owner = item % C, j = item / C;
+    const float4 v = *reinterpret_cast<const float4*>(tile + b * tp + c);
+    st_async4(mapa(recv0 + (uint32_t)(((r * R.ipr + j) * P + part) * 16), owner), v,
+              mapa(R.bar, owner));
+  }
+  if (!red_wait(R.bar)) {
+    if (a.err && threadIdx.x == 0) atomicOr(a.err, 4);
+    return;
+  }
+  // finish the owned items, partials summed in rank order
+  for (int j = threadIdx.x; r + C * j < R.nitems; j += blockDim.x) {
+    const int item = r + C * j;
+    if (e.kind == EPI_SWIGLU) {
+      const int b = item / g4, c = (item - b * g4) * 4;
+      float4 gs = make_float4(0.f, 0.f, 0.f, 0.f), us = gs;
+      for (int src = 0; src < C; src += 2) gs = f4add(gs, R.recv[src * R.ipr + j]);
+      for (int src = 1; src < C; src += 2) us = f4add(us, R.recv[src * R.ipr + j]);
       const float gv[4] = {gs.x, gs.y, gs.z, gs.w}, uv[4] = {us.x, us.y, us.z, us.w};
+      __half* out = reinterpret_cast<__half*>(e.y[0]);
       const size_t o = (size_t)b * e.ldy[0] + col0 + c;
 #pragma unroll
-      for (int j = 0; j < 4; j++) {
-        const float v = silu(gv[j]) * uv[j];  // swiglu, tensor_utils.rs:512-532
+      for (int u = 0; u < 4; u++) {
+        const float v = silu(gv[u]) * uv[u];  // swiglu, tensor_utils.rs:512-532
         const __half hi = __float2half_rn(v);
-        out[o + j] = hi;
-        out[o + j + e.y_plane] = __float2half_rn(v - __half2float(hi));
+        out[o + u] = hi;
+        out[o + u + e.y_plane] = __float2half_rn(v - __half2float(hi));
       }
-    }
-  } else if (e.kind == EPI_QKV && e.rope && seg < 2) {
-    // NeoX rotation inside each head (RoPE::apply_f32, woolly-tensor/src/ops/mod.rs:476-527);
-    // col0 is a multiple of head_dim.
-    const int hd = e.head_dim, half = hd / 2;
-    const int np4 = ncv / 8;  // groups of 4 pairs
-    for (int i = r + C * threadIdx.x; i < B * np4; i += C * blockDim.x) {
-      const int b = i / np4, j = (i - b * np4) * 4;
-      const int h = j / half, ii = j - h * half;
+    } else if (P == 2) {
+      // NeoX rotation inside each head (RoPE::apply_f32, woolly-tensor/src/ops/mod.rs:476-527);
+      // col0 is a multiple of head_dim.
+      const int np4 = g4 / 2;
+      const int b = item / np4, p = item - b * np4;
+      const int h = p / (half / 4), ii = (p - h * (half / 4)) * 4;
       const int c1 = h * hd + ii, c2 = c1 + half;
-      const float4 s1 = rank_sum<1>(cl, tile, b * tp + c1, C, 0);
-      const float4 s2 = rank_sum<1>(cl, tile, b * tp + c2, C, 0);
+      float4 s1 = make_float4(0.f, 0.f, 0.f, 0.f), s2 = s1;
+      for (int src = 0; src < C; src++) {
+        s1 = f4add(s1, R.recv[(src * R.ipr + j) * 2]);
+        s2 = f4add(s2, R.recv[(src * R.ipr + j) * 2 + 1]);
+      }
       const float x1[4] = {s1.x, s1.y, s1.z, s1.w}, x2[4] = {s2.x, s2.y, s2.z, s2.w};
 #pragma unroll
       for (int u = 0; u < 4; u++) {
@@ -271,35 +370,35 @@ __device__ void cluster_finish(const GemvArgs& a, float* tile, int tp, int cols,
         store_out(a, seg, b, col0 + c1 + u, x1[u] * cs - x2[u] * sn);
         store_out(a, seg, b, col0 + c2 + u, x1[u] * sn + x2[u] * cs);
       }
-    }
-  } else {
-    for (int i = r + C * threadIdx.x; i < B * g4; i += C * blockDim.x) {
-      const int b = i / g4, c = (i - b * g4) * 4;
-      if (c >= ncv) continue;
-      const float4 v = rank_sum<1>(cl, tile, b * tp + c, C, 0);
+    } else {
+      const int b = item / g4, c = (item - b * g4) * 4;
+      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int src = 0; src < C; src++) v = f4add(v, R.recv[src * R.ipr + j]);
       store_out(a, seg, b, col0 + c, v.x);
       store_out(a, seg, b, col0 + c + 1, v.y);
       store_out(a, seg, b, col0 + c + 2, v.z);
       store_out(a, seg, b, col0 + c + 3, v.w);
     }
   }
-  cl.sync();  // keep this CTA's tile alive until every rank has read it
 }
 
 // ------------------------------------------------------------------ layout B
 template <int T, int NT>
-__global__ void __launch_bounds__(kThreads) k_qgemv_b(const GemvArgs a) {
+__global__ void __launch_bounds__(kThreadsB) k_qgemv_b(const GemvArgs a) {
   using Q = QT<T>;
   constexpr int BP = NT * 8;  // padded batch rows
   constexpr int RAW = kRows * Q::SP;
   constexpr int XP = kRows + 8;               // halves per staged x row (bank-conflict pad)
   constexpr int SST = RAW + 2 * BP * XP * 2;  // stage: weight tile + hi/lo x planes
+  constexpr int SB = stages_b(NT);
   constexpr int CH = kGroupBlocks * Q::S / 16;  // 16-byte chunks per tile row
   constexpr int XCH = 2 * BP * (kRows / 8);     // 16-byte chunks of x per stage
   extern __shared__ __align__(16) uint8_t smem[];
   uint8_t* raw = smem;
+  TL(0);
 
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int tid = threadIdx.x, lane = tid & 31;
+  const int warp = (tid >> 5) & 3, kpart = tid >> 7;  // block pair, k-step part
   const int g = lane >> 2, t = lane & 3;
   const int gx = blockIdx.x, split = blockIdx.y;
   int seg = 0, lg;
@@ -319,14 +418,19 @@ __global__ void __launch_bounds__(kThreads) k_qgemv_b(const GemvArgs a) {
   const int nstage = k1 > k0 ? (k1 - k0 + kRows - 1) / kRows : 0;
   // valid payload bytes of this group's tile row (the last group may be partial)
   const int vbytes = min(kGroupBlocks, Nseg / 32 - lg * kGroupBlocks) * Q::S;
+  const int ncv = min(kColsB, Nseg - lg * kColsB);
+  constexpr int PIPE = SB * SST > BP * (kColsB + 4) * 4 ? SB * SST : BP * (kColsB + 4) * 4;
+  __shared__ uint64_t red_bar;
+  ClusterRed R;
+  red_begin(R, a, seg, ncv, &red_bar, smem + PIPE);
 
   // this thread's 16-byte chunks of a stage (fixed across stages)
-  constexpr int NWC = (kRows * CH + kThreads - 1) / kThreads;
-  constexpr int NXC = (XCH + kThreads - 1) / kThreads;
+  constexpr int NWC = (kRows * CH + kThreadsB - 1) / kThreadsB;
+  constexpr int NXC = (XCH + kThreadsB - 1) / kThreadsB;
   int wr[NWC], wc[NWC];
 #pragma unroll
   for (int j = 0; j < NWC; j++) {
-    const int i = tid + j * kThreads;
+    const int i = tid + j * kThreadsB;
     wr[j] = i < kRows * CH ? i / CH : -1;
     wc[j] = i - (i / CH) * CH;
   }
@@ -335,7 +439,7 @@ __global__ void __launch_bounds__(kThreads) k_qgemv_b(const GemvArgs a) {
   size_t xsrc[NXC];
 #pragma unroll
   for (int j = 0; j < NXC; j++) {
-    const int i = tid + j * kThreads;
+    const int i = tid + j * kThreadsB;
     const int p = i / (BP * (kRows / 8)), rem = i - p * BP * (kRows / 8);
     const int b = rem / (kRows / 8), c = rem - b * (kRows / 8);
     const bool live = i < XCH && b < a.B;
@@ -343,7 +447,7 @@ __global__ void __launch_bounds__(kThreads) k_qgemv_b(const GemvArgs a) {
     xo[j] = (p * BP * XP + b * XP + c * 8) * 2;
     xsrc[j] = live ? p * a.x_plane + (size_t)b * a.ldx + c * 8 : 0;
   }
-  auto load_stage = [&](int st, int buf) {
+  auto load_w = [&](int st, int buf) {  // immutable weights
     const int r0 = k0 + st * kRows;
     uint8_t* dst = raw + buf * SST;
 #pragma unroll
@@ -354,17 +458,31 @@ __global__ void __launch_bounds__(kThreads) k_qgemv_b(const GemvArgs a) {
       cp_async16(dst + wr[j] * Q::SP + wc[j] * 16,
                  W + (ok ? (size_t)row * pitch + wc[j] * 16 : 0), ok ? 16 : 0);
     }
+  };
+  auto load_x = [&](int st, int buf) {  // activations written by the previous kernel
+    const int r0 = k0 + st * kRows;
+    uint8_t* dst = raw + buf * SST;
 #pragma unroll
     for (int j = 0; j < NXC; j++) {
-      if (tid + j * kThreads >= XCH) continue;
+      if (tid + j * kThreadsB >= XCH) continue;
       const bool ok = xc[j] >= 0 && r0 + xc[j] < k1;
       cp_async16(dst + RAW + xo[j], xg + (ok ? xsrc[j] + r0 : 0), ok ? 16 : 0);
     }
   };
+  auto load_stage = [&](int st, int buf) {
+    load_w(st, buf);
+    load_x(st, buf);
+  };
 
+  // weight prefetch of the first stages may overlap the previous kernel (PDL)
 #pragma unroll
-  for (int s = 0; s < kStages - 1; s++) {
-    if (s < nstage) load_stage(s, s);
+  for (int s = 0; s < SB - 1; s++)
+    if (s < nstage) load_w(s, s);
+  pdl_wait();
+  pdl_trigger();
+#pragma unroll
+  for (int s = 0; s < SB - 1; s++) {
+    if (s < nstage) load_x(s, s);
     cp_commit();
   }
 
@@ -378,18 +496,25 @@ __global__ void __launch_bounds__(kThreads) k_qgemv_b(const GemvArgs a) {
       for (int q = 0; q < 4; q++) acc[i][0][n][q] = acc[i][1][n][q] = accm[i][n][q] = 0.f;
 
   for (int st = 0; st < nstage; st++) {
-    cp_wait<kStages - 2>();
+    cp_wait<SB - 2>();
     __syncthreads();
+#ifdef WL_EXP_TIMING
+    if (st == 0 && threadIdx.x == 0) {
+      const int cid = blockIdx.x + gridDim.x * blockIdx.y;
+      if (cid < 8192) g_tl[cid][1] = gtime();
+    }
+#endif
     {
-      const int nx = st + kStages - 1;
-      if (nx < nstage) load_stage(nx, nx % kStages);
+      const int nx = st + SB - 1;
+      if (nx < nstage) load_stage(nx, nx % SB);
       cp_commit();
     }
-    const uint8_t* rs = raw + (st % kStages) * SST;
+    const uint8_t* rs = raw + (st % SB) * SST;
     const __half* xs = reinterpret_cast<const __half*>(rs + RAW);
     // rows past the end of this split are zero-filled and contribute exactly 0
 #pragma unroll
-    for (int ks = 0; ks < kRows / 16; ks++) {
+    for (int kk = 0; kk < kRows / 16 / kKParts; kk++) {
+      const int ks = kpart * (kRows / 16 / kKParts) + kk;
       // B fragments (session = n*8 + g, k = 2t..2t+1 | +8) of the hi and lo planes:
       // matrices {hi k0-7, hi k8-15, lo k0-7, lo k8-15} of rows n*8..n*8+7
       uint32_t xh[NT][2], xl[NT][2];
@@ -468,27 +593,38 @@ __global__ void __launch_bounds__(kThreads) k_qgemv_b(const GemvArgs a) {
   }
   cp_wait<0>();
   __syncthreads();
+  TL(2);
 
-  // accumulators -> tile[b][c] (reuses the pipeline buffers)
+  // accumulators -> tile[b][c] (reuses the pipeline buffers); the k-step parts
+  // add up in the tile
   constexpr int TP = kColsB + 4;
   float* tile = reinterpret_cast<float*>(smem);
 #pragma unroll
-  for (int blk = 0; blk < 2; blk++)
+  for (int pass = 0; pass < kKParts; pass++) {
+    if (kpart == pass) {
 #pragma unroll
-    for (int mt = 0; mt < 2; mt++)
+      for (int blk = 0; blk < 2; blk++)
 #pragma unroll
-      for (int n = 0; n < NT; n++)
+        for (int mt = 0; mt < 2; mt++)
 #pragma unroll
-        for (int q = 0; q < 4; q++) {
-          const int b = n * 8 + 2 * t + (q & 1);
-          const int c = (warp * 2 + blk) * 32 + 16 * mt + 2 * g + (q >> 1);
-          // m-tile 1 of the 4-bit types accumulated 16x the codes (exact power of two)
-          const float sc = (T != WL_Q8_0 && mt == 1) ? 0.0625f : 1.0f;
-          tile[b * TP + c] = acc[blk][mt][n][q] * sc + accm[blk][n][q];
-        }
-  __syncthreads();
-  const int ncv = min(kColsB, Nseg - lg * kColsB);
-  cluster_finish(a, tile, TP, kColsB, ncv, seg, lg * kColsB);
+          for (int n = 0; n < NT; n++)
+#pragma unroll
+            for (int q = 0; q < 4; q++) {
+              const int b = n * 8 + 2 * t + (q & 1);
+              const int c = (warp * 2 + blk) * 32 + 16 * mt + 2 * g + (q >> 1);
+              // m-tile 1 of the 4-bit types accumulated 16x the codes (exact power of two)
+              const float sc = (T != WL_Q8_0 && mt == 1) ? 0.0625f : 1.0f;
+              const float v = acc[blk][mt][n][q] * sc + accm[blk][n][q];
+              if (pass == 0)
+                tile[b * TP + c] = v;
+              else
+                tile[b * TP + c] += v;
+            }
+    }
+    __syncthreads();
+  }
+  cluster_finish(a, R, tile, TP, ncv, seg, lg * kColsB);
+  TL(4);
 }
 
 // ------------------------------------------------------------------ layout A
@@ -505,6 +641,8 @@ __global__ void __launch_bounds__(kThreads) k_qgemv_a(const GemvArgs a) {
   constexpr int PIPE = STG * SST > BP * (kColsA + 4) * 4 ? STG * SST : BP * (kColsA + 4) * 4;
   extern __shared__ __align__(16) uint8_t smem[];
   uint8_t* raw = smem;
+  pdl_wait();
+  pdl_trigger();
   __half* xs = reinterpret_cast<__half*>(smem + PIPE);
   const __half* xl_base = xs + BP * XP;
 
@@ -516,6 +654,10 @@ __global__ void __launch_bounds__(kThreads) k_qgemv_a(const GemvArgs a) {
   const int k0 = split * a.kchunk;
   const int k1 = min(a.K, k0 + a.kchunk);
   const int nstage = k1 > k0 ? (k1 - k0) / KS : 0;
+  const int ncv = min(kColsA, S.N - n0);
+  __shared__ uint64_t red_bar;
+  ClusterRed R;
+  red_begin(R, a, 0, ncv, &red_bar, smem + PIPE + 2 * BP * XP * 2);
 
   auto load_stage = [&](int st, int buf) {
     const size_t byte0 = (size_t)((k0 + st * KS) / 32) * Q::S;
@@ -637,7 +779,7 @@ __global__ void __launch_bounds__(kThreads) k_qgemv_a(const GemvArgs a) {
       tile[b * TP + c] = acc[n][q];
     }
   __syncthreads();
-  cluster_finish(a, tile, TP, kColsA, min(kColsA, S.N - n0), 0, n0);
+  cluster_finish(a, R, tile, TP, ncv, 0, n0);
 }
 
 // ------------------------------------------------------------------ generic fallback
@@ -696,9 +838,9 @@ __global__ void k_split_planes(const float* x, __half* y, size_t n, size_t plane
 template <int T>
 size_t smem_b(int NT) {
   const size_t BP = (size_t)NT * 8;
-  const size_t pipe = (size_t)kStages * (kRows * QT<T>::SP + 2 * BP * (kRows + 8) * 2);
+  const size_t pipe = (size_t)stages_b(NT) * (kRows * QT<T>::SP + 2 * BP * (kRows + 8) * 2);
   const size_t tile = BP * (kColsB + 4) * 4;
-  return std::max(pipe, tile);
+  return std::max(pipe, tile) + recv_bytes((int)BP, kColsB);
 }
 template <int T>
 size_t smem_a(int NT) {
@@ -707,12 +849,12 @@ size_t smem_a(int NT) {
   const size_t pipe = (size_t)stg * (kColsA * QT<T>::SP + BP * 256 * 4);
   const size_t tile = BP * (kColsA + 4) * 4;
   const size_t xs = 2 * BP * (256 + 8) * 2;
-  return std::max(pipe, tile) + xs;
+  return std::max(pipe, tile) + xs + recv_bytes((int)BP, kColsA);
 }
 
 template <class Kern>
-int launch_cluster(Kern kern, dim3 grid, size_t smem, int cx, int cy, const GemvArgs& a,
-                   cudaStream_t st, unsigned& attr_done) {
+int launch_cluster(Kern kern, dim3 grid, int threads, size_t smem, int cx, int cy,
+                   const GemvArgs& a, cudaStream_t st, unsigned& attr_done) {
   int dev = 0;
   cudaGetDevice(&dev);
   if (!(attr_done >> (dev & 31) & 1u)) {
@@ -722,16 +864,21 @@ int launch_cluster(Kern kern, dim3 grid, size_t smem, int cx, int cy, const Gemv
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
-  cfg.blockDim = dim3(kThreads);
+  cfg.blockDim = dim3(threads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
-  cudaLaunchAttribute at[1];
+  cudaLaunchAttribute at[2];
   at[0].id = cudaLaunchAttributeClusterDimension;
   at[0].val.clusterDim.x = cx;
   at[0].val.clusterDim.y = cy;
   at[0].val.clusterDim.z = 1;
-  cfg.attrs = at;
   cfg.numAttrs = 1;
+  if (pdl_enabled()) {
+    at[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.numAttrs = 2;
+  }
+  cfg.attrs = at;
   WL_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, a));
   return WL_OK;
 }
@@ -742,14 +889,16 @@ int launch_b_t(const GemvArgs& a, cudaStream_t st) {
   int groups = 0;
   for (int s = 0; s < a.nseg; s++) groups += a.seg[s].groups;
   const bool sw = a.epi.kind == EPI_SWIGLU;
-  return launch_cluster(k_qgemv_b<T, NT>, dim3(groups, a.csplit), smem_b<T>(NT), sw ? 2 : 1,
+  return launch_cluster(k_qgemv_b<T, NT>, dim3(groups, a.csplit), kThreadsB, smem_b<T>(NT),
+                        sw ? 2 : 1,
                         a.csplit, a, st, attr_done);
 }
 
 template <int T, int NT>
 int launch_a_t(const GemvArgs& a, cudaStream_t st) {
   static unsigned attr_done = 0;
-  return launch_cluster(k_qgemv_a<T, NT>, dim3(a.seg[0].groups, a.csplit), smem_a<T>(NT), 1,
+  return launch_cluster(k_qgemv_a<T, NT>, dim3(a.seg[0].groups, a.csplit), kThreads,
+                        smem_a<T>(NT), 1,
                         a.csplit, a, st, attr_done);
 }
 
@@ -793,10 +942,10 @@ void qgemv_plan(GemvArgs& a, int layout, int num_sms) {
   for (int s = 0; s < a.nseg; s++) groups += a.seg[s].groups;
   const int gran = layout == WL_LAYOUT_B ? 16 : 256;
   const int units = (a.K + gran - 1) / gran;
-  static const int per_sm = getenv("WL_PLAN_CTAS") ? atoi(getenv("WL_PLAN_CTAS")) : kPlanCtasPerSm;
-  const int target = per_sm * num_sms;
+  const int target = kPlanCtasPerSm * num_sms;
   const int cmax = a.epi.kind == EPI_SWIGLU ? kMaxCluster / 2 : kMaxCluster;
-  int c = (target + groups - 1) / std::max(groups, 1);
+  // round down: every CTA resident in one wave
+  int c = target / std::max(groups, 1);
   c = std::max(1, std::min({c, cmax, units}));
   a.kchunk = (units + c - 1) / c * gran;
   a.csplit = (a.K + a.kchunk - 1) / a.kchunk;

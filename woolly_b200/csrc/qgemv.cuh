@@ -25,6 +25,7 @@ enum XKind : int {
   X_F32 = 1,
 };
 
+
 // Paged KV cache addressing for one layer: element (token j, kv head h, dim d)
 // of a session lives at page = table[sess][j / page], slot = j % page, in
 //   base[((page * kv_heads + h) * page_tokens + slot) * head_dim + d]
@@ -78,6 +79,7 @@ struct GemvArgs {
   int csplit = 1;  // CTAs per cluster splitting K (1..16)
   int kchunk = 0;  // rows of K per CTA (multiple of 16; of 256 for layout A)
   Epilogue epi;
+  int* err = nullptr;  // optional: bit 2 set when the cluster reduction wait gave up
 };
 
 // Host launchers (stream-ordered).  Return a wl_status.
@@ -94,6 +96,7 @@ bool qgemv_b_fast_ok(int type, int K, int N, int pitch, const void* W);
 bool qgemv_a_fast_ok(int type, int K, int N, int pitch, const void* W);
 // picks csplit / kchunk for a launch (fills the GPU)
 void qgemv_plan(GemvArgs& a, int layout, int num_sms);
+
 int qgemv_group_cols(int layout);
 
 }  // namespace wl
