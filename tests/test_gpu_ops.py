@@ -178,7 +178,7 @@ def test_quantized_matvec_q4_1_unsupported():
     assert e.value.code == _lib.WL_ERR_UNSUPPORTED
 
 
-@pytest.mark.parametrize("d", [64, 2048, 4096, 5120])
+@pytest.mark.parametrize("d", [64, 1030, 2048, 4096, 5120, 12288, 16384])
 def test_rmsnorm(d):
     rng = np.random.default_rng(d)
     x = rng.standard_normal((7, d)).astype(np.float32)

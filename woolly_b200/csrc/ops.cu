@@ -3,6 +3,7 @@
 #include <cuda_fp16.h>
 
 #include <cmath>
+#include <cstdint>
 #include <string>
 
 #include "common.h"
@@ -68,6 +69,63 @@ __global__ void __launch_bounds__(kNormThreads)
     float x1 = srow[c1], x2 = srow[c2];
     put_y(y, y_mode, y_plane, (size_t)r * dim + c1, x1 * cs - x2 * sn);
     put_y(y, y_mode, y_plane, (size_t)r * dim + c2, x1 * sn + x2 * cs);
+  }
+}
+
+// Same RMSNorm without rotation, one CTA per row with up to 1024 threads: each
+// thread keeps V4 float4 chunks of the row in registers (one read), the sum of
+// squares is reduced across the CTA, and the outputs are stored 4 at a time.
+template <int V4>
+__global__ void __launch_bounds__(1024) k_rmsnorm_v(const float* x, const float* w, int dim, float eps,
+                                                    void* y, int y_mode, size_t y_plane) {
+  __shared__ float sred[32];
+  pdl_wait();
+  pdl_trigger();
+  const int r = blockIdx.x, tid = threadIdx.x, nt = blockDim.x;
+  const int n4 = dim >> 2;
+  const float4* xr = reinterpret_cast<const float4*>(x + (size_t)r * dim);
+  float4 v[V4];
+  float ss = 0.f;
+#pragma unroll
+  for (int j = 0; j < V4; j++) {
+    const int i = tid + j * nt;
+    v[j] = i < n4 ? xr[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+    ss += v[j].x * v[j].x + v[j].y * v[j].y + v[j].z * v[j].z + v[j].w * v[j].w;
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+  if ((tid & 31) == 0) sred[tid >> 5] = ss;
+  __syncthreads();
+  if (tid < 32) {
+    float t = tid < (nt >> 5) ? sred[tid] : 0.f;
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) t += __shfl_xor_sync(0xffffffffu, t, off);
+    if (tid == 0) sred[0] = t;
+  }
+  __syncthreads();
+  const float rms = sqrtf(sred[0] / (float)dim + eps);
+  const float4* w4 = reinterpret_cast<const float4*>(w);
+#pragma unroll
+  for (int j = 0; j < V4; j++) {
+    const int i = tid + j * nt;
+    if (i >= n4) break;
+    const float4 wv = w4[i];
+    const float o[4] = {__fdiv_rn(v[j].x, rms) * wv.x, __fdiv_rn(v[j].y, rms) * wv.y,
+                        __fdiv_rn(v[j].z, rms) * wv.z, __fdiv_rn(v[j].w, rms) * wv.w};
+    const size_t at = (size_t)r * dim + 4 * (size_t)i;
+    if (y_mode == 0) {
+      reinterpret_cast<float4*>(y)[at >> 2] = make_float4(o[0], o[1], o[2], o[3]);
+    } else {
+      __half hi[4], lo[4];
+#pragma unroll
+      for (int q = 0; q < 4; q++) {
+        hi[q] = __float2half_rn(o[q]);
+        lo[q] = __float2half_rn(o[q] - __half2float(hi[q]));
+      }
+      __half* yh = reinterpret_cast<__half*>(y);
+      *reinterpret_cast<uint2*>(yh + at) = *reinterpret_cast<const uint2*>(hi);
+      if (y_mode == 2) *reinterpret_cast<uint2*>(yh + at + y_plane) = *reinterpret_cast<const uint2*>(lo);
+    }
   }
 }
 
@@ -154,6 +212,23 @@ int launch_rmsnorm(const float* x, const float* w, int rows, int dim, float eps,
                    const int* pos, int head_dim, float theta, void* y, int y_mode,
                    size_t y_plane, cudaStream_t st) {
   if (rows <= 0) return WL_OK;
+  // vector path: no rotation, dim % 4 == 0, aligned rows and (for planes) an 8-byte aligned lo plane
+  const bool vec_ok = !rope && dim % 4 == 0 && dim <= 16384 &&
+                      (reinterpret_cast<uintptr_t>(x) & 15) == 0 &&
+                      (reinterpret_cast<uintptr_t>(w) & 15) == 0 &&
+                      (reinterpret_cast<uintptr_t>(y) & 15) == 0 && (y_mode != 2 || y_plane % 4 == 0);
+  if (vec_ok) {
+    const int n4 = dim / 4;
+    const int v4 = (n4 + 1023) / 1024;
+    int nt = (n4 + v4 - 1) / v4;
+    nt = (nt + 31) / 32 * 32;
+    switch (v4) {
+      case 1: return launch_k(k_rmsnorm_v<1>, dim3(rows), dim3(nt), 0, st, x, w, dim, eps, y, y_mode, y_plane);
+      case 2: return launch_k(k_rmsnorm_v<2>, dim3(rows), dim3(nt), 0, st, x, w, dim, eps, y, y_mode, y_plane);
+      case 3: return launch_k(k_rmsnorm_v<3>, dim3(rows), dim3(nt), 0, st, x, w, dim, eps, y, y_mode, y_plane);
+      default: return launch_k(k_rmsnorm_v<4>, dim3(rows), dim3(nt), 0, st, x, w, dim, eps, y, y_mode, y_plane);
+    }
+  }
   size_t smem = rope ? (size_t)dim * sizeof(float) : 0;
   if (rope && (head_dim <= 0 || dim % head_dim || head_dim % 2))
     return fail(WL_ERR_INVALID_ARGUMENT, "rmsnorm_rope: dim must be a multiple of an even head_dim");
