@@ -31,7 +31,14 @@ namespace {
 
 constexpr int kAttnThreads = 128;
 constexpr int kPage = 16;    // tokens per KV page
-constexpr int kStagesA = 4;  // pages in flight per CTA
+#ifndef WL_ATTN_TILE_PAGES
+#define WL_ATTN_TILE_PAGES 2
+#endif
+#ifndef WL_ATTN_RING
+#define WL_ATTN_RING 3
+#endif
+constexpr int kTilePages = WL_ATTN_TILE_PAGES;  // pages per softmax round
+constexpr int kRingA = WL_ATTN_RING;            // tiles in flight per CTA
 constexpr int kTile = 64;    // tokens per softmax tile (f32 path)
 
 // ---------------------------------------------------------------- mbarrier / bulk copy
@@ -88,9 +95,10 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_paged(const AttnArgs a, f
   constexpr int NW = kAttnThreads / 32;
   constexpr int DP = HD / 2;
   constexpr int NS = kAttnThreads / DP;  // token streams in the V phase
-  extern __shared__ __align__(128) __half kvs[];  // [kStagesA][2][CHUNK]
-  __shared__ __align__(8) uint64_t bars[kStagesA];
-  __shared__ float s_p[G][kPage];
+  constexpr int TT = kTilePages * kPage;     // tokens per round
+  extern __shared__ __align__(128) __half kvs[];  // [kRingA][kTilePages][2][CHUNK]
+  __shared__ __align__(8) uint64_t bars[kRingA];
+  __shared__ float s_p[G][TT];
   __shared__ float s_m[G], s_l[G], s_alpha[G];
   __shared__ float s_red[NS][G][HD];
   __shared__ int s_fail;
@@ -108,24 +116,30 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_paged(const AttnArgs a, f
   const int pa = P0 + sp * pc;
   const int pb = min(P1 + 1, pa + pc);
   const int mine = pb > pa ? pb - pa : 0;
+  const int ntile = (mine + kTilePages - 1) / kTilePages;
   const int* table = a.kv.page_table + (size_t)sess * a.kv.max_pages;
 
-  auto issue = [&](int i) {  // page pa+i into stage i % kStagesA (thread 0 only)
-    const int st = i % kStagesA;
-    const int pg = table[pa + i];
-    const size_t off = ((size_t)pg * a.kv.kv_heads + kvh) * CHUNK;
-    mbar_expect_tx(&bars[st], 2 * CHUNK * 2);
-    bulk_g2s(kvs + (size_t)st * 2 * CHUNK, a.kv.k + off, CHUNK * 2, &bars[st]);
-    bulk_g2s(kvs + (size_t)st * 2 * CHUNK + CHUNK, a.kv.v + off, CHUNK * 2, &bars[st]);
+  auto issue = [&](int i) {  // tile i (pages pa + 4i ...) into ring slot i % kRingA (thread 0 only)
+    const int st = i % kRingA;
+    const int q0 = i * kTilePages;
+    const int n = min(kTilePages, mine - q0);
+    mbar_expect_tx(&bars[st], (unsigned)(n * 2 * CHUNK * 2));
+    for (int q = 0; q < n; q++) {
+      const int pg = table[pa + q0 + q];
+      const size_t off = ((size_t)pg * a.kv.kv_heads + kvh) * CHUNK;
+      __half* dst = kvs + ((size_t)st * kTilePages + q) * 2 * CHUNK;
+      bulk_g2s(dst, a.kv.k + off, CHUNK * 2, &bars[st]);
+      bulk_g2s(dst + CHUNK, a.kv.v + off, CHUNK * 2, &bars[st]);
+    }
   };
   if (tid == 0) {
-    for (int s = 0; s < kStagesA; s++) mbar_init(&bars[s], 1);
+    for (int s = 0; s < kRingA; s++) mbar_init(&bars[s], 1);
     asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
     s_fail = 0;
   }
   __syncthreads();
   if (tid == 0)
-    for (int i = 0; i < kStagesA && i < mine; i++) issue(i);
+    for (int i = 0; i < kRingA && i < ntile; i++) issue(i);
 
   const int sub = tid / LPT, li = tid % LPT;
   float qr[G][8];
@@ -142,29 +156,35 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_paged(const AttnArgs a, f
   for (int h = 0; h < G; h++) o[h][0] = o[h][1] = 0.f;
   __syncthreads();
 
-  for (int i = 0; i < mine; i++) {
-    const int st = i % kStagesA;
-    if (!mbar_wait(&bars[st], (unsigned)((i / kStagesA) & 1))) {
+  for (int i = 0; i < ntile; i++) {
+    const int st = i % kRingA;
+    if (!mbar_wait(&bars[st], (unsigned)((i / kRingA) & 1))) {
       if (a.err) atomicOr(a.err, 2);
       s_fail = 1;
     }
     __syncthreads();
     if (s_fail) break;
-    const __half* Ks = kvs + (size_t)st * 2 * CHUNK;
-    const __half* Vs = Ks + CHUNK;
-    const int tok0 = (pa + i) * kPage;
-#pragma unroll
-    for (int pass = 0; pass < kPage / TPP; pass++) {
+    const __half* T = kvs + (size_t)st * kTilePages * 2 * CHUNK;  // page q: K at q*2*CHUNK, V after
+    const int tok0 = (pa + i * kTilePages) * kPage;
+    const int tvalid = min(TT, (mine - i * kTilePages) * kPage);  // tokens of loaded pages
+#pragma unroll 4
+    for (int pass = 0; pass < TT / TPP; pass++) {
       const int tk = pass * TPP + sub;
       const int j = tok0 + tk;
-      const bool ok = j >= j0 && j <= pos;
-      const uint4 u = *reinterpret_cast<const uint4*>(Ks + tk * HD + li * 8);
-      const __half2* hh = reinterpret_cast<const __half2*>(&u);
+      const bool ok = tk < tvalid && j >= j0 && j <= pos;
       float kf[8];
+      if (tk < tvalid) {
+        const uint4 u = *reinterpret_cast<const uint4*>(T + (size_t)(tk / kPage) * 2 * CHUNK +
+                                                        (tk % kPage) * HD + li * 8);
+        const __half2* hh = reinterpret_cast<const __half2*>(&u);
 #pragma unroll
-      for (int q = 0; q < 4; q++) {
-        const float2 f = __half22float2(hh[q]);
-        kf[2 * q] = f.x, kf[2 * q + 1] = f.y;
+        for (int q = 0; q < 4; q++) {
+          const float2 f = __half22float2(hh[q]);
+          kf[2 * q] = f.x, kf[2 * q + 1] = f.y;
+        }
+      } else {
+#pragma unroll
+        for (int q = 0; q < 8; q++) kf[q] = 0.f;
       }
 #pragma unroll
       for (int h = 0; h < G; h++) {
@@ -178,18 +198,27 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_paged(const AttnArgs a, f
     }
     __syncthreads();
     for (int h = warp; h < G; h += NW) {
-      const float sv = lane < kPage ? s_p[h][lane] : -INFINITY;
-      float mx = sv;
+      constexpr int SV = (TT + 31) / 32;
+      float sv[SV];
+      float mx = -INFINITY;
+#pragma unroll
+      for (int q = 0; q < SV; q++) {
+        sv[q] = lane + 32 * q < TT ? s_p[h][lane + 32 * q] : -INFINITY;
+        mx = fmaxf(mx, sv[q]);
+      }
 #pragma unroll
       for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
       const float m_old = s_m[h];
       const float m_new = fmaxf(m_old, mx);
-      const float p = sv == -INFINITY ? 0.f : expf(sv - m_new);
-      float sum = p;
+      float sum = 0.f;
+#pragma unroll
+      for (int q = 0; q < SV; q++) {
+        const float p = sv[q] == -INFINITY ? 0.f : expf(sv[q] - m_new);
+        if (lane + 32 * q < TT) s_p[h][lane + 32 * q] = p;
+        sum += p;
+      }
 #pragma unroll
       for (int off = 16; off > 0; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
-      if (lane < kPage) s_p[h][lane] = p;
-      __syncwarp();
       if (lane == 0) {
         const float alpha = m_old == -INFINITY ? 0.f : expf(m_old - m_new);
         s_alpha[h] = alpha;
@@ -203,9 +232,11 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_paged(const AttnArgs a, f
       const float al = s_alpha[h];
       o[h][0] *= al, o[h][1] *= al;
     }
-#pragma unroll
-    for (int tk = stream; tk < kPage; tk += NS) {
-      const float2 vv = __half22float2(*reinterpret_cast<const __half2*>(Vs + tk * HD + 2 * dp));
+    // V rows of loaded pages only (tokens past tvalid were never copied)
+#pragma unroll 4
+    for (int tk = stream; tk < tvalid; tk += NS) {
+      const float2 vv = __half22float2(*reinterpret_cast<const __half2*>(
+          T + (size_t)(tk / kPage) * 2 * CHUNK + CHUNK + (tk % kPage) * HD + 2 * dp));
 #pragma unroll
       for (int h = 0; h < G; h++) {
         const float p = s_p[h][tk];
@@ -213,8 +244,8 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_paged(const AttnArgs a, f
         o[h][1] += p * vv.y;
       }
     }
-    __syncthreads();  // stage st fully consumed
-    if (tid == 0 && i + kStagesA < mine) issue(i + kStagesA);
+    __syncthreads();  // ring slot st fully consumed
+    if (tid == 0 && i + kRingA < ntile) issue(i + kRingA);
   }
 #pragma unroll
   for (int h = 0; h < G; h++) {
@@ -266,7 +297,7 @@ __global__ void k_attn_combine(const float* part_o, const float* part_ml, int he
 template <int HD, int G>
 int launch_paged_g(const AttnArgs& a, float scale, cudaStream_t st) {
   static unsigned done = 0;
-  const size_t smem = (size_t)kStagesA * 2 * kPage * HD * sizeof(__half);
+  const size_t smem = (size_t)kRingA * kTilePages * 2 * kPage * HD * sizeof(__half);
   int dev = 0;
   cudaGetDevice(&dev);
   if (!(done >> (dev & 31) & 1u)) {
