@@ -39,6 +39,30 @@ def model_options(**kw) -> _lib.ModelOptions:
     return o
 
 
+def nccl_communicator(rank: int, world: int, group=None) -> int:
+    """NCCL communicator for tensor parallelism across `world` ranks (one GPU
+    each; call after torch.cuda.set_device).  Rank 0 draws the unique id
+    (wl_nccl_unique_id) and the torch.distributed process group `group` (any
+    backend; the default group when None) shares it.  Returns the handle to
+    pass as CudaTransformer(..., tp_rank=rank, tp_size=world, nccl_comm=handle);
+    release it with nccl_destroy() after the model is closed.
+    """
+    import torch.distributed as dist
+    buf = (C.c_uint8 * 128)()
+    if rank == 0:
+        check(lib().wl_nccl_unique_id(buf))
+    obj = [bytes(buf)]
+    dist.broadcast_object_list(obj, src=0, group=group)
+    uid = (C.c_uint8 * 128).from_buffer_copy(obj[0])
+    comm = C.c_void_p()
+    check(lib().wl_nccl_comm_init(world, uid, rank, C.byref(comm)))
+    return comm.value
+
+
+def nccl_destroy(comm: int) -> None:
+    check(lib().wl_nccl_comm_destroy(C.c_void_p(comm)))
+
+
 class CudaTransformer:
     """Drop-in for LazyTransformer behind woolly's Model trait.
 
