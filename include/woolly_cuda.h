@@ -161,6 +161,17 @@ int wl_qgemv(int ggml_type, int layout, const void* W, int K, int N, const float
 int wl_qgemv_planes(int ggml_type, const void* W, int K, int N, const void* x_planes,
                     size_t x_plane, int B, float* y, void* stream);
 
+/* Quantized GEMM for prompts (prefill): y[m, o] = sum_k x[m, k] * W(k, o) for
+ * all M rows in one launch, layout B (W is [K][N] GGUF blocks), the
+ * woolly-core `matmul` over a whole sequence (tensor_utils.rs:118-157;
+ * Gemm::compute, woolly-tensor/src/ops/matmul.rs:83-259, is the reference's
+ * general GEMM entry).  x f32 [M][K], y f32 [M][N].  Runs on the tcgen05
+ * tensor cores when K % 64 == 0, N % 128 == 0 and the weight rows are 16-byte
+ * aligned (N/32 * block bytes % 16 == 0); other shapes take the layout-B GEMV
+ * path, 32 rows per launch.  Results within f32 rounding of the restatement. */
+int wl_qgemm(int ggml_type, const void* W, int K, int N, const float* x, int M, float* y,
+             void* stream);
+
 /* Allocation-free variant of wl_qgemv for layout B.  No counterpart in the
  * reference: it exists for callers that may not allocate device memory after
  * start-up (fixed-budget serving processes, hosts whose allocator belongs to

@@ -236,3 +236,39 @@ def test_attention_f32_vs_oracle(heads, kv_heads, hd, rows, past, window):
     got = ops.attention(dev(q), dev(k), dev(v), past=past, heads=heads, kv_heads=kv_heads,
                         head_dim=hd, window=window).cpu().numpy()
     assert np.allclose(got, ref, rtol=2e-5, atol=2e-5)
+
+
+# ---------------------------------------------------------------- prefill GEMM
+@pytest.mark.parametrize("qt", [Q4_0, Q4_1, Q8_0])
+@pytest.mark.parametrize("K,N,M", [(128, 128, 128), (256, 256, 200), (4096, 512, 512),
+                                   (1024, 384, 1), (2048, 1280, 129),
+                                   # GEMV fallback shapes (K % 64 or N % 128 != 0)
+                                   (96, 64, 40), (160, 96, 70)])
+def test_qgemm_vs_oracle(qt, K, N, M):
+    raw = quant_matrix(qt, K, N, seed=K + N + M + qt)
+    x = np.random.default_rng(M).standard_normal((M, K)).astype(np.float32)
+    y = ops.qgemm(dev(raw), qt, dev(x), N).cpu().numpy()
+    check_gemv(y, ref_gemv(qt, LAYOUT_B, raw, K, N, x))
+
+
+@pytest.mark.parametrize("qt", [Q4_0, Q8_0])
+def test_qgemm_sweep_shape_512_rows(qt):
+    """The sweep's GEMM case (M = 512) on the 7B FFN shape, against float64."""
+    K, N, M = 4096, 14336, 512
+    raw = quant_matrix(qt, K, N, seed=9)
+    W = dev(O.dequantize(raw.tobytes(), qt, K * N).astype(np.float32).reshape(K, N))
+    x = dev(np.random.default_rng(2).standard_normal((M, K)).astype(np.float32))
+    y = ops.qgemm(dev(raw), qt, x, N)
+    ref = (x.double() @ W.double()).cpu().numpy()
+    check_gemv(y.cpu().numpy(), ref)
+
+
+def test_qgemm_matches_gemv_rows():
+    """The tensor-core GEMM and the 32-row GEMV agree on the same rows."""
+    K, N, M = 2048, 1024, 96
+    raw = quant_matrix(Q4_0, K, N, seed=4)
+    x = dev(np.random.default_rng(8).standard_normal((M, K)).astype(np.float32))
+    a = ops.qgemm(dev(raw), Q4_0, x, N)
+    b = ops.qgemv(dev(raw), Q4_0, LAYOUT_B, x, N)
+    scale = b.abs().max().item()
+    assert (a - b).abs().max().item() <= 1e-5 * scale

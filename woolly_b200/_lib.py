@@ -120,6 +120,7 @@ _SIGS = {
     "wl_forward": (C.c_int, [P, C.POINTER(P), C.c_int, P, P, P, C.c_int]),
     "wl_decode_step_device": (C.c_int, [P, C.POINTER(P), C.c_int, P, P, P]),
     "wl_decode_kernel_count": (C.c_int, [P, C.c_int]),
+    "wl_qgemm": (C.c_int, [C.c_int, P, C.c_int, C.c_int, P, C.c_int, P, P]),
     "wl_nccl_unique_id": (C.c_int, [P]),
     "wl_nccl_comm_init": (C.c_int, [C.c_int, P, C.c_int, C.POINTER(P)]),
     "wl_nccl_comm_destroy": (C.c_int, [P]),

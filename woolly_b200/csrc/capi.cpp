@@ -287,6 +287,49 @@ int wl_qgemv_planes(int type, const void* W, int K, int N, const void* xp, size_
   return WL_OK;
 }
 
+// Prefill GEMM (tensor_utils.rs:118-157 over a whole sequence): tcgen05 tiles
+// when the shape allows, else the GEMV in 32-row launches.
+int wl_qgemm(int type, const void* W, int K, int N, const float* x, int M, float* y, void* stream) {
+  if (!W || !x || !y) return fail(WL_ERR_INVALID_ARGUMENT, "null pointer");
+  if (!bb(type)) return fail(WL_ERR_UNSUPPORTED, "qgemm: type must be Q4_0, Q4_1 or Q8_0");
+  if (K <= 0 || N <= 0 || M <= 0 || N % 32) return fail(WL_ERR_INVALID_ARGUMENT, "qgemm: bad shape");
+  cudaStream_t st = (cudaStream_t)stream;
+  const int pitch = N / 32 * bb(type);
+  const bool aligned = pitch % 16 == 0 && (reinterpret_cast<uintptr_t>(W) & 15) == 0;
+  if (!aligned || K % 16) return qgemv_op(type, WL_LAYOUT_B, (const uint8_t*)W, K, N, x, M, y, st);
+  GemvArgs a;
+  a.type = type;
+  a.nseg = 1;
+  a.seg[0].W = (const uint8_t*)W;
+  a.seg[0].N = N;
+  a.seg[0].pitch = pitch;
+  a.seg[0].groups = (N + 255) / 256;
+  a.K = K;
+  a.ldx = K;
+  a.xkind = X_PLANES;
+  a.x_plane = (size_t)M * K;
+  a.epi.kind = EPI_F32;
+  a.epi.y[0] = y;
+  a.epi.ldy[0] = N;
+  __half* planes = nullptr;
+  WL_CUDA_TRY(cudaMallocAsync((void**)&planes, (size_t)2 * M * K * sizeof(__half), st));
+  int s = launch_split_planes(x, planes, (size_t)M * K, (size_t)M * K, st);
+  a.x = planes;
+  if (!s && qgemm_b_ok(a, M)) {
+    s = launch_qgemm_b(a, M, st);
+  } else {
+    for (int r0 = 0; r0 < M && !s; r0 += 32) {
+      a.B = std::min(32, M - r0);
+      a.x = planes + (size_t)r0 * K;
+      a.epi.y[0] = y + (size_t)r0 * N;
+      qgemv_plan(a, WL_LAYOUT_B, sm_count());
+      s = launch_qgemv_b(a, st);
+    }
+  }
+  cudaFreeAsync(planes, st);
+  return s;
+}
+
 // quantization::simd::quantized_matvec (woolly-tensor/src/quantization.rs:869-909)
 int wl_quantized_matvec(int type, const void* W, const float* input, float* output, int m, int k,
                         void* stream) {

@@ -274,6 +274,8 @@ static int allreduce_sum(wl_model* m, float* buf, size_t count) {
 }
 
 // ------------------------------------------------------------------ GEMV dispatch
+// Rows from which a projection runs as one tcgen05 GEMM instead of 32-row GEMVs.
+constexpr int kGemmMinRows = 64;
 // rows r in [0, R) of x (f16 hi/lo planes, lo plane x_plane elements after
 // hi), up to 32 rows per launch.
 static int gemv(wl_model* m, int nseg, const QMat* mats, int R, const __half* x, size_t x_plane,
@@ -289,6 +291,26 @@ static int gemv(wl_model* m, int nseg, const QMat* mats, int R, const __half* x,
   const bool sw = epi.kind == EPI_SWIGLU;
   if (sw && (nseg != 2 || mats[0].N != mats[1].N))
     return fail(WL_ERR_INVALID_ARGUMENT, "SwiGLU GEMV needs gate and up of equal width");
+  // prompts: every row in one tensor-core GEMM launch when the shape allows
+  if (fast && R >= kGemmMinRows) {
+    GemvArgs a;
+    a.type = (int)mats[0].type;
+    a.nseg = nseg;
+    for (int s = 0; s < nseg; s++) {
+      a.seg[s].W = mats[s].w;
+      a.seg[s].N = mats[s].N;
+      a.seg[s].pitch = mats[s].pitch;
+    }
+    a.K = mats[0].K;
+    a.B = R;
+    a.xkind = X_PLANES;
+    a.x = x;
+    a.x_plane = x_plane;
+    a.ldx = ldx;
+    a.epi = epi;
+    a.err = m->err;
+    if (qgemm_b_ok(a, R)) return launch_qgemm_b(a, R, m->st);
+  }
   for (int r0 = 0; r0 < R; r0 += 32) {
     const int b = std::min(32, R - r0);
     Epilogue e = epi;

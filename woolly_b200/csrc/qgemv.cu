@@ -155,7 +155,6 @@ __device__ __forceinline__ void scale_split(uint32_t d, uint32_t xh, uint32_t xl
   lo = as_u(__hfma2(as_h2(d), as_h2(xl), r));
 }
 
-__device__ __forceinline__ float silu(float g) { return g * (1.0f / (1.0f + expf(-g))); }
 
 // Layout A: cp.async copies of one stage's f32 activation tile [BP][KC]; rows
 // >= B and columns >= k1 are zero-filled.
@@ -201,28 +200,7 @@ __device__ __forceinline__ unsigned long long gtime() {
 #define TL(i)
 #endif
 // ------------------------------------------------------------------ epilogue
-__device__ __forceinline__ void store_out(const GemvArgs& a, int seg, int b, int col, float v) {
-  const Epilogue& e = a.epi;
-  switch (e.kind) {
-    case EPI_F32:
-      reinterpret_cast<float*>(e.y[seg])[(size_t)b * e.ldy[seg] + col] = v;
-      break;
-    case EPI_ADD:
-      reinterpret_cast<float*>(e.y[seg])[(size_t)b * e.ldy[seg] + col] += v;
-      break;
-    case EPI_QKV:
-      if (seg == 0) {
-        reinterpret_cast<float*>(e.y[0])[(size_t)b * e.ldy[0] + col] = v;
-      } else {
-        const int p = e.row_pos[b];
-        const int pg = e.kv.page_table[(size_t)e.row_sess[b] * e.kv.max_pages + p / e.kv.page];
-        const size_t off =
-            kv_offset(e.kv, pg, p % e.kv.page, col / e.kv.head_dim, col % e.kv.head_dim);
-        (seg == 1 ? e.kv.k : e.kv.v)[off] = __float2half_rn(v);
-      }
-      break;
-  }
-}
+// store_out (qgemv.cuh) applies F32 / ADD / QKV outputs per element.
 
 // Cluster split-K reduction by push.  The output tile of a CTA (B rows x
 // `cols` columns, ncv valid) is cut into float4 groups; group q of every CTA

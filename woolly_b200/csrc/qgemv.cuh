@@ -82,6 +82,43 @@ struct GemvArgs {
   int* err = nullptr;  // optional: bit 2 set when the cluster reduction wait gave up
 };
 
+#ifdef __CUDACC__
+// swiglu activation (tensor_utils.rs:512-532): silu(g) = g * (1 / (1 + exp(-g)))
+__device__ __forceinline__ float silu(float g) { return g * (1.0f / (1.0f + expf(-g))); }
+
+// One output element of segment `seg`, launch row b, segment column col:
+// F32 store, residual ADD, or the QKV split (q as f32; k and v as f16 into the
+// row's KV page).
+__device__ __forceinline__ void store_out(const GemvArgs& a, int seg, int b, int col, float v) {
+  const Epilogue& e = a.epi;
+  switch (e.kind) {
+    case EPI_F32:
+      reinterpret_cast<float*>(e.y[seg])[(size_t)b * e.ldy[seg] + col] = v;
+      break;
+    case EPI_ADD:
+      reinterpret_cast<float*>(e.y[seg])[(size_t)b * e.ldy[seg] + col] += v;
+      break;
+    case EPI_QKV:
+      if (seg == 0) {
+        reinterpret_cast<float*>(e.y[0])[(size_t)b * e.ldy[0] + col] = v;
+      } else {
+        const int p = e.row_pos[b];
+        const int pg = e.kv.page_table[(size_t)e.row_sess[b] * e.kv.max_pages + p / e.kv.page];
+        const size_t off =
+            kv_offset(e.kv, pg, p % e.kv.page, col / e.kv.head_dim, col % e.kv.head_dim);
+        (seg == 1 ? e.kv.k : e.kv.v)[off] = __float2half_rn(v);
+      }
+      break;
+  }
+}
+#endif
+
+// Prefill GEMM on tcgen05 tensor cores (qgemm.cu): all M rows of x (f16 hi/lo
+// planes, a.ldx % 8 == 0) against layout-B weights in one launch.  Needs
+// K % 64 == 0 and every segment's N % 128 == 0 (SwiGLU: N % 64 == 0); rope off.
+bool qgemm_b_ok(const GemvArgs& a, int M);
+int launch_qgemm_b(const GemvArgs& a, int M, cudaStream_t st);
+
 // Host launchers (stream-ordered).  Return a wl_status.
 int launch_qgemv_b(const GemvArgs& a, cudaStream_t st);
 int launch_qgemv_a(const GemvArgs& a, cudaStream_t st);

@@ -58,6 +58,19 @@ def qgemv(weights: torch.Tensor, ggml_type: int, layout: int, x: torch.Tensor, n
     return y.reshape(*x.shape[:-1], n)
 
 
+def qgemm(weights: torch.Tensor, ggml_type: int, x: torch.Tensor, n: int) -> torch.Tensor:
+    """Prefill GEMM y[m, :] = x[m, :] @ W for layout-B W ([K][N] GGUF blocks),
+    all rows in one call (tcgen05 tensor cores where the shape allows)."""
+    _dev(weights, torch.uint8, "weights")
+    _dev(x, torch.float32, "x")
+    x2 = x.reshape(-1, x.shape[-1])
+    M, K = x2.shape
+    y = torch.empty(M, n, dtype=torch.float32, device=x.device)
+    check(lib().wl_qgemm(int(ggml_type), weights.data_ptr(), K, n, x2.data_ptr(), M, y.data_ptr(),
+                         _stream()))
+    return y.reshape(*x.shape[:-1], n)
+
+
 def split_planes(x: torch.Tensor) -> torch.Tensor:
     """f32 [B, K] -> f16 [2, B, K]: hi = f16(x), lo = f16(x - hi)."""
     hi = x.to(torch.float16)
