@@ -256,6 +256,92 @@ def gemv_roofline(torch, dev, reps=24):
     return tot_bytes / tot_ms / 1e6, res
 
 
+SWEEP_SHAPES = [(4096, 4096), (4096, 14336), (14336, 4096)]
+
+
+def _rand_blocks(torch, dev, qt, K, N, copies):
+    """Random GGUF blocks with finite, realistic scales (d ~ 0.0078; Q4_1 m too)."""
+    S = {2: 18, 3: 20, 8: 34}[qt]
+    nbytes = K * N // 32 * S
+    ws = []
+    for _ in range(copies):
+        w = torch.randint(0, 256, (nbytes,), dtype=torch.uint8, device=dev)
+        v = w.view(-1, S)
+        v[:, 0] = 0
+        v[:, 1] = 0x20
+        if qt == 3:
+            v[:, 2] = 0
+            v[:, 3] = 0xA0  # m ~ -0.0078
+        ws.append(w)
+    return ws, nbytes
+
+
+def _graph_time(torch, dev, fn, reps):
+    s = torch.cuda.Stream(dev)
+    with torch.cuda.stream(s):
+        for i in range(3):
+            fn(i)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=s):
+        for i in range(reps):
+            fn(i)
+    g.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(s):
+        e0.record(s)
+        g.replay()
+        e1.record(s)
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / reps
+
+
+def gemv_gemm_sweep(torch, dev, hbm_peak, tc_peak):
+    """The standalone sweep: layout-B GEMV for Q4_0/Q4_1/Q8_0 x three shapes x
+    B in {1, 4, 16} (weights rotated over copies > 4x L2, CUDA-graph timed;
+    GB/s of algorithmic bytes and fraction of the measured HBM peak), and the
+    tcgen05 prefill GEMM at M = 512 (useful TFLOP/s = 2*M*K*N / time, and the
+    fraction of the measured bf16 dense peak it issues with its 3 exact MMAs)."""
+    from woolly_b200 import ops
+    out = {"gemv_layout_b": {}, "gemm_m512": {}}
+    for qt, name in ((2, "q4_0"), (3, "q4_1"), (8, "q8_0")):
+        for K, N in SWEEP_SHAPES:
+            ws, nbytes = _rand_blocks(torch, dev, qt, K, N, 2)
+            copies = max(2, int(600e6 // nbytes) + 1)
+            ws += _rand_blocks(torch, dev, qt, K, N, copies - 2)[0]
+            for B in (1, 4, 16):
+                planes = ops.split_planes(torch.randn(B, K, device=dev))
+                y = torch.empty(B, N, device=dev)
+                ms = _graph_time(torch, dev, lambda i: ops.qgemv_planes(ws[i % copies], qt, planes, N, out=y), 24)
+                alg = nbytes + 4 * B * (K + N)
+                gbs = alg / ms / 1e6
+                out["gemv_layout_b"][f"{name} {K}x{N} B={B}"] = {
+                    "us": round(ms * 1e3, 2), "GBps": round(gbs, 1), "frac": round(gbs / hbm_peak, 3)}
+            del ws
+        if qt != 2:
+            continue
+        for K, N in SWEEP_SHAPES:
+            ws, _ = _rand_blocks(torch, dev, qt, K, N, 1)
+            x = torch.randn(512, K, device=dev)
+            for _ in range(3):
+                ops.qgemm(ws[0], qt, x, N)
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(10):
+                ops.qgemm(ws[0], qt, x, N)
+            e1.record()
+            torch.cuda.synchronize()
+            ms = e0.elapsed_time(e1) / 10
+            tf = 2 * 512 * K * N / ms / 1e9
+            out["gemm_m512"][f"{name} {K}x{N}"] = {
+                "us": round(ms * 1e3, 1), "TFLOPs_useful": round(tf, 1),
+                "issued_frac_of_bf16_peak": round(3 * tf / tc_peak, 3) if tc_peak else None}
+            del ws
+    return out
+
+
 def run_gpu(args):
     import torch
     ws, rank, local = dist_init()
@@ -341,6 +427,14 @@ def run_gpu(args):
 
     # ---- dominant kernel: the layout-B Q4_0 GEMV ----
     achieved, per_shape = gemv_roofline(torch, dev)
+    sweep = None
+    if not args.no_sweep and rank == 0:
+        try:
+            with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+                tc_peak = float(json.load(f)["bf16_tflops"])
+        except Exception:
+            tc_peak = 1590.0
+        sweep = gemv_gemm_sweep(torch, dev, hbm_peak, tc_peak)
     traffic = None  # dram bytes per launch, scaled from the committed ncu capture
     try:
         with open(os.path.join(ROOT, "profiles", "qgemv_b_q4_0_7b_decode.json")) as f:
@@ -373,6 +467,8 @@ def run_gpu(args):
             "clocks": clocks,
             "gpu_launches": launches,
         }
+        if sweep is not None:
+            line["sweep"] = sweep
         if not args.no_cpu_baseline and ws == 1:
             line["cpu_baseline"] = cpu_baseline(path)
         print(json.dumps(line), flush=True)
@@ -390,6 +486,7 @@ def main():
     ap.add_argument("--bs1-steps", type=int, default=64)
     ap.add_argument("--impl", default="woolly_b200", choices=["woolly_b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-sweep", action="store_true", help="skip the GEMV/GEMM shape sweep")
     ap.add_argument("--tmpdir", default=os.environ.get("WOOLLY_BENCH_DIR", "/tmp/woolly_bench"))
     args = ap.parse_args()
     if args.warmup < 3:

@@ -38,7 +38,7 @@ constexpr int kGN = 128;  // weight columns per CTA (MMA M)
 constexpr int kGM = 128;  // token rows per CTA (MMA N)
 constexpr int kGK = 64;   // k rows per stage (one 128-byte swizzle row of f16)
 constexpr int kGStages = 3;
-constexpr int kGThreads = 256;
+constexpr int kGThreads = 512;  // 16 warps: two per quant block of each k row
 constexpr int kGTile = 128 * kGK * 2;  // bytes of one f16 operand tile (16 KB)
 constexpr int kGStage = 4 * kGTile;    // W hi, W lo, X hi, X lo
 constexpr int kGSmem = kGStages * kGStage + 1024 + 64;  // + alignment slack + barriers
@@ -114,35 +114,51 @@ __device__ __forceinline__ void split_pair(uint32_t q, __half2 d2, uint32_t& hi,
   lo = h2u(__hfma2(u2h(q), d2, __hneg2(h)));
 }
 
-// One quant block's bytes held in registers as 16-bit words (blocks are only
-// 2-byte aligned in a layout-B row): Q4_0 9 words, Q4_1 10, Q8_0 17.
+// Half a quant block's bytes held in registers as 16-bit words (blocks are only
+// 2-byte aligned in a layout-B row): the scale (Q4_1: and min) plus the code
+// words of the half.  Q4_0 / Q4_1 half p holds code bytes 8p..8p+7 (columns
+// 8p..8p+7 and 16+8p..23+8p); Q8_0 half p holds codes 16p..16p+15.
 template <int T>
 struct RawBlock {
-  static constexpr int W = T == WL_Q4_0 ? 9 : T == WL_Q4_1 ? 10 : 17;
-  uint16_t w[W];
+  static constexpr int HDR = T == WL_Q4_1 ? 2 : 1;  // words before the codes
+  static constexpr int CW = T == WL_Q8_0 ? 8 : 4;   // code words per half
+  uint16_t w[HDR + CW];
 };
 template <int T>
-__device__ __forceinline__ void raw_load(RawBlock<T>& r, const uint8_t* blk, bool live) {
+__device__ __forceinline__ void raw_load(RawBlock<T>& r, const uint8_t* blk, int part, bool live) {
+  using R = RawBlock<T>;
+  const unsigned short* p = reinterpret_cast<const unsigned short*>(blk);
 #pragma unroll
-  for (int i = 0; i < RawBlock<T>::W; i++)
-    r.w[i] = live ? __ldg(reinterpret_cast<const unsigned short*>(blk) + i) : (unsigned short)0;
+  for (int i = 0; i < R::HDR; i++) r.w[i] = live ? __ldg(p + i) : (unsigned short)0;
+#pragma unroll
+  for (int i = 0; i < R::CW; i++) r.w[R::HDR + i] = live ? __ldg(p + R::HDR + part * R::CW + i) : (unsigned short)0;
 }
 
-// Dequantizes one quant block (32 columns) of k row `kk` of the stage into the
-// hi and lo tiles: columns b*32 .. b*32+31 of the tile.
+// Dequantizes half (`part`) of one quant block (16 of its 32 columns) of k row
+// `kk` of the stage into the hi and lo tiles; the block is columns b*32.. of
+// the tile.
 template <int T>
-__device__ __forceinline__ void dequant_block(const RawBlock<T>& raw, uint8_t* whi, uint8_t* wlo,
-                                              int kk, int b, bool live) {
-  uint32_t hi[16], lo[16];  // 16 column pairs (c, c+1)
+__device__ __forceinline__ void dequant_half(const RawBlock<T>& raw, uint8_t* whi, uint8_t* wlo,
+                                             int kk, int b, int part, bool live) {
+  constexpr int H = RawBlock<T>::HDR;
+  uint32_t hi[8], lo[8];  // two 8-column chunks: pairs 0-3 -> chunk A, 4-7 -> chunk B
+  int chA, chB;           // chunk indices (8 columns each) within the block
+  if constexpr (T == WL_Q8_0) {
+    chA = 2 * part;
+    chB = 2 * part + 1;
+  } else {
+    chA = part;      // low nibbles: columns 8p..8p+7
+    chB = 2 + part;  // high nibbles: columns 16+8p..
+  }
   if (!live) {
 #pragma unroll
-    for (int j = 0; j < 16; j++) hi[j] = lo[j] = 0u;
+    for (int j = 0; j < 8; j++) hi[j] = lo[j] = 0u;
   } else if constexpr (T == WL_Q4_1) {
     const float d = __half2float(__ushort_as_half(raw.w[0]));
     const float m = __half2float(__ushort_as_half(raw.w[1]));
 #pragma unroll
-    for (int j = 0; j < 8; j++) {
-      const uint32_t w = raw.w[2 + j];  // bytes 2j, 2j+1 of qs
+    for (int j = 0; j < 4; j++) {
+      const uint32_t w = raw.w[H + j];
       const float q[4] = {(float)(w & 15u), (float)((w >> 8) & 15u), (float)((w >> 4) & 15u),
                           (float)((w >> 12) & 15u)};
       __half hh[4], hl[4];
@@ -154,15 +170,15 @@ __device__ __forceinline__ void dequant_block(const RawBlock<T>& raw, uint8_t* w
       }
       hi[j] = h2u(__halves2half2(hh[0], hh[1]));
       lo[j] = h2u(__halves2half2(hl[0], hl[1]));
-      hi[8 + j] = h2u(__halves2half2(hh[2], hh[3]));
-      lo[8 + j] = h2u(__halves2half2(hl[2], hl[3]));
+      hi[4 + j] = h2u(__halves2half2(hh[2], hh[3]));
+      lo[4 + j] = h2u(__halves2half2(hl[2], hl[3]));
     }
   } else if constexpr (T == WL_Q8_0) {
     const __half dh = __ushort_as_half(raw.w[0]);
     const __half2 d2 = __halves2half2(dh, dh);
 #pragma unroll
-    for (int j = 0; j < 16; j++) {
-      const uint32_t w = raw.w[1 + j];  // codes of columns 2j, 2j+1
+    for (int j = 0; j < 8; j++) {
+      const uint32_t w = raw.w[H + j];  // codes of columns 16p+2j, 16p+2j+1
       const uint32_t v = ((w & 0xFFu) | ((w & 0xFF00u) << 8)) ^ 0x00800080u;
       const uint32_t q = h2u(__hsub2(u2h(v | 0x64006400u), u2h(0x64806480u)));  // exact int8
       split_pair(q, d2, hi[j], lo[j]);
@@ -171,28 +187,26 @@ __device__ __forceinline__ void dequant_block(const RawBlock<T>& raw, uint8_t* w
     const __half dh = __ushort_as_half(raw.w[0]);
     const __half2 d2 = __halves2half2(dh, dh);
 #pragma unroll
-    for (int j = 0; j < 8; j++) {
-      const uint32_t w = raw.w[1 + j];                                     // bytes 2j, 2j+1
-      const uint32_t lo_n = (w & 0x000Fu) | ((w & 0x0F00u) << 8);         // columns 2j, 2j+1
-      const uint32_t hi_n = ((w & 0x00F0u) >> 4) | ((w & 0xF000u) << 4);  // columns 16+2j, 17+2j
+    for (int j = 0; j < 4; j++) {
+      const uint32_t w = raw.w[H + j];                                     // bytes 8p+2j, +1
+      const uint32_t lo_n = (w & 0x000Fu) | ((w & 0x0F00u) << 8);         // low nibbles
+      const uint32_t hi_n = ((w & 0x00F0u) >> 4) | ((w & 0xF000u) << 4);  // high nibbles
       const uint32_t qa = h2u(__hsub2(u2h(lo_n | 0x64006400u), u2h(0x64086408u)));
       const uint32_t qb = h2u(__hsub2(u2h(hi_n | 0x64006400u), u2h(0x64086408u)));
       split_pair(qa, d2, hi[j], lo[j]);
-      split_pair(qb, d2, hi[8 + j], lo[8 + j]);
+      split_pair(qb, d2, hi[4 + j], lo[4 + j]);
     }
   }
   // column c of the tile: 64-column block jb = c / 64, 16-byte chunk c8 = (c % 64) / 8;
   // N-major 128B-swizzled atom (k group g = kk / 8, jb) holds 8 k rows of 128 bytes
   const int g = kk >> 3, r = kk & 7;
 #pragma unroll
-  for (int ch = 0; ch < 4; ch++) {
-    const int c = b * 32 + ch * 8;
+  for (int q = 0; q < 2; q++) {
+    const int c = b * 32 + (q ? chB : chA) * 8;
     const int jb = c >> 6, c8 = (c & 63) >> 3;
     const uint32_t off = (uint32_t)(((g * 2 + jb) << 10) + (r << 7) + ((c8 ^ r) << 4));
-    *reinterpret_cast<uint4*>(whi + off) =
-        make_uint4(hi[ch * 4], hi[ch * 4 + 1], hi[ch * 4 + 2], hi[ch * 4 + 3]);
-    *reinterpret_cast<uint4*>(wlo + off) =
-        make_uint4(lo[ch * 4], lo[ch * 4 + 1], lo[ch * 4 + 2], lo[ch * 4 + 3]);
+    *reinterpret_cast<uint4*>(whi + off) = make_uint4(hi[q * 4], hi[q * 4 + 1], hi[q * 4 + 2], hi[q * 4 + 3]);
+    *reinterpret_cast<uint4*>(wlo + off) = make_uint4(lo[q * 4], lo[q * 4 + 1], lo[q * 4 + 2], lo[q * 4 + 3]);
   }
 }
 
@@ -254,25 +268,33 @@ __global__ void __launch_bounds__(kGThreads, 1) k_qgemm_b(const GemvArgs a, int 
 
   const int nk = a.K / kGK;
   const __half* x = reinterpret_cast<const __half*>(a.x);
-  // dequant task of this thread: k row kk of the stage, quant block b of the tile
-  const int kk = tid >> 2, b = tid & 3;
+  // dequant task of this thread: half `part` of quant block b of the tile, k row kk
+  const int kk = tid >> 3, b = (tid >> 1) & 3, part = tid & 1;
   const GemvSeg& ws = a.seg[sw ? (b >> 1) : seg];
   const int col0 = sw ? n0 + (b & 1) * 32 : n0 + b * 32;  // first column of the block in its segment
   const bool wlive = col0 < ws.N;
   const uint8_t* wsrc = ws.W + (size_t)(col0 / 32) * S;
 
-  // activations of stage `it` into ring slot it % kGStages (K-major, 128B swizzle)
+  // activations of stage `it` into ring slot it % kGStages (K-major, 128B swizzle):
+  // this thread copies chunk c of rows rr0 + 32q (q < 4) of both planes; the
+  // swizzled destination and the source row offsets do not change per stage
+  const int xc = tid & 7, xr0 = tid >> 3;  // rows xr0, xr0 + 64
+  uint32_t xdst[4];
+  const __half* xsrc[4];
+  bool xok[4];
+#pragma unroll
+  for (int q = 0; q < 4; q++) {
+    const int pl = q >> 1, rr = xr0 + (q & 1) * 64;
+    xok[q] = m0 + rr < M;
+    xdst[q] = (uint32_t)((2 + pl) * kGTile + (rr << 7) + ((xc ^ (rr & 7)) << 4));
+    xsrc[q] = x + (size_t)pl * a.x_plane + (size_t)(xok[q] ? m0 + rr : 0) * a.ldx + xc * 8;
+  }
+  const uint32_t smb = smem_addr(sm);
   auto load_x = [&](int it) {
-    uint8_t* st = sm + (it % kGStages) * kGStage;
+    const uint32_t st = smb + (uint32_t)((it % kGStages) * kGStage);
     const int k0 = it * kGK;
 #pragma unroll
-    for (int q = 0; q < 8; q++) {
-      const int i = tid + q * kGThreads;
-      const int pl = i >> 10, rr = (i & 1023) >> 3, c = i & 7;
-      const bool ok = m0 + rr < M;
-      const __half* src = x + (size_t)pl * a.x_plane + (size_t)(ok ? m0 + rr : 0) * a.ldx + k0 + c * 8;
-      cp16(smem_addr(st + (2 + pl) * kGTile + (rr << 7) + ((c ^ (rr & 7)) << 4)), src, ok);
-    }
+    for (int q = 0; q < 4; q++) cp16(st + xdst[q], xsrc[q] + k0, xok[q]);
     asm volatile("cp.async.commit_group;\n" ::: "memory");
   };
   // waits until the MMAs that last read ring slot (it % kGStages) are done (uniform result)
@@ -284,9 +306,11 @@ __global__ void __launch_bounds__(kGThreads, 1) k_qgemm_b(const GemvArgs a, int 
     return !bad;
   };
 
-  RawBlock<T> cur, nxt;
+  // raw weight words run two stages ahead of the dequantization
+  RawBlock<T> r0, r1, r2;
   load_x(0);
-  raw_load<T>(cur, wsrc + (size_t)kk * ws.pitch, wlive);
+  raw_load<T>(r0, wsrc + (size_t)kk * ws.pitch, part, wlive);
+  if (nk > 1) raw_load<T>(r1, wsrc + (size_t)(kGK + kk) * ws.pitch, part, wlive);
   for (int it = 0; it < nk; it++) {
     const int s = it % kGStages;
     uint8_t* st = sm + s * kGStage;
@@ -297,9 +321,9 @@ __global__ void __launch_bounds__(kGThreads, 1) k_qgemm_b(const GemvArgs a, int 
         break;
       }
       load_x(it + 1);
-      raw_load<T>(nxt, wsrc + (size_t)((it + 1) * kGK + kk) * ws.pitch, wlive);
     }
-    dequant_block<T>(cur, st, st + kGTile, kk, b, wlive);
+    if (it + 2 < nk) raw_load<T>(r2, wsrc + (size_t)((it + 2) * kGK + kk) * ws.pitch, part, wlive);
+    dequant_half<T>(r0, st, st + kGTile, kk, b, part, wlive);
     if (more)
       asm volatile("cp.async.wait_group 1;\n" ::: "memory");
     else
@@ -325,7 +349,8 @@ __global__ void __launch_bounds__(kGThreads, 1) k_qgemm_b(const GemvArgs a, int 
       umma_commit(smem_addr(bars + s));
       s_issued = it + 1;
     }
-    cur = nxt;
+    r0 = r1;
+    r1 = r2;
   }
   asm volatile("cp.async.wait_group 0;\n" ::: "memory");
   // wait for the last issued commit (it covers every MMA issued before it); after
