@@ -137,8 +137,12 @@ int wl_synth_normal(uint64_t seed, uint64_t stream, float mean, float std, size_
 /* Device ops (stream-ordered, device pointers).                       */
 
 /* woolly_gguf::dequantize (woolly-gguf/src/dequantize.rs:189-205) for F32,
- * F16, Q4_0, Q4_1, Q8_0; bit-exact with the reference.  `nbytes` is the size
- * of `blocks` (BufferTooSmall semantics as the reference). */
+ * F16, Q4_0, Q4_1, Q8_0 and the K-quants Q4_K / Q6_K (the reference's own
+ * formulas, :381-537), bit-exact with the reference; Q5_0, Q5_1, Q5_K and
+ * Q8_K yield zeros as the reference's stubs do (:539-551, :595-607).
+ * `nbytes` is the size of `blocks` (BufferTooSmall semantics as the
+ * reference; a short Q4_K / Q6_K buffer is WL_ERR_INVALID_FORMAT, its
+ * InvalidTensorInfo). */
 int wl_dequantize(int ggml_type, const void* blocks, size_t nbytes, size_t n, float* out,
                   void* stream);
 

@@ -155,6 +155,57 @@ int or_dequantize(const uint8_t* data, size_t len, int type, size_t n, float* ou
       }
       return OR_OK;
     }
+    case 12: { /* Q4_K, dequantize.rs:381-462 (the scalar path the x86 build runs) */
+      size_t nbk = (n + 255) / 256;
+      if (len < nbk * 144) return OR_ERR_INVALID; /* InvalidTensorInfo("Q4_K data too small") */
+      size_t o = 0;
+      for (size_t b = 0; b < nbk; b++) {
+        const uint8_t* blk = data + b * 144;
+        uint8_t sc[8];
+        for (int i = 0; i < 8; i++) { /* 8 six-bit scales from the first 12 bytes */
+          int src = (i * 3) / 2;
+          sc[i] = (i % 2 == 0) ? (uint8_t)(blk[src] & 63)
+                               : (uint8_t)(((blk[src] >> 6) | ((blk[src + 1] & 15) << 2)) & 63);
+        }
+        float d = or_half_to_float(rd16(blk + 12));
+        float dmin = or_half_to_float(rd16(blk + 14));
+        const uint8_t* qs = blk + 16;
+        for (int i = 0; i < 256 && o < n; i++) {
+          int q = (i % 2 == 0) ? (qs[i / 2] & 0x0F) : ((qs[i / 2] >> 4) & 0x0F);
+          float t = d * (float)sc[i / 32];
+          t = t * (float)q;
+          out[o++] = t + dmin;
+        }
+      }
+      return OR_OK;
+    }
+    case 14: { /* Q6_K, dequantize.rs:465-537 */
+      size_t nbk = (n + 255) / 256;
+      if (len < nbk * 210) return OR_ERR_INVALID; /* InvalidTensorInfo("Q6_K data too small") */
+      size_t o = 0;
+      for (size_t b = 0; b < nbk; b++) {
+        const uint8_t* blk = data + b * 210;
+        const uint8_t *ql = blk, *qh = blk + 128, *scales = blk + 192;
+        float d = or_half_to_float(rd16(blk + 208));
+        for (int i = 0; i < 256 && o < n; i++) {
+          int is = i / 16;
+          int ql_idx = 64 * (i / 128) + 32 * ((i % 128) / 64) + 16 * ((i % 64) / 32) + (i % 16);
+          int qh_idx = 32 * (i / 128) + 16 * ((i % 128) / 64) + 8 * ((i % 64) / 32) + (i % 32) / 4;
+          int qh_shift = 2 * ((i % 32) % 4);
+          uint8_t qh_val = qh[qh_idx];
+          uint8_t q1_ext = (qh_val >> qh_shift) & 3;
+          uint8_t q2_ext = qh_shift < 6 ? (uint8_t)((qh_val >> (qh_shift + 2)) & 3)
+                                        : (uint8_t)(qh_idx + 1 < 64 ? (qh[qh_idx + 1] & 3) : 0);
+          uint8_t q1 = (uint8_t)((ql[ql_idx] & 0x0F) | (q1_ext << 4));
+          uint8_t q2 = (uint8_t)((ql[ql_idx] >> 4) | (q2_ext << 4));
+          uint8_t q = i < 128 ? q1 : q2;
+          float t = d * (float)scales[is];
+          t = t * (float)((int8_t)q - 32);
+          out[o++] = t / 64.0f;
+        }
+      }
+      return OR_OK;
+    }
     case 6: case 7: case 13: case 15: /* Q5_0/Q5_1/Q5_K/Q8_K: zero stubs (:539-551,:595-607) */
       memset(out, 0, n * sizeof(float));
       return OR_OK;

@@ -272,3 +272,35 @@ def test_qgemm_matches_gemv_rows():
     b = ops.qgemv(dev(raw), Q4_0, LAYOUT_B, x, N)
     scale = b.abs().max().item()
     assert (a - b).abs().max().item() <= 1e-5 * scale
+
+
+# ---------------------------------------------------------------- K-quant dequant
+def _k_blocks(qt, nb, seed):
+    rng = np.random.default_rng(seed)
+    S = 144 if qt == 12 else 210
+    raw = rng.integers(0, 256, size=(nb, S), dtype=np.uint8)
+    d = rng.choice(np.array([0.0123, -0.5, 3e-5, 1.0, 2.0], np.float16), (nb, 2))
+    if qt == 12:
+        raw[:, 12:16] = d.view(np.uint8).reshape(nb, 4)
+    else:
+        raw[:, 208:210] = d[:, :1].view(np.uint8).reshape(nb, 2)
+    return raw.reshape(-1)
+
+
+@pytest.mark.parametrize("qt", [12, 14])  # Q4_K, Q6_K
+def test_k_quant_dequant_bit_exact(qt):
+    nb = 4000
+    raw = _k_blocks(qt, nb, qt)
+    n = nb * 256 - 77
+    ref = O.dequantize(raw.tobytes(), qt, n)
+    got = ops.dequantize(dev(raw), qt, n).cpu().numpy()
+    assert np.array_equal(got.view(np.uint32), ref.view(np.uint32))
+
+
+def test_k_quant_short_buffer_and_stubs():
+    with pytest.raises(WoollyError) as e:
+        ops.dequantize(dev(np.zeros(143, np.uint8)), 12, 256)
+    assert e.value.code == _lib.WL_ERR_INVALID_FORMAT
+    for qt in (6, 7, 13, 15):  # Q5_0, Q5_1, Q5_K, Q8_K: zeros as the reference's stubs
+        out = ops.dequantize(dev(np.full(400, 7, np.uint8)), qt, 256)
+        assert not out.any().item()

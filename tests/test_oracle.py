@@ -145,3 +145,89 @@ def test_kat_fixture_file():
     for k in kats["dequant"]:
         out = O.dequantize(bytes.fromhex(k["hex"]), k["type"], k["n"])
         assert out.tolist() == k["expect"], k["source"]
+
+
+# ---------------------------------------------------------------- K-quants
+# The reference's own woolly_gguf::dequantize formulas for Q4_K and Q6_K
+# (crates/woolly-gguf/src/dequantize.rs:404-462, :465-537), transcribed here a
+# second time in plain Python float32 arithmetic, independently of oracle.c.
+Q4_K, Q5_K, Q6_K, Q8_K = 12, 13, 14, 15
+F32 = np.float32
+
+
+def py_q4_k(block: bytes, n: int) -> list:
+    sc = []
+    for i in range(8):
+        src = (i * 3) // 2
+        if i % 2 == 0:
+            sc.append(block[src] & 63)
+        else:
+            sc.append(((block[src] >> 6) | ((block[src + 1] & 15) << 2)) & 63)
+    d = F32(np.frombuffer(block[12:14], np.float16)[0])
+    dmin = F32(np.frombuffer(block[14:16], np.float16)[0])
+    out = []
+    for i in range(min(n, 256)):
+        q = block[16 + i // 2] & 0x0F if i % 2 == 0 else (block[16 + i // 2] >> 4) & 0x0F
+        out.append(d * F32(sc[i // 32]) * F32(q) + dmin)
+    return out
+
+
+def py_q6_k(block: bytes, n: int) -> list:
+    ql, qh, scales = block[0:128], block[128:192], block[192:208]
+    d = F32(np.frombuffer(block[208:210], np.float16)[0])
+    out = []
+    for i in range(min(n, 256)):
+        ql_idx = 64 * (i // 128) + 32 * ((i % 128) // 64) + 16 * ((i % 64) // 32) + (i % 16)
+        qh_idx = 32 * (i // 128) + 16 * ((i % 128) // 64) + 8 * ((i % 64) // 32) + (i % 32) // 4
+        sh = 2 * ((i % 32) % 4)
+        q1e = (qh[qh_idx] >> sh) & 3
+        q2e = (qh[qh_idx] >> (sh + 2)) & 3 if sh < 6 else (qh[qh_idx + 1] & 3 if qh_idx + 1 < 64 else 0)
+        q1 = (ql[ql_idx] & 0x0F) | (q1e << 4)
+        q2 = (ql[ql_idx] >> 4) | (q2e << 4)
+        q = q1 if i < 128 else q2
+        out.append(d * F32(scales[i // 16]) * F32(q - 32) / F32(64.0))
+    return out
+
+
+def k_blocks(qt, nb, seed):
+    rng = np.random.default_rng(seed)
+    S = 144 if qt == Q4_K else 210
+    raw = rng.integers(0, 256, size=(nb, S), dtype=np.uint8)
+    d = rng.choice(np.array([0.0123, -0.5, 3e-5, 1.0, 2.0], np.float16), (nb, 2))
+    if qt == Q4_K:
+        raw[:, 12:16] = d.view(np.uint8).reshape(nb, 4)
+    else:
+        raw[:, 208:210] = d[:, :1].view(np.uint8).reshape(nb, 2)
+    return raw
+
+
+@pytest.mark.parametrize("qt,fn", [(Q4_K, py_q4_k), (Q6_K, py_q6_k)])
+def test_k_quant_oracle_matches_transcription(qt, fn):
+    raw = k_blocks(qt, 24, 7 + qt)
+    n = 24 * 256 - 100  # the last super-block is partial (result.truncate)
+    got = O.dequantize(raw.tobytes(), qt, n)
+    ref = []
+    for b in range(24):
+        ref += fn(raw[b].tobytes(), n - 256 * b)
+    assert np.array_equal(got.view(np.uint32), np.array(ref, np.float32).view(np.uint32))
+
+
+def test_q4_k_hand_values():
+    # scale 0 = 1 (byte 0 low six bits), d = 1, dmin = 0.5; qs[0] = 0x21 -> q = 1, 2
+    blk = bytearray(144)
+    blk[0] = 1
+    blk[12:14] = np.float16(1.0).tobytes()
+    blk[14:16] = np.float16(0.5).tobytes()
+    blk[16] = 0x21
+    out = O.dequantize(bytes(blk), Q4_K, 256)
+    assert out[0] == 1.5 and out[1] == 2.5 and out[2] == 0.5
+    assert out[32] == 0.5  # scale 1 is 0
+
+
+def test_k_quant_short_buffer_and_zero_stubs():
+    with pytest.raises(ValueError):
+        O.dequantize(b"\x00" * 143, Q4_K, 256)
+    with pytest.raises(ValueError):
+        O.dequantize(b"\x00" * 209, Q6_K, 256)
+    for qt in (6, 7, Q5_K, Q8_K):  # Q5_0, Q5_1, Q5_K, Q8_K: zeros (dequantize.rs:539-607)
+        assert not O.dequantize(b"\x01" * 400, qt, 256).any()

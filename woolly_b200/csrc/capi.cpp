@@ -239,6 +239,13 @@ int wl_dequantize(int type, const void* blocks, size_t nbytes, size_t n, float* 
     if (nbytes < need)
       return fail(WL_ERR_BUFFER_TOO_SMALL, "Buffer too small: needed " + std::to_string(need) +
                                                 " bytes, but only " + std::to_string(nbytes) + " available");
+  } else if (type == 12 || type == 14) {  // Q4_K / Q6_K: every super-block must be present
+    need = (n + 255) / 256 * (type == 12 ? 144 : 210);
+    if (nbytes < need)
+      return fail(WL_ERR_INVALID_FORMAT, std::string("Invalid tensor info: ") +
+                                             (type == 12 ? "Q4_K" : "Q6_K") + " data too small");
+  } else if (type == 6 || type == 7 || type == 13 || type == 15) {
+    // Q5_0 / Q5_1 / Q5_K / Q8_K: the reference returns zeros (dequantize.rs:539-551, 595-607)
   } else {
     return fail(type_valid((uint32_t)type) ? WL_ERR_UNSUPPORTED : WL_ERR_INVALID_TENSOR_TYPE,
                 "dequantize: type " + std::to_string(type) + " not supported");

@@ -177,6 +177,42 @@ __global__ void k_rope(const float* x, float* out, const int* pos, float base, i
 // woolly_gguf::dequantize (dequantize.rs:286-327, :337-378, :553-586), one
 // thread per 32-value block; bit-exact: (q-8)*d, q*d then +m (two roundings,
 // no FMA), q*d with d widened exactly from f16.
+// K-quant super-blocks of 256 values as woolly_gguf::dequantize reads them
+// (one thread per value): Q4_K dequantize.rs:404-462 = d*scale[i/32]*q + dmin
+// with 8 six-bit scales and nibble i%2 of byte i/2; Q6_K dequantize.rs:465-537
+// = d*scale[i/16]*(q6 - 32)/64 with the reference's ql/qh indexing.  Each
+// product and sum is rounded separately (no FMA), as in the Rust code.
+__global__ void k_dequant_k(int type, const uint8_t* blocks, size_t n, float* out) {
+  const size_t i_all = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
+  if (i_all >= n) return;
+  const size_t b = i_all / 256;
+  const int i = (int)(i_all % 256);
+  float v;
+  if (type == 12) {
+    const uint8_t* blk = blocks + b * 144;
+    const int si = i / 32, src = (si * 3) / 2;
+    const int sc = (si % 2 == 0) ? (blk[src] & 63) : (((blk[src] >> 6) | ((blk[src + 1] & 15) << 2)) & 63);
+    const float d = __half2float(__ushort_as_half((uint16_t)(blk[12] | (blk[13] << 8))));
+    const float dmin = __half2float(__ushort_as_half((uint16_t)(blk[14] | (blk[15] << 8))));
+    const int q = (i % 2 == 0) ? (blk[16 + i / 2] & 15) : ((blk[16 + i / 2] >> 4) & 15);
+    v = __fadd_rn(__fmul_rn(__fmul_rn(d, (float)sc), (float)q), dmin);
+  } else {
+    const uint8_t* blk = blocks + b * 210;
+    const uint8_t *ql = blk, *qh = blk + 128, *scales = blk + 192;
+    const float d = __half2float(__ushort_as_half((uint16_t)(blk[208] | (blk[209] << 8))));
+    const int ql_idx = 64 * (i / 128) + 32 * ((i % 128) / 64) + 16 * ((i % 64) / 32) + (i % 16);
+    const int qh_idx = 32 * (i / 128) + 16 * ((i % 128) / 64) + 8 * ((i % 64) / 32) + (i % 32) / 4;
+    const int qh_shift = 2 * ((i % 32) % 4);
+    const int qv = qh[qh_idx];
+    const int q1_ext = (qv >> qh_shift) & 3;
+    const int q2_ext = qh_shift < 6 ? ((qv >> (qh_shift + 2)) & 3) : (qh_idx + 1 < 64 ? (qh[qh_idx + 1] & 3) : 0);
+    const int q1 = (ql[ql_idx] & 15) | (q1_ext << 4), q2 = (ql[ql_idx] >> 4) | (q2_ext << 4);
+    const int q = i < 128 ? q1 : q2;
+    v = __fdiv_rn(__fmul_rn(__fmul_rn(d, (float)scales[i / 16]), (float)(q - 32)), 64.0f);
+  }
+  out[i_all] = v;
+}
+
 __global__ void k_dequant(int type, const uint8_t* blocks, size_t n, float* out) {
   size_t b = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
   size_t nb = (n + 31) / 32;
@@ -274,9 +310,18 @@ int launch_dequant(int type, const void* blocks, size_t n, float* out, cudaStrea
     WL_CUDA_TRY(cudaGetLastError());
     return WL_OK;
   }
+  if (type == 12 || type == 14) {
+    if (n) k_dequant_k<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(type, (const uint8_t*)blocks, n, out);
+    WL_CUDA_TRY(cudaGetLastError());
+    return WL_OK;
+  }
+  if (type == 6 || type == 7 || type == 13 || type == 15) {  // reference zero stubs
+    if (n) WL_CUDA_TRY(cudaMemsetAsync(out, 0, n * sizeof(float), st));
+    return WL_OK;
+  }
   if (!(type == WL_Q4_0 || type == WL_Q4_1 || type == WL_Q8_0))
     return fail(WL_ERR_UNSUPPORTED, "dequantize: type " + std::to_string(type) + " not supported");
-  size_t nb = (n + 31) / 32;
+  const size_t nb = (n + 31) / 32;
   k_dequant<<<(unsigned)((nb + 127) / 128), 128, 0, st>>>(type, (const uint8_t*)blocks, n, out);
   WL_CUDA_TRY(cudaGetLastError());
   return WL_OK;
