@@ -108,7 +108,7 @@ def check_gemv(y, ref):
 @pytest.mark.parametrize("qt", [Q4_0, Q4_1, Q8_0])
 @pytest.mark.parametrize("layout", [LAYOUT_B, LAYOUT_A])
 @pytest.mark.parametrize("K,N", [(512, 1024), (2048, 256), (768, 96), (256, 4096), (160, 64)])
-@pytest.mark.parametrize("B", [1, 5, 16, 33])
+@pytest.mark.parametrize("B", [1, 3, 5, 16, 33])
 def test_qgemv_vs_oracle(qt, layout, K, N, B):
     raw = quant_matrix(qt, K, N, seed=K * 7 + N + qt)
     x = np.random.default_rng(B).standard_normal((B, K)).astype(np.float32)

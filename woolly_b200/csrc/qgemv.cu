@@ -361,7 +361,11 @@ __device__ void cluster_finish(const GemvArgs& a, const ClusterRed& R, float* ti
 }
 
 // ------------------------------------------------------------------ layout B
-template <int T, int NT>
+// LOC (lo in columns, B <= 4 only): the MMA's 8 columns carry the hi part of
+// (x*d) for rows 0-3 in columns 0-3 and the lo part in columns 4-7, so one MMA
+// pair per tile replaces the hi and lo pairs; the epilogue adds column c + 4
+// to column c.
+template <int T, int NT, bool LOC>
 __global__ void __launch_bounds__(kThreadsB) k_qgemv_b(const GemvArgs a) {
   using Q = QT<T>;
   constexpr int BP = NT * 8;  // padded batch rows
@@ -499,7 +503,8 @@ __global__ void __launch_bounds__(kThreadsB) k_qgemv_b(const GemvArgs a) {
 #pragma unroll
       for (int n = 0; n < NT; n++) {
         const int mi = lane >> 3;
-        const __half* ra = xs + (mi >> 1) * BP * XP + (n * 8 + (lane & 7)) * XP + ks * 16 + (mi & 1) * 8;
+        const int xrow = LOC ? (lane & 3) : (lane & 7);  // LOC: rows 4-7 read rows 0-3 again
+        const __half* ra = xs + (mi >> 1) * BP * XP + (n * 8 + xrow) * XP + ks * 16 + (mi & 1) * 8;
         ldsm_x4(ra, xh[n][0], xh[n][1], xl[n][0], xl[n][1]);
       }
       const uint8_t* p0b = rs + (ks * 16 + 2 * t) * Q::SP + warp * 2 * Q::S;
@@ -553,17 +558,29 @@ __global__ void __launch_bounds__(kThreadsB) k_qgemv_b(const GemvArgs a) {
           uint32_t bh0, bl0, bh1, bl1;
           scale_split(d01, xh[n][0], xl[n][0], bh0, bl0);
           scale_split(d23, xh[n][1], xl[n][1], bh1, bl1);
-          mma16816(acc[blk][0][n], af[0], bh0, bh1);
-          mma16816(acc[blk][1][n], af[1], bh0, bh1);
-          mma16816(acc[blk][0][n], af[0], bl0, bl1);
-          mma16816(acc[blk][1][n], af[1], bl0, bl1);
+          if constexpr (LOC) {
+            const bool loc = g >= 4;  // this lane's B column carries a lo part
+            const uint32_t b0 = loc ? bl0 : bh0, b1 = loc ? bl1 : bh1;
+            mma16816(acc[blk][0][n], af[0], b0, b1);
+            mma16816(acc[blk][1][n], af[1], b0, b1);
+          } else {
+            mma16816(acc[blk][0][n], af[0], bh0, bh1);
+            mma16816(acc[blk][1][n], af[1], bh0, bh1);
+            mma16816(acc[blk][0][n], af[0], bl0, bl1);
+            mma16816(acc[blk][1][n], af[1], bl0, bl1);
+          }
           if constexpr (T == WL_Q4_1) {
             const uint32_t ones[4] = {kOnes, kOnes, kOnes, kOnes};
             uint32_t mh0, ml0, mh1, ml1;
             scale_split(m01, xh[n][0], xl[n][0], mh0, ml0);
             scale_split(m23, xh[n][1], xl[n][1], mh1, ml1);
-            mma16816(accm[blk][n], ones, mh0, mh1);
-            mma16816(accm[blk][n], ones, ml0, ml1);
+            if constexpr (LOC) {
+              const bool loc = g >= 4;
+              mma16816(accm[blk][n], ones, loc ? ml0 : mh0, loc ? ml1 : mh1);
+            } else {
+              mma16816(accm[blk][n], ones, mh0, mh1);
+              mma16816(accm[blk][n], ones, ml0, ml1);
+            }
           }
         }
       }
@@ -592,7 +609,11 @@ __global__ void __launch_bounds__(kThreadsB) k_qgemv_b(const GemvArgs a) {
               const int c = (warp * 2 + blk) * 32 + 16 * mt + 2 * g + (q >> 1);
               // m-tile 1 of the 4-bit types accumulated 16x the codes (exact power of two)
               const float sc = (T != WL_Q8_0 && mt == 1) ? 0.0625f : 1.0f;
-              const float v = acc[blk][mt][n][q] * sc + accm[blk][n][q];
+              float v = acc[blk][mt][n][q] * sc + accm[blk][n][q];
+              if constexpr (LOC) {  // column b + 4 (lane t + 2) holds row b's lo part
+                v += __shfl_xor_sync(0xffffffffu, v, 2);
+                if (t >= 2) continue;
+              }
               if (pass == 0)
                 tile[b * TP + c] = v;
               else
@@ -861,13 +882,13 @@ int launch_cluster(Kern kern, dim3 grid, int threads, size_t smem, int cx, int c
   return WL_OK;
 }
 
-template <int T, int NT>
+template <int T, int NT, bool LOC = false>
 int launch_b_t(const GemvArgs& a, cudaStream_t st) {
   static unsigned attr_done = 0;
   int groups = 0;
   for (int s = 0; s < a.nseg; s++) groups += a.seg[s].groups;
   const bool sw = a.epi.kind == EPI_SWIGLU;
-  return launch_cluster(k_qgemv_b<T, NT>, dim3(groups, a.csplit), kThreadsB, smem_b<T>(NT),
+  return launch_cluster(k_qgemv_b<T, NT, LOC>, dim3(groups, a.csplit), kThreadsB, smem_b<T>(NT),
                         sw ? 2 : 1,
                         a.csplit, a, st, attr_done);
 }
@@ -883,7 +904,9 @@ int launch_a_t(const GemvArgs& a, cudaStream_t st) {
 template <int T, bool LB>
 int dispatch(const GemvArgs& a, cudaStream_t st) {
   switch ((a.B + 7) / 8) {
-    case 1: return LB ? launch_b_t<T, 1>(a, st) : launch_a_t<T, 1>(a, st);
+    case 1:
+      if (LB) return a.B <= 4 ? launch_b_t<T, 1, true>(a, st) : launch_b_t<T, 1>(a, st);
+      return launch_a_t<T, 1>(a, st);
     case 2: return LB ? launch_b_t<T, 2>(a, st) : launch_a_t<T, 2>(a, st);
     case 3: return LB ? launch_b_t<T, 3>(a, st) : launch_a_t<T, 3>(a, st);
     case 4: return LB ? launch_b_t<T, 4>(a, st) : launch_a_t<T, 4>(a, st);
