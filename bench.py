@@ -213,9 +213,10 @@ def run_reference(args):
 # ---------------------------------------------------------------- GPU arm
 def gemv_roofline(torch, dev, reps=24):
     """Average duration of the layout-B Q4_0 GEMV at B=16 over the four 7B
-    projection shapes (the launches of one decode layer), weights rotated
-    across copies totalling > 4x L2, launches captured in a CUDA graph and
-    timed with CUDA events on the capturing stream."""
+    projection shapes (the launches of one decode layer), on the tiled decode
+    copies the model runtime uses, weights rotated across copies totalling
+    > 4x L2, launches captured in a CUDA graph and timed with CUDA events on
+    the capturing stream."""
     from woolly_b200 import ops
     shapes = [(4096, 12288), (4096, 4096), (4096, 22016), (11008, 4096)]
     res = {}
@@ -228,17 +229,18 @@ def gemv_roofline(torch, dev, reps=24):
             v = w.view(-1, 18)
             v[:, 0] = 0
             v[:, 1] = 0x20
+        ws = [ops.qtile(w, 2, K, N) for w in ws]
         planes = ops.split_planes(torch.randn(BATCH, K, device=dev))
         y = torch.empty(BATCH, N, device=dev)
         s = torch.cuda.Stream(dev)
         with torch.cuda.stream(s):
             for i in range(3):
-                ops.qgemv_planes(ws[i % copies], 2, planes, N, out=y)
+                ops.qgemv_tiled(ws[i % copies], 2, planes, N, out=y)
         torch.cuda.synchronize()
         g = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g, stream=s):
             for i in range(reps):
-                ops.qgemv_planes(ws[i % copies], 2, planes, N, out=y)
+                ops.qgemv_tiled(ws[i % copies], 2, planes, N, out=y)
         g.replay()
         torch.cuda.synchronize()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -298,8 +300,9 @@ def _graph_time(torch, dev, fn, reps):
 
 
 def gemv_gemm_sweep(torch, dev, hbm_peak, tc_peak):
-    """The standalone sweep: layout-B GEMV for Q4_0/Q4_1/Q8_0 x three shapes x
-    B in {1, 4, 16} (weights rotated over copies > 4x L2, CUDA-graph timed;
+    """The standalone sweep: layout-B GEMV (tiled decode copies) for
+    Q4_0/Q4_1/Q8_0 x three shapes x B in {1, 4, 16} (weights rotated over
+    copies > 4x L2, CUDA-graph timed;
     GB/s of algorithmic bytes and fraction of the measured HBM peak), and the
     tcgen05 prefill GEMM at M = 512 (useful TFLOP/s = 2*M*K*N / time, and the
     fraction of the measured bf16 dense peak it issues with its 3 exact MMAs)."""
@@ -310,10 +313,11 @@ def gemv_gemm_sweep(torch, dev, hbm_peak, tc_peak):
             ws, nbytes = _rand_blocks(torch, dev, qt, K, N, 2)
             copies = max(2, int(600e6 // nbytes) + 1)
             ws += _rand_blocks(torch, dev, qt, K, N, copies - 2)[0]
+            ws = [ops.qtile(w, qt, K, N) for w in ws]
             for B in (1, 4, 16):
                 planes = ops.split_planes(torch.randn(B, K, device=dev))
                 y = torch.empty(B, N, device=dev)
-                ms = _graph_time(torch, dev, lambda i: ops.qgemv_planes(ws[i % copies], qt, planes, N, out=y), 24)
+                ms = _graph_time(torch, dev, lambda i: ops.qgemv_tiled(ws[i % copies], qt, planes, N, out=y), 24)
                 alg = nbytes + 4 * B * (K + N)
                 gbs = alg / ms / 1e6
                 out["gemv_layout_b"][f"{name} {K}x{N} B={B}"] = {
@@ -462,7 +466,7 @@ def run_gpu(args):
                               "bytes_per_step": step_bytes, "peak_kind": peak_kind},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
                          "frac": achieved / hbm_peak, "traffic": traffic,
-                         "kernel": "k_qgemv_b<Q4_0, B=16>", "peak_kind": peak_kind,
+                         "kernel": "k_qgemv_b<Q4_0, B=16, tiled copy>", "peak_kind": peak_kind,
                          "shapes": per_shape},
             "clocks": clocks,
             "gpu_launches": launches,

@@ -165,6 +165,24 @@ int wl_qgemv(int ggml_type, int layout, const void* W, int K, int N, const float
 int wl_qgemv_planes(int ggml_type, const void* W, int K, int N, const void* x_planes,
                     size_t x_plane, int B, float* y, void* stream);
 
+/* Tiled decode copy of a layout-B matrix (no counterpart in the reference; a
+ * re-layout of the same GGUF blocks for the decode GEMV).  For each 256-column
+ * group and 64-row stage the codes and f16 scales the GEMV's lanes read are
+ * stored as one contiguous block, so a stage is a single coalesced copy and each
+ * lane's operands are two aligned 8-byte loads.  Same size as the GGUF matrix
+ * rounded up to whole (group, stage) tiles.
+ * wl_qtile_bytes: bytes of the copy (0 for an unsupported type or shape).
+ * wl_qtile_repack: writes the copy of W ([K][N] GGUF blocks, N % 32 == 0,
+ *   row pitch N/32 * block bytes) into dst (wl_qtile_bytes bytes, 16-byte
+ *   aligned), asynchronously on `stream`.
+ * wl_qgemv_tiled: wl_qgemv_planes on the tiled copy (K % 16 == 0): the same
+ *   exact per-block products; the K range is split across CTAs in steps of 64
+ *   rows instead of 16, so the f32 summation order (not the math) may differ. */
+size_t wl_qtile_bytes(int ggml_type, int K, int N);
+int wl_qtile_repack(int ggml_type, const void* W, int K, int N, void* dst, void* stream);
+int wl_qgemv_tiled(int ggml_type, const void* W_tiled, int K, int N, const void* x_planes,
+                   size_t x_plane, int B, float* y, void* stream);
+
 /* Quantized GEMM for prompts (prefill): y[m, o] = sum_k x[m, k] * W(k, o) for
  * all M rows in one launch, layout B (W is [K][N] GGUF blocks), the
  * woolly-core `matmul` over a whole sequence (tensor_utils.rs:118-157;

@@ -142,6 +142,37 @@ def test_qgemv_planes_matches_f32_entry(qt):
     assert torch.equal(ref, got)
 
 
+@pytest.mark.parametrize("qt", [Q4_0, Q4_1, Q8_0])
+@pytest.mark.parametrize("K,N", [(512, 1024), (80, 288), (768, 96), (4096, 4096), (11008, 4096)])
+@pytest.mark.parametrize("B", [1, 3, 5, 16, 33])
+def test_qgemv_tiled_vs_oracle(qt, K, N, B):
+    """The tiled decode copy (ragged last group N = 288, a partial last stage
+    K = 80, LOC for B <= 4) against the restatement, and within f32 summation
+    order of the GGUF-layout kernel on the same planes where that kernel takes
+    the shape (16-byte rows; the repack reads any row pitch)."""
+    raw = quant_matrix(qt, K, N, seed=K + N + qt)
+    x = np.random.default_rng(B + 11).standard_normal((B, K)).astype(np.float32)
+    planes = ops.split_planes(dev(x))
+    W = dev(raw)
+    tiled = ops.qtile(W, qt, K, N)
+    assert tiled.numel() == (N + 255) // 256 * ((K + 63) // 64) * 512 * TS[qt]
+    y = ops.qgemv_tiled(tiled, qt, planes, N)
+    ref = ref_gemv(qt, LAYOUT_B, raw, K, N, x)
+    check_gemv(y.cpu().numpy(), ref)
+    if (N // 32 * TS[qt]) % 16:
+        return
+    y0 = ops.qgemv_planes(W, qt, planes, N)
+    assert (y - y0).abs().max().item() <= 1e-5 * max(1.0, float(np.abs(ref).max()))
+
+
+def test_qtile_rejects_bad_shapes():
+    assert _lib.lib().wl_qtile_bytes(Q4_0, 64, 48) == 0
+    assert _lib.lib().wl_qtile_bytes(12, 64, 64) == 0
+    W = torch.zeros(64 * 2 * 18, dtype=torch.uint8, device="cuda")
+    with pytest.raises((ValueError, WoollyError)):
+        ops.qtile(W, Q4_0, 64, 48)
+
+
 def test_matmul_2x2_kat_layout_b():
     """tensor_utils.rs:608-620 ([1,2;3,4] @ [5,6;7,8] = [19,22;43,50]) through the
     layout-B GEMV with Q8_0 blocks of scale 1: the K=2 case takes the generic

@@ -96,6 +96,36 @@ int qgemv_op(int type, int layout, const uint8_t* W, int K, int N, const float* 
 
 using namespace wl;
 
+namespace {
+// Layout-B GEMV on hi/lo planes, 32 rows per launch; `tiled`: W is the tiled
+// decode copy made by wl_qtile_repack.
+int qgemv_planes_op(int type, const void* W, int K, int N, const void* xp, size_t x_plane, int B,
+                    float* y, bool tiled, cudaStream_t st) {
+  GemvArgs a;
+  a.type = type;
+  a.nseg = 1;
+  a.tiled = tiled;
+  a.seg[0].W = (const uint8_t*)W;
+  a.seg[0].N = N;
+  a.seg[0].pitch = N / 32 * bb(type);
+  a.seg[0].groups = (N + 255) / 256;
+  a.K = K;
+  a.ldx = K;
+  a.xkind = X_PLANES;
+  a.x_plane = x_plane;
+  a.epi.kind = EPI_F32;
+  a.epi.ldy[0] = N;
+  for (int r0 = 0; r0 < B; r0 += 32) {
+    a.B = std::min(32, B - r0);
+    a.x = (const __half*)xp + (size_t)r0 * K;
+    a.epi.y[0] = y + (size_t)r0 * N;
+    qgemv_plan(a, WL_LAYOUT_B, sm_count());
+    WL_TRY(launch_qgemv_b(a, st));
+  }
+  return WL_OK;
+}
+}  // namespace
+
 extern "C" {
 
 const char* wl_last_error(void) { return g_err.c_str(); }
@@ -271,27 +301,29 @@ int wl_qgemv_planes(int type, const void* W, int K, int N, const void* xp, size_
   const int pitch = N / 32 * bb(type);
   if (N % 32 || !qgemv_b_fast_ok(type, K, N, pitch, W))
     return fail(WL_ERR_INVALID_ARGUMENT, "qgemv_planes: needs N % 32 == 0, K % 16 == 0, 16-byte rows");
-  GemvArgs a;
-  a.type = type;
-  a.nseg = 1;
-  a.seg[0].W = (const uint8_t*)W;
-  a.seg[0].N = N;
-  a.seg[0].pitch = pitch;
-  a.seg[0].groups = (N + 255) / 256;
-  a.K = K;
-  a.ldx = K;
-  a.xkind = X_PLANES;
-  a.x_plane = x_plane;
-  a.epi.kind = EPI_F32;
-  a.epi.ldy[0] = N;
-  for (int r0 = 0; r0 < B; r0 += 32) {
-    a.B = std::min(32, B - r0);
-    a.x = (const __half*)xp + (size_t)r0 * K;
-    a.epi.y[0] = y + (size_t)r0 * N;
-    qgemv_plan(a, WL_LAYOUT_B, sm_count());
-    WL_TRY(launch_qgemv_b(a, (cudaStream_t)stream));
-  }
-  return WL_OK;
+  return qgemv_planes_op(type, W, K, N, xp, x_plane, B, y, false, (cudaStream_t)stream);
+}
+
+size_t wl_qtile_bytes(int type, int K, int N) {
+  if (!bb(type) || K <= 0 || N <= 0 || N % 32) return 0;
+  return qtile_bytes(type, K, N);
+}
+
+int wl_qtile_repack(int type, const void* W, int K, int N, void* dst, void* stream) {
+  if (!W || !dst) return fail(WL_ERR_INVALID_ARGUMENT, "null pointer");
+  if (!bb(type)) return fail(WL_ERR_UNSUPPORTED, "qtile: type must be Q4_0, Q4_1 or Q8_0");
+  if (K <= 0 || N <= 0 || N % 32) return fail(WL_ERR_INVALID_ARGUMENT, "qtile: needs K > 0, N % 32 == 0");
+  return launch_repack_tiled(type, (const uint8_t*)W, K, N, N / 32 * bb(type), (uint8_t*)dst,
+                             (cudaStream_t)stream);
+}
+
+int wl_qgemv_tiled(int type, const void* Wt, int K, int N, const void* xp, size_t x_plane, int B,
+                   float* y, void* stream) {
+  if (!Wt || !xp || !y || B <= 0) return fail(WL_ERR_INVALID_ARGUMENT, "bad argument");
+  if (!bb(type)) return fail(WL_ERR_UNSUPPORTED, "qgemv: type must be Q4_0, Q4_1 or Q8_0");
+  if (K <= 0 || K % 16 || N <= 0 || N % 32 || (reinterpret_cast<uintptr_t>(Wt) & 15))
+    return fail(WL_ERR_INVALID_ARGUMENT, "qgemv_tiled: needs K % 16 == 0, N % 32 == 0, 16-byte aligned copy");
+  return qgemv_planes_op(type, Wt, K, N, xp, x_plane, B, y, true, (cudaStream_t)stream);
 }
 
 // Prefill GEMM (tensor_utils.rs:118-157 over a whole sequence): tcgen05 tiles

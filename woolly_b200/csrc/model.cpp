@@ -329,9 +329,12 @@ static int gemv(wl_model* m, int nseg, const QMat* mats, int R, const __half* x,
     GemvArgs a;
     a.type = (int)mats[0].type;
     a.nseg = nseg;
+    bool tiled = true;
+    for (int s = 0; s < nseg; s++) tiled = tiled && mats[s].wt != nullptr;
+    a.tiled = tiled ? 1 : 0;
     int gb = 0;
     for (int s = 0; s < nseg; s++) {
-      a.seg[s].W = mats[s].w;
+      a.seg[s].W = tiled ? mats[s].wt : mats[s].w;
       a.seg[s].N = mats[s].N;
       a.seg[s].pitch = mats[s].pitch;
       a.seg[s].groups = (mats[s].N + 255) / 256;
@@ -668,6 +671,33 @@ int model_load(wl_ctx* ctx, const char* path, const wl_model_options* o, wl_mode
     y.wu.w = B + z.u;
     y.wd.w = B + z.dn;
   }
+  // ---- tiled decode copies (the GEMV's lane-ready layout) of every quantized projection ----
+  {
+    static const bool off = getenv("WL_NO_TILED") != nullptr;
+    std::vector<QMat*> mats;
+    if (!off) {
+      for (Layer& y : m->layers)
+        for (QMat* q : {&y.wq, &y.wk, &y.wv, &y.wo, &y.wg, &y.wu, &y.wd}) mats.push_back(q);
+      mats.push_back(&m->out);
+    }
+    size_t total = 0;
+    std::vector<size_t> offs;
+    for (QMat* q : mats) {
+      const bool ok = block_bytes(q->type) && qgemv_b_fast_ok(q->type, q->K, q->N, q->pitch, q->w);
+      offs.push_back(ok ? total : SIZE_MAX);
+      if (ok) total = align_up(total + qtile_bytes((int)q->type, q->K, q->N), 256);
+    }
+    if (total) {
+      WL_CUDA_TRY(cudaMalloc(&m->dtiled, total));
+      for (size_t i = 0; i < mats.size(); i++) {
+        if (offs[i] == SIZE_MAX) continue;
+        QMat* q = mats[i];
+        WL_TRY(launch_repack_tiled((int)q->type, q->w, q->K, q->N, q->pitch, m->dtiled + offs[i], m->st));
+        q->wt = m->dtiled + offs[i];
+      }
+      WL_CUDA_TRY(cudaStreamSynchronize(m->st));
+    }
+  }
   // ---- KV page pool ----
   m->max_sessions = opt.max_sessions;
   m->max_pages = (opt.max_context + m->page - 1) / m->page;
@@ -711,6 +741,7 @@ void model_free(wl_model* m) {
   for (wl_session* s : m->slots)
     if (s) s->m = nullptr;
   cudaFree(m->dweights);
+  cudaFree(m->dtiled);
   cudaFree(m->kvbuf);
   cudaFree(m->d_tables);
   cudaFree(m->h);

@@ -28,6 +28,7 @@ struct QMat {
   uint32_t type = 0;
   int K = 0, N = 0;
   int pitch = 0;  // bytes per row
+  const uint8_t* wt = nullptr;  // tiled decode copy (qtile_bytes), when the type has one
 };
 
 struct Layer {
@@ -53,6 +54,7 @@ struct wl_model {
   int window = 0, rope = 0;
   // weights
   uint8_t* dweights = nullptr;
+  uint8_t* dtiled = nullptr;  // tiled decode copies of the quantized projections
   size_t weight_bytes = 0;
   const float* embd = nullptr;  // [d][V] f32
   const float* out_norm = nullptr;

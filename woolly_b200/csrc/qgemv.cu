@@ -365,7 +365,10 @@ __device__ void cluster_finish(const GemvArgs& a, const ClusterRed& R, float* ti
 // (x*d) for rows 0-3 in columns 0-3 and the lo part in columns 4-7, so one MMA
 // pair per tile replaces the hi and lo pairs; the epilogue adds column c + 4
 // to column c.
-template <int T, int NT, bool LOC>
+// TLD: weights in the tiled decode layout (qtile_bytes): a stage is one
+// contiguous copy and each lane reads its A-fragment codes and scales with two
+// 8-byte loads (outputs g, g+8, 16+g, 24+g of its block).
+template <int T, int NT, bool LOC, bool TLD>
 __global__ void __launch_bounds__(kThreadsB) k_qgemv_b(const GemvArgs a) {
   using Q = QT<T>;
   constexpr int BP = NT * 8;  // padded batch rows
@@ -394,7 +397,10 @@ __global__ void __launch_bounds__(kThreadsB) k_qgemv_b(const GemvArgs a) {
     lg = gx - a.seg[seg].group_base;
   }
   const int Nseg = a.seg[seg].N, pitch = a.seg[seg].pitch;
-  const uint8_t* W = a.seg[seg].W + (size_t)lg * kGroupBlocks * Q::S;
+  constexpr int STB = 512 * Q::S;                  // tiled: bytes of one (group, stage) block
+  constexpr int CODEB = 1024 * (T == WL_Q8_0 ? 16 : 8);  // tiled: code bytes of a stage block
+  const uint8_t* W = TLD ? a.seg[seg].W + ((size_t)lg * ((a.K + kRows - 1) / kRows) + split * (a.kchunk / kRows)) * STB
+                         : a.seg[seg].W + (size_t)lg * kGroupBlocks * Q::S;
   const int k0 = split * a.kchunk;
   const int k1 = min(a.K, k0 + a.kchunk);
   const int nstage = k1 > k0 ? (k1 - k0 + kRows - 1) / kRows : 0;
@@ -430,6 +436,16 @@ __global__ void __launch_bounds__(kThreadsB) k_qgemv_b(const GemvArgs a) {
     xsrc[j] = live ? p * a.x_plane + (size_t)b * a.ldx + c * 8 : 0;
   }
   auto load_w = [&](int st, int buf) {  // immutable weights
+    if constexpr (TLD) {  // one contiguous block per stage
+      uint8_t* dst = raw + buf * SST;
+      const uint8_t* src = W + (size_t)st * STB;
+#pragma unroll
+      for (int j = 0; j < (STB / 16 + kThreadsB - 1) / kThreadsB; j++) {
+        const int c = tid + j * kThreadsB;
+        if (c < STB / 16) cp_async16(dst + c * 16, src + c * 16, 16);
+      }
+      return;
+    }
     const int r0 = k0 + st * kRows;
     uint8_t* dst = raw + buf * SST;
 #pragma unroll
@@ -510,13 +526,46 @@ __global__ void __launch_bounds__(kThreadsB) k_qgemv_b(const GemvArgs a) {
       const uint8_t* p0b = rs + (ks * 16 + 2 * t) * Q::SP + warp * 2 * Q::S;
 #pragma unroll
       for (int blk = 0; blk < 2; blk++) {
+        uint32_t af[2][4];
+        uint32_t d01, d23, m01 = 0, m23 = 0;
+        if constexpr (TLD) {
+          const int u = (warp * 4 + ks) * 2 + blk;
+          const uint2 sw = *reinterpret_cast<const uint2*>(rs + CODEB + (u * 4 + t) * 8);
+          d01 = sw.x;
+          d23 = sw.y;
+          if constexpr (T == WL_Q4_1) {
+            const uint2 mw = *reinterpret_cast<const uint2*>(rs + CODEB + 1024 + (u * 4 + t) * 8);
+            m01 = mw.x;
+            m23 = mw.y;
+          }
+          if constexpr (T == WL_Q8_0) {
+            const uint4 cw = *reinterpret_cast<const uint4*>(rs + u * 512 + lane * 16);
+            const uint32_t w[4] = {cw.x, cw.y, cw.z, cw.w};
+#pragma unroll
+            for (int q = 0; q < 4; q++) {
+              af[q >> 1][(q & 1) * 2] = q8a(prmt(w[q], 0u, 0x4140));
+              af[q >> 1][(q & 1) * 2 + 1] = q8a(prmt(w[q], 0u, 0x4342));
+            }
+          } else {
+            const uint2 cw = *reinterpret_cast<const uint2*>(rs + u * 256 + lane * 8);
+            const uint32_t w0 = cw.x, w1 = cw.y, v0 = w0 >> 8, v1 = w1 >> 8;
+            const uint32_t ML = 0x000F000Fu, MH = 0x00F000F0u;
+            af[0][0] = q4a<T>((w0 & ML) | kMagic);
+            af[0][1] = q4a<T>((v0 & ML) | kMagic);
+            af[0][2] = q4a<T>((w1 & ML) | kMagic);
+            af[0][3] = q4a<T>((v1 & ML) | kMagic);
+            af[1][0] = q4a_hi<T>((w0 & MH) | kMagic);
+            af[1][1] = q4a_hi<T>((v0 & MH) | kMagic);
+            af[1][2] = q4a_hi<T>((w1 & MH) | kMagic);
+            af[1][3] = q4a_hi<T>((v1 & MH) | kMagic);
+          }
+        } else {
         const uint8_t* p0 = p0b + blk * Q::S;
         const uint8_t* p1 = p0 + Q::SP;
         const uint8_t* p2 = p0 + 8 * Q::SP;
         const uint8_t* p3 = p2 + Q::SP;
-        const uint32_t d01 = prmt(ld16(p0), ld16(p1), 0x5410);
-        const uint32_t d23 = prmt(ld16(p2), ld16(p3), 0x5410);
-        uint32_t af[2][4];
+        d01 = prmt(ld16(p0), ld16(p1), 0x5410);
+        d23 = prmt(ld16(p2), ld16(p3), 0x5410);
         const int o = Q::QOFF + 2 * g;
         // byte 0 (sel 0x6420) or byte 1 (sel 0x6521) of the 16-bit payload words of
         // rows (r0, r0+1) and (r0+8, r0+9), one per f16 lane
@@ -548,10 +597,10 @@ __global__ void __launch_bounds__(kThreadsB) k_qgemv_b(const GemvArgs a) {
           af[1][2] = q4a_hi<T>((x20 & MH) | kMagic);
           af[1][3] = q4a_hi<T>((x21 & MH) | kMagic);
         }
-        uint32_t m01 = 0, m23 = 0;
         if constexpr (T == WL_Q4_1) {
           m01 = prmt(ld16(p0 + 2), ld16(p1 + 2), 0x5410);
           m23 = prmt(ld16(p2 + 2), ld16(p3 + 2), 0x5410);
+        }
         }
 #pragma unroll
         for (int n = 0; n < NT; n++) {
@@ -606,7 +655,8 @@ __global__ void __launch_bounds__(kThreadsB) k_qgemv_b(const GemvArgs a) {
 #pragma unroll
             for (int q = 0; q < 4; q++) {
               const int b = n * 8 + 2 * t + (q & 1);
-              const int c = (warp * 2 + blk) * 32 + 16 * mt + 2 * g + (q >> 1);
+              // A-row r of m-tile mt: output 2r / 2r+1 (GGUF byte order) or r (tiled)
+              const int c = (warp * 2 + blk) * 32 + 16 * mt + (TLD ? g + 8 * (q >> 1) : 2 * g + (q >> 1));
               // m-tile 1 of the 4-bit types accumulated 16x the codes (exact power of two)
               const float sc = (T != WL_Q8_0 && mt == 1) ? 0.0625f : 1.0f;
               float v = acc[blk][mt][n][q] * sc + accm[blk][n][q];
@@ -882,13 +932,88 @@ int launch_cluster(Kern kern, dim3 grid, int threads, size_t smem, int cx, int c
   return WL_OK;
 }
 
-template <int T, int NT, bool LOC = false>
+// ------------------------------------------------------------------ tiled decode copy
+// One thread per (group, stage, unit, lane): writes the lane's code bytes of
+// one unit (warp w, k step ks, block pair member blk) and, for lanes 0-3, the
+// unit's scales (and mins) for t = lane.  Source: GGUF blocks [K][N/32].
+template <int T>
+__global__ void k_repack_tiled(const uint8_t* src, int K, int N, int pitch, uint8_t* dst, int stages,
+                               size_t total) {
+  using Q = QT<T>;
+  constexpr int STB = 512 * Q::S;
+  constexpr int CB = T == WL_Q8_0 ? 16 : 8;  // code bytes per lane per unit
+  constexpr int CODEB = 1024 * CB;  // 32 units x 32 lanes
+  const size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
+  if (i >= total) return;
+  const int lane = (int)(i & 31), u = (int)((i >> 5) & 31);
+  const size_t gs = i >> 10;  // group * stages + stage
+  const int stage = (int)(gs % stages);
+  const int group = (int)(gs / stages);
+  const int w = u >> 3, ks = (u >> 1) & 3, blk = u & 1;
+  const int cb = group * kGroupBlocks + w * 2 + blk;
+  const bool colok = cb < N / 32;
+  const int g = lane >> 2, t = lane & 3;
+  const int kb = stage * kRows + ks * 16;
+  uint8_t* D = dst + gs * STB;
+  auto code = [&](int o, int k) -> uint32_t {  // output o (0..31) of block cb at k row k
+    if (!colok || k >= K) return T == WL_Q4_0 ? 8u : 0u;
+    const uint8_t* b = src + (size_t)k * pitch + (size_t)cb * Q::S;
+    if (T == WL_Q8_0) return b[2 + o];
+    return o < 16 ? (b[Q::QOFF + o] & 15u) : (b[Q::QOFF + o - 16] >> 4);
+  };
+  auto scale = [&](int k, int which) -> uint32_t {  // which 0: d, 1: m (Q4_1)
+    if (!colok || k >= K) return 0u;
+    const uint8_t* b = src + (size_t)k * pitch + (size_t)cb * Q::S + 2 * which;
+    return (uint32_t)(b[0] | (b[1] << 8));
+  };
+  uint8_t* C = D + u * (32 * CB) + lane * CB;
+  if (T == WL_Q8_0) {
+    // registers m-tile 0 a0..a3, m-tile 1 a0..a3, 2 codes each (k even, k odd)
+    for (int mt = 0; mt < 2; mt++)
+      for (int r = 0; r < 4; r++) {
+        const int o = mt * 16 + g + 8 * (r & 1), k = kb + 2 * t + 8 * (r >> 1);
+        C[(mt * 4 + r) * 2] = (uint8_t)code(o, k);
+        C[(mt * 4 + r) * 2 + 1] = (uint8_t)code(o, k + 1);
+      }
+  } else {
+    // word w (k rows 2t, 2t+1 | 2t+8, 2t+9): nibbles 0..7 =
+    // (g,k) (16+g,k) (g+8,k) (24+g,k) (g,k+1) (16+g,k+1) (g+8,k+1) (24+g,k+1)
+    for (int wd = 0; wd < 2; wd++) {
+      const int k = kb + 2 * t + 8 * wd;
+      const int os[4] = {g, 16 + g, g + 8, 24 + g};
+      uint32_t word = 0;
+      for (int j = 0; j < 8; j++) word |= code(os[j & 3], k + (j >> 2)) << (4 * j);
+      for (int j = 0; j < 4; j++) C[wd * 4 + j] = (uint8_t)(word >> (8 * j));
+    }
+  }
+  if (g == 0) {  // scales: d(2t) d(2t+1) d(2t+8) d(2t+9) (then the mins) of unit u
+    for (int which = 0; which < (T == WL_Q4_1 ? 2 : 1); which++) {
+      uint16_t* sp = reinterpret_cast<uint16_t*>(D + CODEB + which * 1024 + (u * 4 + t) * 8);
+      sp[0] = (uint16_t)scale(kb + 2 * t, which);
+      sp[1] = (uint16_t)scale(kb + 2 * t + 1, which);
+      sp[2] = (uint16_t)scale(kb + 2 * t + 8, which);
+      sp[3] = (uint16_t)scale(kb + 2 * t + 9, which);
+    }
+  }
+}
+
+template <int T>
+int repack_tiled_t(const uint8_t* src, int K, int N, int pitch, uint8_t* dst, cudaStream_t st) {
+  const int groups = (N + kColsB - 1) / kColsB, stages = (K + kRows - 1) / kRows;
+  const size_t total = (size_t)groups * stages * 1024;
+  if (!total) return WL_OK;
+  k_repack_tiled<T><<<(unsigned)((total + 255) / 256), 256, 0, st>>>(src, K, N, pitch, dst, stages, total);
+  WL_CUDA_TRY(cudaGetLastError());
+  return WL_OK;
+}
+
+template <int T, int NT, bool LOC = false, bool TLD = false>
 int launch_b_t(const GemvArgs& a, cudaStream_t st) {
   static unsigned attr_done = 0;
   int groups = 0;
   for (int s = 0; s < a.nseg; s++) groups += a.seg[s].groups;
   const bool sw = a.epi.kind == EPI_SWIGLU;
-  return launch_cluster(k_qgemv_b<T, NT, LOC>, dim3(groups, a.csplit), kThreadsB, smem_b<T>(NT),
+  return launch_cluster(k_qgemv_b<T, NT, LOC, TLD>, dim3(groups, a.csplit), kThreadsB, smem_b<T>(NT),
                         sw ? 2 : 1,
                         a.csplit, a, st, attr_done);
 }
@@ -901,15 +1026,25 @@ int launch_a_t(const GemvArgs& a, cudaStream_t st) {
                         a.csplit, a, st, attr_done);
 }
 
+template <int T, bool TLD>
+int dispatch_b(const GemvArgs& a, cudaStream_t st) {
+  switch ((a.B + 7) / 8) {
+    case 1: return a.B <= 4 ? launch_b_t<T, 1, true, TLD>(a, st) : launch_b_t<T, 1, false, TLD>(a, st);
+    case 2: return launch_b_t<T, 2, false, TLD>(a, st);
+    case 3: return launch_b_t<T, 3, false, TLD>(a, st);
+    case 4: return launch_b_t<T, 4, false, TLD>(a, st);
+  }
+  return fail(WL_ERR_INVALID_ARGUMENT, "qgemv: B must be 1..32 per launch");
+}
+
 template <int T, bool LB>
 int dispatch(const GemvArgs& a, cudaStream_t st) {
+  if (LB) return a.tiled ? dispatch_b<T, true>(a, st) : dispatch_b<T, false>(a, st);
   switch ((a.B + 7) / 8) {
-    case 1:
-      if (LB) return a.B <= 4 ? launch_b_t<T, 1, true>(a, st) : launch_b_t<T, 1>(a, st);
-      return launch_a_t<T, 1>(a, st);
-    case 2: return LB ? launch_b_t<T, 2>(a, st) : launch_a_t<T, 2>(a, st);
-    case 3: return LB ? launch_b_t<T, 3>(a, st) : launch_a_t<T, 3>(a, st);
-    case 4: return LB ? launch_b_t<T, 4>(a, st) : launch_a_t<T, 4>(a, st);
+    case 1: return launch_a_t<T, 1>(a, st);
+    case 2: return launch_a_t<T, 2>(a, st);
+    case 3: return launch_a_t<T, 3>(a, st);
+    case 4: return launch_a_t<T, 4>(a, st);
   }
   return fail(WL_ERR_INVALID_ARGUMENT, "qgemv: B must be 1..32 per launch");
 }
@@ -941,7 +1076,7 @@ bool qgemv_a_fast_ok(int type, int K, int N, int pitch, const void* W) {
 void qgemv_plan(GemvArgs& a, int layout, int num_sms) {
   int groups = 0;
   for (int s = 0; s < a.nseg; s++) groups += a.seg[s].groups;
-  const int gran = layout == WL_LAYOUT_B ? 16 : 256;
+  const int gran = layout == WL_LAYOUT_B ? (a.tiled ? kRows : 16) : 256;
   const int units = (a.K + gran - 1) / gran;
   const int target = kPlanCtasPerSm * num_sms;
   const int cmax = a.epi.kind == EPI_SWIGLU ? kMaxCluster / 2 : kMaxCluster;
@@ -950,6 +1085,22 @@ void qgemv_plan(GemvArgs& a, int layout, int num_sms) {
   c = std::max(1, std::min({c, cmax, units}));
   a.kchunk = (units + c - 1) / c * gran;
   a.csplit = (a.K + a.kchunk - 1) / a.kchunk;
+}
+
+size_t qtile_bytes(int type, int K, int N) {
+  const int S = block_bytes(type);
+  return (size_t)((N + kColsB - 1) / kColsB) * ((K + kRows - 1) / kRows) * 512 * S;
+}
+
+int launch_repack_tiled(int type, const uint8_t* src, int K, int N, int pitch, uint8_t* dst,
+                        cudaStream_t st) {
+  if (N % 32 || K <= 0) return fail(WL_ERR_INVALID_ARGUMENT, "repack: N % 32 != 0 or K <= 0");
+  switch (type) {
+    case WL_Q4_0: return repack_tiled_t<WL_Q4_0>(src, K, N, pitch, dst, st);
+    case WL_Q4_1: return repack_tiled_t<WL_Q4_1>(src, K, N, pitch, dst, st);
+    case WL_Q8_0: return repack_tiled_t<WL_Q8_0>(src, K, N, pitch, dst, st);
+  }
+  return fail(WL_ERR_UNSUPPORTED, "repack: unsupported type " + std::to_string(type));
 }
 
 int launch_qgemv_b(const GemvArgs& a, cudaStream_t st) {

@@ -77,7 +77,8 @@ struct GemvArgs {
   size_t x_plane = 0;
   int ldx = 0;
   int csplit = 1;  // CTAs per cluster splitting K (1..16)
-  int kchunk = 0;  // rows of K per CTA (multiple of 16; of 256 for layout A)
+  int kchunk = 0;  // rows of K per CTA (multiple of 16; of 64 tiled; of 256 for layout A)
+  int tiled = 0;   // layout B only: seg[s].W is the tiled decode copy (qtile_bytes)
   Epilogue epi;
   int* err = nullptr;  // optional: bit 2 set when the cluster reduction wait gave up
 };
@@ -133,6 +134,18 @@ bool qgemv_b_fast_ok(int type, int K, int N, int pitch, const void* W);
 bool qgemv_a_fast_ok(int type, int K, int N, int pitch, const void* W);
 // picks csplit / kchunk for a launch (fills the GPU)
 void qgemv_plan(GemvArgs& a, int layout, int num_sms);
+
+// Tiled decode copy of a layout-B matrix: for each 256-column group and each
+// 64-row k stage, one contiguous block of 512 quant blocks' bytes (Q4_0 9216)
+// arranged as the GEMV's MMA lanes read them: per (warp w, 16-row k step,
+// block pair member) unit, each lane's A-fragment codes (8 bytes; Q8_0 16)
+// for k rows 2t, 2t+1, 2t+8, 2t+9 and outputs g, g+8, 16+g, 24+g of its
+// block, then the scales (Q4_1: and mins) as 8 bytes per (unit, t).  Rows
+// past K and columns past N are zero weights.  Same size as the GGUF bytes
+// when K % 64 == 0 and N % 256 == 0.
+size_t qtile_bytes(int type, int K, int N);
+int launch_repack_tiled(int type, const uint8_t* src, int K, int N, int pitch, uint8_t* dst,
+                        cudaStream_t st);
 
 int qgemv_group_cols(int layout);
 

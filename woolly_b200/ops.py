@@ -90,6 +90,29 @@ def qgemv_planes(weights: torch.Tensor, ggml_type: int, planes: torch.Tensor, n:
     return y
 
 
+def qtile(weights: torch.Tensor, ggml_type: int, k: int, n: int) -> torch.Tensor:
+    """Tiled decode copy of a layout-B GGUF matrix [k][n] (wl_qtile_repack)."""
+    _dev(weights, torch.uint8, "weights")
+    nb = lib().wl_qtile_bytes(int(ggml_type), k, n)
+    if not nb:
+        raise ValueError(f"qtile: unsupported type {ggml_type} or shape {k}x{n}")
+    t = torch.empty(nb, dtype=torch.uint8, device=weights.device)
+    check(lib().wl_qtile_repack(int(ggml_type), weights.data_ptr(), k, n, t.data_ptr(), _stream()))
+    return t
+
+
+def qgemv_tiled(tiled: torch.Tensor, ggml_type: int, planes: torch.Tensor, n: int,
+                out: torch.Tensor | None = None) -> torch.Tensor:
+    """qgemv_planes on the tiled copy made by qtile()."""
+    _dev(tiled, torch.uint8, "tiled")
+    _dev(planes, torch.float16, "planes")
+    _, B, K = planes.shape
+    y = out if out is not None else torch.empty(B, n, dtype=torch.float32, device=planes.device)
+    check(lib().wl_qgemv_tiled(int(ggml_type), tiled.data_ptr(), K, n, planes.data_ptr(), B * K,
+                               B, y.data_ptr(), _stream()))
+    return y
+
+
 def rmsnorm_rope(x: torch.Tensor, w: torch.Tensor, eps: float, *, rope: bool = False,
                  positions: torch.Tensor | None = None, head_dim: int = 0, theta: float = 10000.0,
                  out_dtype=torch.float32) -> torch.Tensor:
