@@ -386,6 +386,12 @@ __global__ void __launch_bounds__(kThreadsB) k_qgemv_b(const GemvArgs a) {
   uint8_t* raw = smem;
   TL(0);
 
+  // Tiled codes enter the MMA as f16 subnormals (q * 2^-24: one LOP3 per pair,
+  // no HSUB2).  Q4_1 has no offset; Q4_0's -8 and Q8_0's -128 (codes stored
+  // as q + 128) then cost a ones-MMA per B fragment, which pays only when LOC
+  // halves the MMAs (Q4_0 decode: B = 1 +7%, B = 16 -2%).
+  constexpr bool SUBN = TLD && (T == WL_Q4_1 || LOC);
+  constexpr float kOff = T == WL_Q4_0 ? -8.0f : -128.0f;  // SUBN offset of Q4_0 / Q8_0
   const int tid = threadIdx.x, lane = tid & 31;
   const int warp = (tid >> 5) & 3, kpart = tid >> 7;  // block pair, k-step part
   const int g = lane >> 2, t = lane & 3;
@@ -547,21 +553,39 @@ __global__ void __launch_bounds__(kThreadsB) k_qgemv_b(const GemvArgs a) {
             const uint32_t w[4] = {cw.x, cw.y, cw.z, cw.w};
 #pragma unroll
             for (int q = 0; q < 4; q++) {
-              af[q >> 1][(q & 1) * 2] = q8a(prmt(w[q], 0u, 0x4140));
-              af[q >> 1][(q & 1) * 2 + 1] = q8a(prmt(w[q], 0u, 0x4342));
+              if constexpr (SUBN) {  // q + 128 as subnormal f16
+                af[q >> 1][(q & 1) * 2] = prmt(w[q], 0u, 0x4140) ^ 0x00800080u;
+                af[q >> 1][(q & 1) * 2 + 1] = prmt(w[q], 0u, 0x4342) ^ 0x00800080u;
+              } else {
+                af[q >> 1][(q & 1) * 2] = q8a(prmt(w[q], 0u, 0x4140));
+                af[q >> 1][(q & 1) * 2 + 1] = q8a(prmt(w[q], 0u, 0x4342));
+              }
             }
           } else {
             const uint2 cw = *reinterpret_cast<const uint2*>(rs + u * 256 + lane * 8);
             const uint32_t w0 = cw.x, w1 = cw.y, v0 = w0 >> 8, v1 = w1 >> 8;
             const uint32_t ML = 0x000F000Fu, MH = 0x00F000F0u;
-            af[0][0] = q4a<T>((w0 & ML) | kMagic);
-            af[0][1] = q4a<T>((v0 & ML) | kMagic);
-            af[0][2] = q4a<T>((w1 & ML) | kMagic);
-            af[0][3] = q4a<T>((v1 & ML) | kMagic);
-            af[1][0] = q4a_hi<T>((w0 & MH) | kMagic);
-            af[1][1] = q4a_hi<T>((v0 & MH) | kMagic);
-            af[1][2] = q4a_hi<T>((w1 & MH) | kMagic);
-            af[1][3] = q4a_hi<T>((v1 & MH) | kMagic);
+            if constexpr (SUBN) {
+              // f16 subnormals: q * 2^-24 (low nibbles), 16q * 2^-24 (high); the
+              // epilogue scales by 2^24 / 2^20 and Q4_0's -8 offset comes from accm
+              af[0][0] = w0 & ML;
+              af[0][1] = v0 & ML;
+              af[0][2] = w1 & ML;
+              af[0][3] = v1 & ML;
+              af[1][0] = w0 & MH;
+              af[1][1] = v0 & MH;
+              af[1][2] = w1 & MH;
+              af[1][3] = v1 & MH;
+            } else {
+              af[0][0] = q4a<T>((w0 & ML) | kMagic);
+              af[0][1] = q4a<T>((v0 & ML) | kMagic);
+              af[0][2] = q4a<T>((w1 & ML) | kMagic);
+              af[0][3] = q4a<T>((v1 & ML) | kMagic);
+              af[1][0] = q4a_hi<T>((w0 & MH) | kMagic);
+              af[1][1] = q4a_hi<T>((v0 & MH) | kMagic);
+              af[1][2] = q4a_hi<T>((w1 & MH) | kMagic);
+              af[1][3] = q4a_hi<T>((v1 & MH) | kMagic);
+            }
           }
         } else {
         const uint8_t* p0 = p0b + blk * Q::S;
@@ -622,6 +646,16 @@ __global__ void __launch_bounds__(kThreadsB) k_qgemv_b(const GemvArgs a) {
             mma16816(acc[blk][0][n], af[0], bl0, bl1);
             mma16816(acc[blk][1][n], af[1], bl0, bl1);
           }
+          if constexpr (SUBN && T != WL_Q4_1) {  // sum_k x*d of the block, for the offset
+            const uint32_t ones[4] = {kOnes, kOnes, kOnes, kOnes};
+            if constexpr (LOC) {
+              const bool loc = g >= 4;
+              mma16816(accm[blk][n], ones, loc ? bl0 : bh0, loc ? bl1 : bh1);
+            } else {
+              mma16816(accm[blk][n], ones, bh0, bh1);
+              mma16816(accm[blk][n], ones, bl0, bl1);
+            }
+          }
           if constexpr (T == WL_Q4_1) {
             const uint32_t ones[4] = {kOnes, kOnes, kOnes, kOnes};
             uint32_t mh0, ml0, mh1, ml1;
@@ -661,9 +695,13 @@ __global__ void __launch_bounds__(kThreadsB) k_qgemv_b(const GemvArgs a) {
               const int b = n * 8 + 2 * t + (q & 1);
               // A-row r of m-tile mt: output 2r / 2r+1 (GGUF byte order) or r (tiled)
               const int c = (warp * 2 + blk) * 32 + 16 * mt + (TLD ? g + 8 * (q >> 1) : 2 * g + (q >> 1));
-              // m-tile 1 of the 4-bit types accumulated 16x the codes (exact power of two)
-              const float sc = (T != WL_Q8_0 && mt == 1) ? 0.0625f : 1.0f;
-              float v = acc[blk][mt][n][q] * sc + accm[blk][n][q];
+              // m-tile 1 of the 4-bit types accumulated 16x the codes; the
+              // subnormal codes of the tiled path carry 2^-24 (exact powers of two)
+              const float sc = SUBN ? ((T != WL_Q8_0 && mt == 1) ? 1048576.0f : 16777216.0f)
+                                    : (T != WL_Q8_0 && mt == 1) ? 0.0625f : 1.0f;
+              // accm: sum x*m (Q4_1) or, subnormal Q4_0 / Q8_0, sum x*d times the offset
+              const float cm = (SUBN && T != WL_Q4_1) ? kOff : 1.0f;
+              float v = acc[blk][mt][n][q] * sc + cm * accm[blk][n][q];
               if constexpr (LOC) {  // column b + 4 (lane t + 2) holds row b's lo part
                 v += __shfl_xor_sync(0xffffffffu, v, 2);
                 if (t >= 2) continue;
