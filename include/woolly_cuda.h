@@ -220,6 +220,24 @@ int wl_qgemv_noalloc(int ggml_type, const void* W, int K, int N, const float* x,
 int wl_quantized_matvec(int ggml_type, const void* W, const float* input, float* output,
                         int m, int k, void* stream);
 
+/* Reduce side of the tensor-parallel exchange that replaces ncclAllReduce after
+ * the row-parallel projections (attn_output, ffn_down; lazy_transformer.rs:
+ * 177-179 residual adds) in decode: each rank's GEMV pushes its partial rows
+ * into slot [rank] of every rank's buffer over NVLink and adds 1 per CTA to
+ * that rank's arrival counter there.  This call waits (bounded, about a
+ * second) until counters[r] >= expect for every r < nranks, sets
+ * h[i] += sum_r slots[r][i] (ranks in order: identical on every rank), writes
+ * h back, and RMS-normalises it (tensor_utils.rs:446-480) into f16 hi/lo
+ * planes (lo plane y_plane elements after hi).  slots is [nranks][32][dim]
+ * f32; counters is [nranks] arrivals followed by one word the call uses to
+ * re-arm them (it subtracts expect once every row is done).  A wait that
+ * gives up sets bit 8 in *err (when err is non-null) and the rows are
+ * invalid; the model runtime reports that as WL_ERR_TIMEOUT.  rows <= 32,
+ * nranks <= 8, dim % 4 == 0. */
+int wl_tp_reduce_rmsnorm(float* h, const float* w, int rows, int dim, float eps, const float* slots,
+                         int nranks, unsigned* counters, unsigned expect, void* y_planes,
+                         size_t y_plane, int* err, void* stream);
+
 /* rms_norm (woolly-core tensor_utils.rs:446-480; TransformerSIMD::rms_norm
  * simd_matmul.rs:811), fused with an optional NeoX RoPE of the normalised row
  * (heads of head_dim, position pos[r]); y may be f32 (y_f16 = 0) or f16. */

@@ -335,3 +335,62 @@ def test_k_quant_short_buffer_and_stubs():
     for qt in (6, 7, 13, 15):  # Q5_0, Q5_1, Q5_K, Q8_K: zeros as the reference's stubs
         out = ops.dequantize(dev(np.full(400, 7, np.uint8)), qt, 256)
         assert not out.any().item()
+
+
+def _tp_reduce(h, w, slots, counters, expect, err):
+    rows, dim = h.shape
+    T = slots.shape[0]
+    y = torch.empty(2, rows, dim, dtype=torch.float16, device="cuda")
+    _lib.check(_lib.lib().wl_tp_reduce_rmsnorm(
+        h.data_ptr(), w.data_ptr(), rows, dim, 1e-5, slots.data_ptr(), T, counters.data_ptr(),
+        expect, y.data_ptr(), rows * dim, err.data_ptr(), None))
+    torch.cuda.synchronize()
+    return y
+
+
+@pytest.mark.parametrize("T,rows", [(1, 1), (2, 5), (3, 16), (8, 32)])
+def test_tp_reduce_rmsnorm(T, rows):
+    """The reduce side of the tensor-parallel exchange with T simulated ranks
+    whose partial rows and arrival counts are written from the host: h gets
+    the rank-ordered f32 sum (bit-exact), the output the RMSNorm of it
+    (tensor_utils.rs:446-480), and the counters are re-armed to zero."""
+    dim, expect = 4096, 37
+    rng = np.random.default_rng(T * 100 + rows)
+    h0 = rng.standard_normal((rows, dim)).astype(np.float32)
+    parts = rng.standard_normal((T, 32, dim)).astype(np.float32)
+    w = (1 + 0.02 * rng.standard_normal(dim)).astype(np.float32)
+    h = dev(h0)
+    slots = dev(parts)
+    counters = torch.zeros(T + 1, dtype=torch.int32, device="cuda")
+    counters[:T] = expect
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    y = _tp_reduce(h, dev(w), slots, counters, expect, err)
+    ref_h = h0.copy()
+    for r in range(T):
+        ref_h = (ref_h + parts[r, :rows]).astype(np.float32)
+    assert np.array_equal(h.cpu().numpy(), ref_h)
+    rms = np.sqrt((ref_h.astype(np.float64) ** 2).mean(-1, keepdims=True) + 1e-5)
+    ref_y = ref_h / rms * w
+    got = y[0].float() + y[1].float()
+    assert np.abs(got.cpu().numpy() - ref_y).max() <= 1e-5 * np.abs(ref_y).max()
+    assert int(err.item()) == 0
+    assert counters.cpu().tolist() == [0] * (T + 1)
+
+
+def test_tp_reduce_wait_gives_up():
+    """Failure detection without a GPU fault: one simulated rank never
+    finishes (its counter stays one short), the bounded wait gives up after
+    about a second with bit 8 in the error word, and the context stays usable."""
+    dim, T, rows, expect = 1024, 2, 2, 5
+    h = torch.zeros(rows, dim, device="cuda")
+    slots = torch.zeros(T, 32, dim, device="cuda")
+    w = torch.ones(dim, device="cuda")
+    counters = torch.zeros(T + 1, dtype=torch.int32, device="cuda")
+    counters[0] = expect
+    counters[1] = expect - 1
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    _tp_reduce(h, w, slots, counters, expect, err)
+    assert int(err.item()) & 8
+    x = torch.ones(4, device="cuda")
+    assert float((x * 2).sum().item()) == 8.0
+

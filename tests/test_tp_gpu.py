@@ -1,6 +1,8 @@
 """Tensor parallelism on 2 GPUs: each rank loads its Megatron shard of a seeded
-model (CudaTransformer(tp_rank, tp_size, nccl_comm)); the NCCL all-reduce after
-attn_output and ffn_down joins the partial sums.  Rank 0's logits for a prompt
+model (CudaTransformer(tp_rank, tp_size, nccl_comm)); after attn_output and
+ffn_down the partial sums are joined either by the NVLink peer exchange (the
+GEMV pushes them to every rank, the next RMSNorm adds them up) or, with
+WL_TP_NCCL set, by ncclAllReduce.  Rank 0's logits for a prompt
 and three teacher-forced decode steps must match the CPU oracle within the
 model-level tolerance (max |d| <= 1e-2).  Skipped with fewer than two GPUs.
 """
@@ -18,8 +20,10 @@ pytestmark = pytest.mark.gpu
 TOL = 1e-2
 
 
-def _rank(rank, world, port, path, prompt, steps, q):
+def _rank(rank, world, port, path, prompt, steps, q, mode):
     import torch.distributed as dist
+    if mode == "nccl":
+        os.environ["WL_TP_NCCL"] = "1"
     from woolly_b200.model import CudaTransformer, Session, nccl_communicator, nccl_destroy
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     torch.cuda.set_device(rank)
@@ -48,7 +52,10 @@ def _free_port():
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
 @pytest.mark.parametrize("name", ["gqa_q4_0", "mha_q4_1"])  # kv heads divisible by 2
-def test_tp2_matches_oracle(tiny_models, name):
+@pytest.mark.parametrize("mode", ["peer", "nccl"])
+def test_tp2_matches_oracle(tiny_models, name, mode):
+    """mode "peer": decode-sized batches exchange partial sums through the
+    GEMV's NVLink stores and the RMSNorm's reduce; "nccl": ncclAllReduce."""
     import torch.multiprocessing as mp
     path = tiny_models[name]
     rng = np.random.default_rng(7)
@@ -63,7 +70,7 @@ def test_tp2_matches_oracle(tiny_models, name):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_rank, args=(r, 2, port, path, prompt, steps, q)) for r in range(2)]
+    procs = [ctx.Process(target=_rank, args=(r, 2, port, path, prompt, steps, q, mode)) for r in range(2)]
     for p in procs:
         p.start()
     got = q.get(timeout=300)

@@ -105,6 +105,8 @@ _SIGS = {
     "wl_quantized_matvec": (C.c_int, [C.c_int, P, P, P, C.c_int, C.c_int, P]),
     "wl_rmsnorm_rope": (C.c_int, [P, P, C.c_int, C.c_int, C.c_float, C.c_int, P, C.c_int,
                                   C.c_float, P, C.c_int, P]),
+    "wl_tp_reduce_rmsnorm": (C.c_int, [P, P, C.c_int, C.c_int, C.c_float, P, C.c_int, P, C.c_uint,
+                                       P, C.c_size_t, P, P]),
     "wl_swiglu": (C.c_int, [P, P, C.c_size_t, P, P]),
     "wl_rope": (C.c_int, [P, P, P, C.c_float, C.c_int, C.c_int, C.c_int, C.c_int, P]),
     "wl_attention": (C.c_int, [P, P, P, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int,

@@ -387,6 +387,23 @@ int wl_rmsnorm_rope(const float* x, const float* w, int rows, int dim, float eps
                         y_f16 ? 1 : 0, 0, (cudaStream_t)stream);
 }
 
+int wl_tp_reduce_rmsnorm(float* h, const float* w, int rows, int dim, float eps, const float* slots,
+                         int nranks, unsigned* counters, unsigned expect, void* y_planes,
+                         size_t y_plane, int* err, void* stream) {
+  if (!h || !w || !slots || !counters || !y_planes || rows < 0 || dim <= 0)
+    return fail(WL_ERR_INVALID_ARGUMENT, "bad argument");
+  if (nranks < 1 || nranks > kMaxPeers || rows > kPeerRows)
+    return fail(WL_ERR_INVALID_ARGUMENT, "tp_reduce: 1..8 ranks and at most 32 rows");
+  PeerReduce pr;
+  pr.nranks = nranks;
+  pr.slots = slots;
+  pr.flags = counters;
+  pr.done = counters + nranks;
+  pr.expect = expect;
+  pr.err = err;
+  return launch_rmsnorm_peer(h, w, rows, dim, eps, y_planes, y_plane, pr, (cudaStream_t)stream);
+}
+
 int wl_swiglu(const float* gate, const float* up, size_t n, float* out, void* stream) {
   if (n && (!gate || !up || !out)) return fail(WL_ERR_INVALID_ARGUMENT, "null pointer");
   return launch_swiglu(gate, up, n, out, (cudaStream_t)stream);

@@ -42,6 +42,12 @@ int launch_rmsnorm(const float* x, const float* w, int rows, int dim, float eps,
                    const int* pos, int head_dim, float theta, void* y, int y_mode,
                    size_t y_plane, cudaStream_t st);
 
+// Tensor-parallel variant: x[r] += sum over ranks of the pushed partial rows
+// (written back to x), then the RMSNorm into f16 hi/lo planes.  rows may be 0
+// (waits and re-arms the counters only).
+int launch_rmsnorm_peer(float* x, const float* w, int rows, int dim, float eps, void* y,
+                        size_t y_plane, const PeerReduce& pr, cudaStream_t st);
+
 // h[r][j] = E[j*V + ids[r]] (token_embd stored [d][V], lazy_transformer.rs:1252-1262)
 int launch_embed(const float* E, int d, int V, const uint32_t* ids, int rows, float* h,
                  int* err_flag, cudaStream_t st);

@@ -30,6 +30,7 @@ struct Nccl {
   int (*GetUniqueId)(void*) = nullptr;
   int (*CommInitRank)(void**, int, /*ncclUniqueId by value*/ ...) = nullptr;
   int (*AllReduce)(const void*, void*, size_t, int, int, void*, cudaStream_t) = nullptr;
+  int (*AllGather)(const void*, void*, size_t, int, void*, cudaStream_t) = nullptr;
   int (*CommDestroy)(void*) = nullptr;
   int (*CommAbort)(void*) = nullptr;
   const char* (*GetErrorString)(int) = nullptr;
@@ -46,6 +47,8 @@ Nccl& nccl() {
     n.CommInitRank = (int (*)(void**, int, ...))dlsym(h, "ncclCommInitRank");
     n.AllReduce = (int (*)(const void*, void*, size_t, int, int, void*, cudaStream_t))dlsym(
         h, "ncclAllReduce");
+    n.AllGather = (int (*)(const void*, void*, size_t, int, void*, cudaStream_t))dlsym(
+        h, "ncclAllGather");
     n.CommDestroy = (int (*)(void*))dlsym(h, "ncclCommDestroy");
     n.CommAbort = (int (*)(void*))dlsym(h, "ncclCommAbort");
     n.GetErrorString = (const char* (*)(int))dlsym(h, "ncclGetErrorString");
@@ -278,8 +281,11 @@ static int allreduce_sum(wl_model* m, float* buf, size_t count) {
 constexpr int kGemmMinRows = 64;
 // rows r in [0, R) of x (f16 hi/lo planes, lo plane x_plane elements after
 // hi), up to 32 rows per launch.
+// `ctas` (optional) receives the CTA count of the (single) GEMV launch.
 static int gemv(wl_model* m, int nseg, const QMat* mats, int R, const __half* x, size_t x_plane,
-                int ldx, Epilogue epi) {
+                int ldx, Epilogue epi, unsigned* ctas = nullptr) {
+  if (epi.kind == EPI_PEER && R > kPeerRows)
+    return fail(WL_ERR_INVALID_ARGUMENT, "peer exchange: more rows than one GEMV launch");
   for (int s = 0; s < nseg; s++)
     if (mats[s].type != mats[0].type)
       return fail(WL_ERR_UNSUPPORTED, "fused GEMV segments must share a quantization type");
@@ -349,9 +355,106 @@ static int gemv(wl_model* m, int nseg, const QMat* mats, int R, const __half* x,
     a.ldx = ldx;
     a.epi = e;
     qgemv_plan(a, WL_LAYOUT_B, m->sms);
+    if (ctas) {
+      int groups = 0;
+      for (int s = 0; s < nseg; s++) groups += a.seg[s].groups;
+      *ctas = (unsigned)(groups * a.csplit);
+    }
     WL_TRY(launch_qgemv_b(a, m->st));
   }
   return WL_OK;
+}
+
+// ---- NVLink peer exchange (tensor parallel decode) ----
+static float* peer_slots(const wl_model* m, int rank, int par, int src) {
+  return reinterpret_cast<float*>(m->pbase[rank] + 256) +
+         (size_t)(par * m->tp_size + src) * kPeerRows * m->d;
+}
+static unsigned* peer_flags(const wl_model* m, int rank) {
+  return reinterpret_cast<unsigned*>(m->pbase[rank]);
+}
+
+// Row-parallel GEMV epilogue of exchange `par`: push into slot (par, this
+// rank) of every rank's buffer.
+static Epilogue peer_push(const wl_model* m, int par) {
+  Epilogue e;
+  e.kind = EPI_PEER;
+  e.ldy[0] = m->d;
+  e.nranks = m->tp_size;
+  for (int r = 0; r < m->tp_size; r++) {
+    e.peer[r] = peer_slots(m, r, par, m->tp_rank);
+    e.pflag[r] = peer_flags(m, r) + par * kMaxPeers + m->tp_rank;
+  }
+  return e;
+}
+
+static PeerReduce peer_take(const wl_model* m, int par, unsigned expect, int row0) {
+  PeerReduce pr;
+  pr.nranks = m->tp_size;
+  pr.slots = peer_slots(m, m->tp_rank, par, 0);
+  pr.flags = peer_flags(m, m->tp_rank) + par * kMaxPeers;
+  pr.done = peer_flags(m, m->tp_rank) + 2 * kMaxPeers + par;
+  pr.expect = expect;
+  pr.row0 = row0;
+  pr.err = m->err;
+  return pr;
+}
+
+// One buffer per rank, mapped into every other rank through CUDA IPC (handles
+// exchanged with one ncclAllGather).  Left off (NCCL all-reduce instead) when
+// WL_TP_NCCL is set, for more than kMaxPeers ranks, or when a row-parallel
+// weight cannot take the fast GEMV.
+static int peer_setup(wl_model* m) {
+  const int T = m->tp_size, rk = m->tp_rank;
+  if (T < 2 || T > kMaxPeers || getenv("WL_TP_NCCL")) return WL_OK;
+  for (const Layer& y : m->layers)
+    for (const QMat* q : {&y.wo, &y.wd})
+      if (!block_bytes(q->type) || !qgemv_b_fast_ok(q->type, q->K, q->N, q->pitch, q->w)) return WL_OK;
+  Nccl& n = nccl();
+  if (!n.AllGather) return WL_OK;
+  const size_t bytes = 256 + (size_t)2 * T * kPeerRows * m->d * sizeof(float);
+  WL_CUDA_TRY(cudaMalloc(&m->pmem, bytes));
+  WL_CUDA_TRY(cudaMemset(m->pmem, 0, bytes));
+  cudaIpcMemHandle_t h;
+  WL_CUDA_TRY(cudaIpcGetMemHandle(&h, m->pmem));
+  uint8_t* dh = nullptr;
+  WL_CUDA_TRY(cudaMalloc(&dh, (size_t)T * sizeof(h)));
+  std::vector<cudaIpcMemHandle_t> all(T);
+  cudaError_t ce = cudaMemcpy(dh + (size_t)rk * sizeof(h), &h, sizeof(h), cudaMemcpyHostToDevice);
+  int nr = 0;
+  if (ce == cudaSuccess) {
+    nr = n.AllGather(dh + (size_t)rk * sizeof(h), dh, sizeof(h), /*ncclUint8*/ 1, m->nccl, m->st);
+    if (!nr) ce = cudaStreamSynchronize(m->st);
+    if (!nr && ce == cudaSuccess) ce = cudaMemcpy(all.data(), dh, (size_t)T * sizeof(h), cudaMemcpyDeviceToHost);
+  }
+  cudaFree(dh);
+  if (nr) return fail(WL_ERR_NCCL, std::string("ncclAllGather: ") + n.GetErrorString(nr));
+  WL_CUDA_TRY(ce);
+  for (int r = 0; r < T; r++) {
+    if (r == rk) {
+      m->pbase[r] = m->pmem;
+      continue;
+    }
+    void* p = nullptr;
+    WL_CUDA_TRY(cudaIpcOpenMemHandle(&p, all[r], cudaIpcMemLazyEnablePeerAccess));
+    m->pbase[r] = static_cast<uint8_t*>(p);
+  }
+  m->peer = true;
+  return WL_OK;
+}
+
+// Device error flags of the finished calls (the pinned mirror is copied at the
+// end of each call): bit 1 token id out of range; 2, 4, 8, 16 a bounded wait
+// (attention ring, cluster reduction, peer exchange, GEMM ring) gave up.
+static int take_err(wl_model* m) {
+  const int e = *m->h_err;
+  if (!e) return WL_OK;
+  *m->h_err = 0;
+  cudaMemsetAsync(m->err, 0, sizeof(int), m->st);
+  if (e & 1) return fail(WL_ERR_TOKEN_OUT_OF_RANGE, "token id exceeds vocabulary size (device check)");
+  return fail(WL_ERR_TIMEOUT, "a bounded device wait gave up (flags " + std::to_string(e) +
+                                  (e & 8 ? ": tensor-parallel peer exchange" : "") +
+                                  "); results of that call are invalid");
 }
 
 // The whole forward for R rows whose ids/positions/sessions are on device.
@@ -362,7 +465,7 @@ static int run_rows_body(wl_model* m, int R, int nsplit, int lfirst);
 // WL_NO_PDL is set in the environment.
 static int run_rows(wl_model* m, int R, int nsplit, int lfirst) {
   static const bool pdl = getenv("WL_NO_PDL") == nullptr;
-  set_pdl(pdl && m->tp_size == 1);
+  set_pdl(pdl && (m->tp_size == 1 || (m->peer && R <= kPeerRows)));
   const int s = run_rows_body(m, R, nsplit, lfirst);
   set_pdl(false);
   return s;
@@ -375,10 +478,19 @@ static int run_rows_body(wl_model* m, int R, int nsplit, int lfirst) {
   const size_t xpl = (size_t)m->MR * m->d;  // lo-plane offsets
   const size_t apl = (size_t)m->MR * qd;
   const size_t fpl = (size_t)m->MR * m->ffl;
+  // tensor parallel decode: the row-parallel GEMVs push their partial sums to
+  // every rank (exchange 0 after attn_output, 1 after ffn_down) and the next
+  // RMSNorm completes h; prompts use ncclAllReduce
+  const bool peer = tp && m->peer && R <= kPeerRows;
+  unsigned ctas_o = 0, ctas_d = 0;
   WL_TRY(launch_embed(m->embd, m->d, m->V, m->ids, R, m->h, m->err, st));
   for (int l = 0; l < m->L; l++) {
     const Layer& y = m->layers[l];
-    WL_TRY(launch_rmsnorm(m->h, y.attn_norm, R, m->d, m->eps, 0, nullptr, 0, 0.f, m->xn, 2, xpl, st));
+    if (peer && l > 0)
+      WL_TRY(launch_rmsnorm_peer(m->h, y.attn_norm, R, m->d, m->eps, m->xn, xpl,
+                                 peer_take(m, 1, ctas_d, 0), st));
+    else
+      WL_TRY(launch_rmsnorm(m->h, y.attn_norm, R, m->d, m->eps, 0, nullptr, 0, 0.f, m->xn, 2, xpl, st));
     KvPages kv;
     const size_t layer_halves = (size_t)m->n_pages * m->page * m->kvdl;
     kv.k = reinterpret_cast<__half*>(m->kvbuf) + (size_t)l * 2 * layer_halves;
@@ -423,15 +535,19 @@ static int run_rows_body(wl_model* m, int R, int nsplit, int lfirst) {
       a.err = m->err;
       WL_TRY(launch_attention_paged(a, st));
     }
-    {
+    if (peer) {
+      WL_TRY(gemv(m, 1, &y.wo, R, m->att, apl, qd, peer_push(m, 0), &ctas_o));
+      WL_TRY(launch_rmsnorm_peer(m->h, y.ffn_norm, R, m->d, m->eps, m->xn, xpl,
+                                 peer_take(m, 0, ctas_o, 0), st));
+    } else {
       Epilogue e;
       e.kind = (tp && m->tp_rank != 0) ? EPI_F32 : EPI_ADD;  // rank 0 carries the residual
       e.y[0] = m->h;
       e.ldy[0] = m->d;
       WL_TRY(gemv(m, 1, &y.wo, R, m->att, apl, qd, e));
       if (tp) WL_TRY(allreduce_sum(m, m->h, (size_t)R * m->d));
+      WL_TRY(launch_rmsnorm(m->h, y.ffn_norm, R, m->d, m->eps, 0, nullptr, 0, 0.f, m->xn, 2, xpl, st));
     }
-    WL_TRY(launch_rmsnorm(m->h, y.ffn_norm, R, m->d, m->eps, 0, nullptr, 0, 0.f, m->xn, 2, xpl, st));
     {
       Epilogue e;
       e.kind = EPI_SWIGLU;
@@ -441,7 +557,9 @@ static int run_rows_body(wl_model* m, int R, int nsplit, int lfirst) {
       QMat segs[2] = {y.wg, y.wu};
       WL_TRY(gemv(m, 2, segs, R, m->xn, xpl, m->d, e));
     }
-    {
+    if (peer) {
+      WL_TRY(gemv(m, 1, &y.wd, R, m->act, fpl, m->ffl, peer_push(m, 1), &ctas_d));
+    } else {
       Epilogue e;
       e.kind = (tp && m->tp_rank != 0) ? EPI_F32 : EPI_ADD;
       e.y[0] = m->h;
@@ -451,9 +569,13 @@ static int run_rows_body(wl_model* m, int R, int nsplit, int lfirst) {
     }
   }
   const int nl = R - lfirst;
+  if (peer)  // completes the logit rows (or, with none, only drains exchange 1)
+    WL_TRY(launch_rmsnorm_peer(m->h + (size_t)lfirst * m->d, m->out_norm, nl, m->d, m->eps, m->xn,
+                               xpl, peer_take(m, 1, ctas_d, lfirst), st));
   if (nl > 0) {
-    WL_TRY(launch_rmsnorm(m->h + (size_t)lfirst * m->d, m->out_norm, nl, m->d, m->eps, 0, nullptr,
-                          0, 0.f, m->xn, 2, xpl, st));
+    if (!peer)
+      WL_TRY(launch_rmsnorm(m->h + (size_t)lfirst * m->d, m->out_norm, nl, m->d, m->eps, 0, nullptr,
+                            0, 0.f, m->xn, 2, xpl, st));
     Epilogue e;
     e.kind = EPI_F32;
     e.y[0] = m->logits;
@@ -728,7 +850,10 @@ int model_load(wl_ctx* ctx, const char* path, const wl_model_options* o, wl_mode
   WL_TRY(dalloc(&m->err, 1));
   WL_CUDA_TRY(cudaMemsetAsync(m->err, 0, sizeof(int), m->st));
   WL_CUDA_TRY(cudaMallocHost(&m->h_meta, (size_t)3 * MR * sizeof(int)));
+  WL_CUDA_TRY(cudaMallocHost(&m->h_err, sizeof(int)));
+  *m->h_err = 0;
   WL_CUDA_TRY(cudaStreamSynchronize(m->st));
+  WL_TRY(peer_setup(m.get()));
   *out = m.release();
   return WL_OK;
 }
@@ -757,6 +882,10 @@ void model_free(wl_model* m) {
   cudaFree(m->ids);
   cudaFree(m->err);
   cudaFreeHost(m->h_meta);
+  cudaFreeHost(m->h_err);
+  for (int r = 0; r < m->tp_size && r < kMaxPeers; r++)
+    if (m->pbase[r] && m->pbase[r] != m->pmem) cudaIpcCloseMemHandle(m->pbase[r]);
+  cudaFree(m->pmem);
   delete m;
 }
 
@@ -827,9 +956,10 @@ int forward(wl_model* m, wl_session* const* ss, int n, const uint32_t* ids, cons
     WL_TRY(upload_meta(m, n));
     WL_TRY(decode_launch(m, n));
     WL_CUDA_TRY(cudaMemcpyAsync(logits, m->logits, (size_t)n * V * 4, cudaMemcpyDeviceToHost, m->st));
+    WL_CUDA_TRY(cudaMemcpyAsync(m->h_err, m->err, sizeof(int), cudaMemcpyDeviceToHost, m->st));
     WL_CUDA_TRY(cudaStreamSynchronize(m->st));
     for (int i = 0; i < n; i++) ss[i]->len += 1;
-    return WL_OK;
+    return take_err(m);
   }
   // per-session prefill, chunked by max_prefill rows
   size_t id_off = 0, lg_off = 0;
@@ -854,8 +984,10 @@ int forward(wl_model* m, wl_session* const* ss, int n, const uint32_t* ids, cons
                                     cudaMemcpyDeviceToHost, m->st));
         lg_off += (size_t)(c - lfirst) * V;
       }
+      WL_CUDA_TRY(cudaMemcpyAsync(m->h_err, m->err, sizeof(int), cudaMemcpyDeviceToHost, m->st));
       WL_CUDA_TRY(cudaStreamSynchronize(m->st));
       s->len += c;
+      WL_TRY(take_err(m));
     }
     id_off += (size_t)cnt;
   }
@@ -869,6 +1001,9 @@ int decode_step_device(wl_model* m, wl_session* const* ss, int n, const uint32_t
   WL_CHECK_ARG(n <= m->opt.max_batch, "n_sess exceeds max_batch");
   std::lock_guard<std::mutex> lk(m->mu);
   WL_CUDA_TRY(cudaSetDevice(m->dev));
+  // asynchronous API: device errors of earlier calls surface here (the pinned
+  // mirror is refreshed at the end of every call)
+  WL_TRY(take_err(m));
   cudaEvent_t ev = nullptr;
   if (user != m->st) {  // order after the caller's work (0 = the legacy default stream)
     WL_CUDA_TRY(cudaEventCreateWithFlags(&ev, cudaEventDisableTiming));
@@ -885,6 +1020,7 @@ int decode_step_device(wl_model* m, wl_session* const* ss, int n, const uint32_t
   WL_CUDA_TRY(cudaMemcpyAsync(m->row_sess, m->h_meta + 2 * m->MR, (size_t)n * 4, cudaMemcpyHostToDevice, m->st));
   WL_TRY(decode_launch(m, n));
   WL_CUDA_TRY(cudaMemcpyAsync(d_logits, m->logits, (size_t)n * m->V * 4, cudaMemcpyDeviceToDevice, m->st));
+  WL_CUDA_TRY(cudaMemcpyAsync(m->h_err, m->err, sizeof(int), cudaMemcpyDeviceToHost, m->st));
   if (ev) {
     cudaEventRecord(ev, m->st);
     cudaStreamWaitEvent(user, ev, 0);

@@ -91,6 +91,13 @@ struct wl_model {
   // tensor parallel
   int tp_rank = 0, tp_size = 1;
   void* nccl = nullptr;
+  // NVLink peer exchange for decode batches (<= kPeerRows rows): every rank's
+  // buffer (own: pmem; peers: CUDA IPC mappings) holds [flags 2x8 u32][done 2
+  // u32] at byte 0 and slots [2][tp_size][kPeerRows][d] f32 at byte 256
+  bool peer = false;
+  uint8_t* pmem = nullptr;
+  uint8_t* pbase[wl::kMaxPeers] = {};
+  int* h_err = nullptr;  // pinned mirror of err, copied after every call
   std::mutex mu;
 };
 

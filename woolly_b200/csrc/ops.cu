@@ -2,6 +2,7 @@
 // SwiGLU, RoPE, block dequantization.
 #include <cuda_fp16.h>
 
+#include <algorithm>
 #include <cmath>
 #include <cstdint>
 #include <string>
@@ -75,58 +76,78 @@ __global__ void __launch_bounds__(kNormThreads)
 // Same RMSNorm without rotation, one CTA per row with up to 1024 threads: each
 // thread keeps V4 float4 chunks of the row in registers (one read), the sum of
 // squares is reduced across the CTA, and the outputs are stored 4 at a time.
+// With pr.nranks > 0 the row is first completed from the tensor-parallel
+// partial sums the ranks pushed into pr.slots (x += sum over ranks, in rank
+// order, written back to x) after a bounded wait for every rank's arrivals;
+// CTAs at or past nrows only take part in the wait (a drain launch).
 template <int V4>
 __global__ void __launch_bounds__(1024) k_rmsnorm_v(const float* x, const float* w, int dim, float eps,
-                                                    void* y, int y_mode, size_t y_plane) {
+                                                    void* y, int y_mode, size_t y_plane,
+                                                    PeerReduce pr, int nrows) {
   __shared__ float sred[32];
   pdl_wait();
   pdl_trigger();
   const int r = blockIdx.x, tid = threadIdx.x, nt = blockDim.x;
   const int n4 = dim >> 2;
-  const float4* xr = reinterpret_cast<const float4*>(x + (size_t)r * dim);
-  float4 v[V4];
-  float ss = 0.f;
+  if (pr.nranks) peer_wait(pr);
+  if (r < nrows) {
+    const float4* xr = reinterpret_cast<const float4*>(x + (size_t)r * dim);
+    float4 v[V4];
+    float ss = 0.f;
 #pragma unroll
-  for (int j = 0; j < V4; j++) {
-    const int i = tid + j * nt;
-    v[j] = i < n4 ? xr[i] : make_float4(0.f, 0.f, 0.f, 0.f);
-    ss += v[j].x * v[j].x + v[j].y * v[j].y + v[j].z * v[j].z + v[j].w * v[j].w;
-  }
-#pragma unroll
-  for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
-  if ((tid & 31) == 0) sred[tid >> 5] = ss;
-  __syncthreads();
-  if (tid < 32) {
-    float t = tid < (nt >> 5) ? sred[tid] : 0.f;
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) t += __shfl_xor_sync(0xffffffffu, t, off);
-    if (tid == 0) sred[0] = t;
-  }
-  __syncthreads();
-  const float rms = sqrtf(sred[0] / (float)dim + eps);
-  const float4* w4 = reinterpret_cast<const float4*>(w);
-#pragma unroll
-  for (int j = 0; j < V4; j++) {
-    const int i = tid + j * nt;
-    if (i >= n4) break;
-    const float4 wv = w4[i];
-    const float o[4] = {__fdiv_rn(v[j].x, rms) * wv.x, __fdiv_rn(v[j].y, rms) * wv.y,
-                        __fdiv_rn(v[j].z, rms) * wv.z, __fdiv_rn(v[j].w, rms) * wv.w};
-    const size_t at = (size_t)r * dim + 4 * (size_t)i;
-    if (y_mode == 0) {
-      reinterpret_cast<float4*>(y)[at >> 2] = make_float4(o[0], o[1], o[2], o[3]);
-    } else {
-      __half hi[4], lo[4];
-#pragma unroll
-      for (int q = 0; q < 4; q++) {
-        hi[q] = __float2half_rn(o[q]);
-        lo[q] = __float2half_rn(o[q] - __half2float(hi[q]));
+    for (int j = 0; j < V4; j++) {
+      const int i = tid + j * nt;
+      v[j] = i < n4 ? xr[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+      if (pr.nranks && i < n4) {
+        for (int src = 0; src < pr.nranks; src++) {
+          const float4 p = __ldcg(reinterpret_cast<const float4*>(
+                                      pr.slots + ((size_t)src * kPeerRows + pr.row0 + r) * dim) + i);
+          v[j].x += p.x;
+          v[j].y += p.y;
+          v[j].z += p.z;
+          v[j].w += p.w;
+        }
+        reinterpret_cast<float4*>(const_cast<float*>(x) + (size_t)r * dim)[i] = v[j];
       }
-      __half* yh = reinterpret_cast<__half*>(y);
-      *reinterpret_cast<uint2*>(yh + at) = *reinterpret_cast<const uint2*>(hi);
-      if (y_mode == 2) *reinterpret_cast<uint2*>(yh + at + y_plane) = *reinterpret_cast<const uint2*>(lo);
+      ss += v[j].x * v[j].x + v[j].y * v[j].y + v[j].z * v[j].z + v[j].w * v[j].w;
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+    if ((tid & 31) == 0) sred[tid >> 5] = ss;
+    __syncthreads();
+    if (tid < 32) {
+      float t = tid < (nt >> 5) ? sred[tid] : 0.f;
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) t += __shfl_xor_sync(0xffffffffu, t, off);
+      if (tid == 0) sred[0] = t;
+    }
+    __syncthreads();
+    const float rms = sqrtf(sred[0] / (float)dim + eps);
+    const float4* w4 = reinterpret_cast<const float4*>(w);
+#pragma unroll
+    for (int j = 0; j < V4; j++) {
+      const int i = tid + j * nt;
+      if (i >= n4) break;
+      const float4 wv = w4[i];
+      const float o[4] = {__fdiv_rn(v[j].x, rms) * wv.x, __fdiv_rn(v[j].y, rms) * wv.y,
+                          __fdiv_rn(v[j].z, rms) * wv.z, __fdiv_rn(v[j].w, rms) * wv.w};
+      const size_t at = (size_t)r * dim + 4 * (size_t)i;
+      if (y_mode == 0) {
+        reinterpret_cast<float4*>(y)[at >> 2] = make_float4(o[0], o[1], o[2], o[3]);
+      } else {
+        __half hi[4], lo[4];
+#pragma unroll
+        for (int q = 0; q < 4; q++) {
+          hi[q] = __float2half_rn(o[q]);
+          lo[q] = __float2half_rn(o[q] - __half2float(hi[q]));
+        }
+        __half* yh = reinterpret_cast<__half*>(y);
+        *reinterpret_cast<uint2*>(yh + at) = *reinterpret_cast<const uint2*>(hi);
+        if (y_mode == 2) *reinterpret_cast<uint2*>(yh + at + y_plane) = *reinterpret_cast<const uint2*>(lo);
+      }
     }
   }
+  if (pr.nranks) peer_release(pr);
 }
 
 // h[r][j] = E[j*V + id]: token_embd is [d][V] in woolly's reading
@@ -244,6 +265,32 @@ __global__ void k_f16_to_f32(const uint8_t* src, size_t n, float* out) {
 
 }  // namespace
 
+static int rmsnorm_v(const float* x, const float* w, int rows, int dim, float eps, void* y,
+                     int y_mode, size_t y_plane, const PeerReduce& pr, cudaStream_t st) {
+  const int n4 = dim / 4;
+  const int v4 = (n4 + 1023) / 1024;
+  int nt = (n4 + v4 - 1) / v4;
+  nt = std::max(32, (nt + 31) / 32 * 32);
+  const dim3 grid(std::max(rows, 1));
+  switch (v4) {
+    case 1: return launch_k(k_rmsnorm_v<1>, grid, dim3(nt), 0, st, x, w, dim, eps, y, y_mode, y_plane, pr, rows);
+    case 2: return launch_k(k_rmsnorm_v<2>, grid, dim3(nt), 0, st, x, w, dim, eps, y, y_mode, y_plane, pr, rows);
+    case 3: return launch_k(k_rmsnorm_v<3>, grid, dim3(nt), 0, st, x, w, dim, eps, y, y_mode, y_plane, pr, rows);
+    default: return launch_k(k_rmsnorm_v<4>, grid, dim3(nt), 0, st, x, w, dim, eps, y, y_mode, y_plane, pr, rows);
+  }
+}
+
+int launch_rmsnorm_peer(float* x, const float* w, int rows, int dim, float eps, void* y,
+                        size_t y_plane, const PeerReduce& pr, cudaStream_t st) {
+  if (pr.nranks < 1 || pr.nranks > kMaxPeers || !pr.slots || !pr.flags || !pr.done)
+    return fail(WL_ERR_INVALID_ARGUMENT, "rmsnorm_peer: bad peer arguments");
+  if (dim % 4 || dim > 16384 || (reinterpret_cast<uintptr_t>(x) & 15) ||
+      (reinterpret_cast<uintptr_t>(w) & 15) || (reinterpret_cast<uintptr_t>(y) & 15) || y_plane % 4 ||
+      rows < 0 || pr.row0 + rows > kPeerRows)
+    return fail(WL_ERR_INVALID_ARGUMENT, "rmsnorm_peer: dim % 4, alignment or rows out of range");
+  return rmsnorm_v(x, w, rows, dim, eps, y, 2, y_plane, pr, st);
+}
+
 int launch_rmsnorm(const float* x, const float* w, int rows, int dim, float eps, int rope,
                    const int* pos, int head_dim, float theta, void* y, int y_mode,
                    size_t y_plane, cudaStream_t st) {
@@ -258,12 +305,7 @@ int launch_rmsnorm(const float* x, const float* w, int rows, int dim, float eps,
     const int v4 = (n4 + 1023) / 1024;
     int nt = (n4 + v4 - 1) / v4;
     nt = (nt + 31) / 32 * 32;
-    switch (v4) {
-      case 1: return launch_k(k_rmsnorm_v<1>, dim3(rows), dim3(nt), 0, st, x, w, dim, eps, y, y_mode, y_plane);
-      case 2: return launch_k(k_rmsnorm_v<2>, dim3(rows), dim3(nt), 0, st, x, w, dim, eps, y, y_mode, y_plane);
-      case 3: return launch_k(k_rmsnorm_v<3>, dim3(rows), dim3(nt), 0, st, x, w, dim, eps, y, y_mode, y_plane);
-      default: return launch_k(k_rmsnorm_v<4>, dim3(rows), dim3(nt), 0, st, x, w, dim, eps, y, y_mode, y_plane);
-    }
+    return rmsnorm_v(x, w, rows, dim, eps, y, y_mode, y_plane, PeerReduce{}, st);
   }
   size_t smem = rope ? (size_t)dim * sizeof(float) : 0;
   if (rope && (head_dim <= 0 || dim % head_dim || head_dim % 2))

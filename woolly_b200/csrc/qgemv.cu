@@ -309,12 +309,10 @@ __device__ void cluster_finish(const GemvArgs& a, const ClusterRed& R, float* ti
     st_async4(mapa(recv0 + (uint32_t)(((r * R.ipr + j) * P + part) * 16), owner), v,
               mapa(R.bar, owner));
   }
-  if (!red_wait(R.bar)) {
-    if (a.err && threadIdx.x == 0) atomicOr(a.err, 4);
-    return;
-  }
+  const bool got = red_wait(R.bar);
+  if (!got && a.err && threadIdx.x == 0) atomicOr(a.err, 4);
   // finish the owned items, partials summed in rank order
-  for (int j = threadIdx.x; r + C * j < R.nitems; j += blockDim.x) {
+  for (int j = threadIdx.x; got && r + C * j < R.nitems; j += blockDim.x) {
     const int item = r + C * j;
     if (e.kind == EPI_SWIGLU) {
       const int b = item / g4, c = (item - b * g4) * 4;
@@ -356,10 +354,25 @@ __device__ void cluster_finish(const GemvArgs& a, const ClusterRed& R, float* ti
       const int b = item / g4, c = (item - b * g4) * 4;
       float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
       for (int src = 0; src < C; src++) v = f4add(v, R.recv[src * R.ipr + j]);
-      store_out(a, seg, b, col0 + c, v.x);
-      store_out(a, seg, b, col0 + c + 1, v.y);
-      store_out(a, seg, b, col0 + c + 2, v.z);
-      store_out(a, seg, b, col0 + c + 3, v.w);
+      if (e.kind == EPI_PEER) {  // NVLink stores into every rank's receive slot
+        const size_t o = (size_t)b * e.ldy[0] + col0 + c;
+        for (int pr = 0; pr < e.nranks; pr++) *reinterpret_cast<float4*>(e.peer[pr] + o) = v;
+      } else {
+        store_out(a, seg, b, col0 + c, v.x);
+        store_out(a, seg, b, col0 + c + 1, v.y);
+        store_out(a, seg, b, col0 + c + 2, v.z);
+        store_out(a, seg, b, col0 + c + 3, v.w);
+      }
+    }
+  }
+  if (e.kind == EPI_PEER) {
+    // every CTA signals once its stores are out (also after a failed cluster
+    // wait, with the error flag set, so that no rank waits for it in vain)
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      __threadfence_system();
+      for (int pr = 0; pr < e.nranks; pr++)
+        asm volatile("red.release.sys.global.add.u32 [%0], 1;\n" ::"l"(e.pflag[pr]) : "memory");
     }
   }
 }

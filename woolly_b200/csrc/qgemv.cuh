@@ -5,6 +5,8 @@
 
 #include <cstdint>
 
+#include "peer.cuh"
+
 namespace wl {
 
 // Epilogue kinds (applied once the full K sum of an output is known).
@@ -14,7 +16,10 @@ enum EpiKind : int {
   EPI_QKV = 2,     // seg0 -> q f32 (+rope), seg1 -> K pages f16 (+rope), seg2 -> V pages f16
   EPI_SWIGLU = 3,  // seg0 = gate, seg1 = up (paired in one cluster): y[0] gets silu(g)*u as
                    // f16 hi/lo planes (lo plane at y[0] + y_plane)
+  EPI_PEER = 4,    // tensor-parallel partial sums pushed to every rank: peer[r][b*ldy + col] = v
+                   // for r < nranks, then each CTA adds 1 to pflag[r] (release, system scope)
 };
+
 
 // Activation operand of the layout-B GEMV: f16 hi/lo planes, x = hi + lo with
 // lo = f16(x - hi) (~22 significant bits).  Element (b, k) of the hi plane is
@@ -56,6 +61,11 @@ struct Epilogue {
   const int* row_pos = nullptr;   // [B] absolute position of each row
   const int* row_sess = nullptr;  // [B] session slot of each row (page table row)
   KvPages kv{};
+  // EPI_PEER: this rank's receive slot in every rank's buffer (own rank included,
+  // peer pointers through CUDA IPC mappings) and its arrival counter there
+  int nranks = 0;
+  float* peer[kMaxPeers] = {};
+  unsigned* pflag[kMaxPeers] = {};
 };
 
 struct GemvSeg {
