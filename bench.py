@@ -482,6 +482,84 @@ def run_gpu(args):
         dist.destroy_process_group()
 
 
+CFG_70B = dict(hidden=8192, heads=64, kv_heads=8, ff=28672, vocab=32000)
+
+
+def run_tp(args):
+    """Tensor-parallel decode of the 70B shape (Q4_0, `--tp-layers` of its 80
+    layers) across all ranks of the launch: per-step device time (max over
+    ranks) at bs1 and bs16, once with the NVLink peer exchange and once with
+    ncclAllReduce (WL_TP_NCCL=1); one JSON line from rank 0."""
+    import torch
+    import torch.distributed as dist
+    ws, rank, local = dist_init()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    from woolly_b200.gguf import write_synthetic
+    from woolly_b200.model import CudaTransformer, Session, nccl_communicator, nccl_destroy
+    hbm_peak, peak_kind = peaks()
+    L = args.tp_layers
+    os.makedirs(args.tmpdir, exist_ok=True)
+    path = os.path.join(args.tmpdir, f"llama70b_{L}l_q4_0.gguf")
+    if rank == 0 and not os.path.exists(path):
+        write_synthetic(path, **CFG_70B, layers=L, weight_type=2, context_length=4096, seed=SEED)
+    barrier(ws)
+    comm = nccl_communicator(rank, ws) if ws > 1 else None
+    d, ff, kv = CFG_70B["hidden"], CFG_70B["ff"], CFG_70B["hidden"] // 8
+    layer_bytes = (2 * d * d + 2 * d * kv + 3 * d * ff) // 32 * 18
+    prompt, steps = 128, 48
+    res = {}
+    for mode in ("peer", "nccl"):
+        if ws == 1 and mode == "nccl":
+            break
+        if mode == "nccl":
+            os.environ["WL_TP_NCCL"] = "1"
+        m = CudaTransformer(path, device=local, tp_rank=rank, tp_size=ws, nccl_comm=comm,
+                            max_sessions=BATCH, max_context=prompt + 2 * steps + 16, max_batch=BATCH,
+                            max_prefill=prompt)
+        rng = np.random.default_rng(SEED)
+        sess = [Session(m) for _ in range(BATCH)]
+        for s in sess:
+            s.infer_last(rng.integers(0, CFG_70B["vocab"], prompt).tolist())
+        logits = torch.empty(BATCH, CFG_70B["vocab"], device=dev)
+        stream = torch.cuda.current_stream(dev).cuda_stream
+        out = {}
+        for B in (1, BATCH):
+            ids = torch.from_numpy(rng.integers(0, CFG_70B["vocab"], (steps + 3, B)).astype(np.int32)).to(dev)
+            for t in range(3):
+                m.decode_step_device(sess[:B], ids[t].data_ptr(), logits.data_ptr(), stream)
+            torch.cuda.synchronize()
+            barrier(ws)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for t in range(3, steps + 3):
+                m.decode_step_device(sess[:B], ids[t].data_ptr(), logits.data_ptr(), stream)
+            e1.record()
+            torch.cuda.synchronize()
+            ms = max_over_ranks(e0.elapsed_time(e1), ws) / steps
+            gbs = L * layer_bytes / ws / (ms / 1e3) / 1e9  # projection weights each GPU reads
+            out[f"bs{B}"] = {"ms_per_step": round(ms, 4), "us_per_layer": round(ms * 1e3 / L, 2),
+                             "tok_s_80_layers_est": round(B * 1e3 / (ms * 80 / L), 1),
+                             "weight_GBps_per_gpu": round(gbs, 1),
+                             "frac_of_measured_hbm": round(gbs / hbm_peak, 3)}
+        for s in sess:
+            s.close()
+        m.close()
+        res[mode] = out
+        barrier(ws)
+    os.environ.pop("WL_TP_NCCL", None)
+    if comm is not None:
+        nccl_destroy(comm)
+    if rank == 0:
+        print(json.dumps({"metric": "tensor-parallel decode step, 70B-shape Q4_0", "n_gpus": ws,
+                          "config": {"workload": f"llama2-70b-shape Q4_0, {L} of 80 layers, TP{ws}, "
+                                                 f"prompt {prompt}, {steps} timed decode steps",
+                                     "parallelism": f"tp{ws}"},
+                          "results": res, "data": "synthetic", "peak_kind": peak_kind}), flush=True)
+    if ws > 1:
+        dist.destroy_process_group()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -491,12 +569,17 @@ def main():
     ap.add_argument("--impl", default="woolly_b200", choices=["woolly_b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-sweep", action="store_true", help="skip the GEMV/GEMM shape sweep")
+    ap.add_argument("--tp", action="store_true",
+                    help="tensor-parallel 70B-shape decode across the launch's ranks (peer vs NCCL)")
+    ap.add_argument("--tp-layers", type=int, default=8)
     ap.add_argument("--tmpdir", default=os.environ.get("WOOLLY_BENCH_DIR", "/tmp/woolly_bench"))
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":
         run_reference(args)
+    elif args.tp:
+        run_tp(args)
     else:
         run_gpu(args)
 
