@@ -31,13 +31,9 @@ namespace {
 
 constexpr int kAttnThreads = 128;
 constexpr int kPage = 16;    // tokens per KV page
-#ifndef WL_ATTN_TILE_PAGES
-#define WL_ATTN_TILE_PAGES 2
-#endif
 #ifndef WL_ATTN_RING
 #define WL_ATTN_RING 3
 #endif
-constexpr int kTilePages = WL_ATTN_TILE_PAGES;  // pages per softmax round
 constexpr int kRingA = WL_ATTN_RING;            // tiles in flight per CTA
 constexpr int kTile = 64;    // tokens per softmax tile (f32 path)
 
@@ -87,8 +83,12 @@ __device__ __forceinline__ void put_out(void* out, size_t plane, size_t i, float
 }
 
 // ---------------------------------------------------------------- paged kernel
-template <int HD, int G>
+// TPG pages per softmax round: 2 when the launch has fewer (KV head, row)
+// pairs than SMs, 1 (shorter rounds, more resident CTAs, more context splits)
+// when it has at least one per SM.
+template <int HD, int G, int TPG>
 __global__ void __launch_bounds__(kAttnThreads) k_attn_paged(const AttnArgs a, float scale) {
+  constexpr int kTilePages = TPG;
   constexpr int CHUNK = kPage * HD;        // halves per (page, head) chunk
   constexpr int LPT = HD / 8;              // lanes per token in the score phase
   constexpr int TPP = kAttnThreads / LPT;  // tokens per pass
@@ -294,19 +294,34 @@ __global__ void k_attn_combine(const float* part_o, const float* part_ml, int he
   put_out(out, out_plane, (size_t)r * ldo + (size_t)h * HD + d, L > 0.f ? acc * (1.0f / L) : 0.f);
 }
 
-template <int HD, int G>
-int launch_paged_g(const AttnArgs& a, float scale, cudaStream_t st) {
+template <int HD, int G, int TPG>
+int launch_paged_t(const AttnArgs& a, float scale, cudaStream_t st) {
   static unsigned done = 0;
-  const size_t smem = (size_t)kRingA * kTilePages * 2 * kPage * HD * sizeof(__half);
+  const size_t smem = (size_t)kRingA * TPG * 2 * kPage * HD * sizeof(__half);
   int dev = 0;
   cudaGetDevice(&dev);
   if (!(done >> (dev & 31) & 1u)) {
-    WL_CUDA_TRY(cudaFuncSetAttribute(k_attn_paged<HD, G>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     (int)smem));
+    WL_CUDA_TRY(cudaFuncSetAttribute(k_attn_paged<HD, G, TPG>,
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     done |= 1u << (dev & 31);
   }
-  return launch_k(k_attn_paged<HD, G>, dim3(a.kv_heads, a.rows, a.nsplit), dim3(kAttnThreads), smem,
-                  st, a, scale);
+  return launch_k(k_attn_paged<HD, G, TPG>, dim3(a.kv_heads, a.rows, a.nsplit), dim3(kAttnThreads),
+                  smem, st, a, scale);
+}
+
+int device_sms() {
+  static int cache[32] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  int& n = cache[dev & 31];
+  if (!n && cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) n = 148;
+  return n;
+}
+
+template <int HD, int G>
+int launch_paged_g(const AttnArgs& a, float scale, cudaStream_t st) {
+  return a.rows * a.kv_heads >= device_sms() ? launch_paged_t<HD, G, 1>(a, scale, st)
+                                             : launch_paged_t<HD, G, 2>(a, scale, st);
 }
 
 template <int HD>
@@ -451,8 +466,11 @@ int launch_f32_hd(const float* q, const float* k, const float* v, int rows, int 
 }  // namespace
 
 int attention_plan_splits(int rows, int kv_heads, int max_len, int num_sms) {
+  // CTAs to aim for: 2 per SM for few (KV head, row) pairs (2-page rounds);
+  // kAttnSplitCtasPerSm once there is one pair per SM (1-page rounds; the
+  // split partials then stay within kAttnSplitCtasPerSm * SMs + rows rows)
   const int ctas = rows * kv_heads;
-  const int target = 2 * num_sms;
+  const int target = (ctas >= num_sms ? kAttnSplitCtasPerSm : 2) * num_sms;
   int ns = (target + ctas - 1) / ctas;
   const int pages = (max_len + kPage - 1) / kPage;
   const int by_len = (pages + 3) / 4;  // at least ~4 pages per split

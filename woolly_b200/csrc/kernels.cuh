@@ -34,6 +34,9 @@ int launch_attention_f32(const float* q, const float* k, const float* v, int row
                          int heads, int kv_heads, int hd, int window, float* out,
                          cudaStream_t st);
 
+// Context splits per (KV head, row) for the paged kernel; the partial buffers
+// need rows * splits <= kAttnSplitCtasPerSm * num_sms + rows.
+constexpr int kAttnSplitCtasPerSm = 12;
 int attention_plan_splits(int rows, int kv_heads, int max_len, int num_sms);
 
 // y = x / sqrt(mean(x^2) + eps) * w per row; optional NeoX rope per head.

@@ -841,7 +841,7 @@ int model_load(wl_ctx* ctx, const char* path, const wl_model_options* o, wl_mode
   WL_TRY(dalloc(&m->att, (size_t)2 * MR * m->Hl * m->hd));
   WL_TRY(dalloc(&m->act, (size_t)2 * MR * m->ffl));
   WL_TRY(dalloc(&m->logits, (size_t)MR * V));
-  m->part_rows = (size_t)2 * m->sms + MR;
+  m->part_rows = (size_t)kAttnSplitCtasPerSm * m->sms + MR;
   WL_TRY(dalloc(&m->part_o, m->part_rows * m->Hl * m->hd));
   WL_TRY(dalloc(&m->part_ml, m->part_rows * m->Hl * 2));
   WL_TRY(dalloc(&m->row_pos, (size_t)MR));
