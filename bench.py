@@ -488,8 +488,8 @@ CFG_70B = dict(hidden=8192, heads=64, kv_heads=8, ff=28672, vocab=32000)
 def run_tp(args):
     """Tensor-parallel decode of the 70B shape (Q4_0, `--tp-layers` of its 80
     layers) across all ranks of the launch: per-step device time (max over
-    ranks) at bs1 and bs16, once with the NVLink peer exchange and once with
-    ncclAllReduce (WL_TP_NCCL=1); one JSON line from rank 0."""
+    ranks) at bs1 and bs16, once with ncclAllReduce (the default) and once
+    with the NVLink peer exchange (WL_TP_PEER=1); one JSON line from rank 0."""
     import torch
     import torch.distributed as dist
     ws, rank, local = dist_init()
@@ -509,11 +509,11 @@ def run_tp(args):
     layer_bytes = (2 * d * d + 2 * d * kv + 3 * d * ff) // 32 * 18
     prompt, steps = 128, 48
     res = {}
-    for mode in ("peer", "nccl"):
-        if ws == 1 and mode == "nccl":
+    for mode in ("nccl", "peer"):
+        if ws == 1 and mode == "peer":
             break
-        if mode == "nccl":
-            os.environ["WL_TP_NCCL"] = "1"
+        if mode == "peer":
+            os.environ["WL_TP_PEER"] = "1"
         m = CudaTransformer(path, device=local, tp_rank=rank, tp_size=ws, nccl_comm=comm,
                             max_sessions=BATCH, max_context=prompt + 2 * steps + 16, max_batch=BATCH,
                             max_prefill=prompt)
@@ -547,7 +547,7 @@ def run_tp(args):
         m.close()
         res[mode] = out
         barrier(ws)
-    os.environ.pop("WL_TP_NCCL", None)
+    os.environ.pop("WL_TP_PEER", None)
     if comm is not None:
         nccl_destroy(comm)
     if rank == 0:

@@ -1,8 +1,8 @@
 """Tensor parallelism on 2 GPUs: each rank loads its Megatron shard of a seeded
 model (CudaTransformer(tp_rank, tp_size, nccl_comm)); after attn_output and
-ffn_down the partial sums are joined either by the NVLink peer exchange (the
-GEMV pushes them to every rank, the next RMSNorm adds them up) or, with
-WL_TP_NCCL set, by ncclAllReduce.  Rank 0's logits for a prompt
+ffn_down the partial sums are joined either by ncclAllReduce (the default)
+or, with WL_TP_PEER set, by the NVLink peer exchange (the GEMV pushes them to
+every rank, the next RMSNorm adds them up).  Rank 0's logits for a prompt
 and three teacher-forced decode steps must match the CPU oracle within the
 model-level tolerance (max |d| <= 1e-2).  Skipped with fewer than two GPUs.
 """
@@ -22,8 +22,8 @@ TOL = 1e-2
 
 def _rank(rank, world, port, path, prompt, steps, q, mode):
     import torch.distributed as dist
-    if mode == "nccl":
-        os.environ["WL_TP_NCCL"] = "1"
+    if mode == "peer":
+        os.environ["WL_TP_PEER"] = "1"
     from woolly_b200.model import CudaTransformer, Session, nccl_communicator, nccl_destroy
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     torch.cuda.set_device(rank)

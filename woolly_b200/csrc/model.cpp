@@ -401,12 +401,13 @@ static PeerReduce peer_take(const wl_model* m, int par, unsigned expect, int row
 }
 
 // One buffer per rank, mapped into every other rank through CUDA IPC (handles
-// exchanged with one ncclAllGather).  Left off (NCCL all-reduce instead) when
-// WL_TP_NCCL is set, for more than kMaxPeers ranks, or when a row-parallel
-// weight cannot take the fast GEMV.
+// exchanged with one ncclAllGather).  Opt-in with WL_TP_PEER set at load: on
+// 2 B200s the exchange measured slower than ncclAllReduce (70B shape: bs1 171
+// vs 147 us per layer), so NCCL is the default.  Also left off for more than
+// kMaxPeers ranks or when a row-parallel weight cannot take the fast GEMV.
 static int peer_setup(wl_model* m) {
   const int T = m->tp_size, rk = m->tp_rank;
-  if (T < 2 || T > kMaxPeers || getenv("WL_TP_NCCL")) return WL_OK;
+  if (T < 2 || T > kMaxPeers || !getenv("WL_TP_PEER")) return WL_OK;
   for (const Layer& y : m->layers)
     for (const QMat* q : {&y.wo, &y.wd})
       if (!block_bytes(q->type) || !qgemv_b_fast_ok(q->type, q->K, q->N, q->pitch, q->w)) return WL_OK;
