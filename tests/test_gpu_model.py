@@ -87,6 +87,17 @@ def test_teacher_forced_parity(tiny_models, name):
     run_parity(tiny_models[name], prompts, steps=12, max_sessions=4, max_context=128)
 
 
+def test_wide_batch_decode_parity(tmp_path):
+    """16 sessions x 16 KV heads = 256 (KV head, row) pairs per decode step,
+    at least one per SM: the attention runs 1-page rounds with context splits
+    and the combine kernel, the bs16 decode configuration of 7B-shape models."""
+    p = write_synthetic(str(tmp_path / "wide.gguf"), hidden=1024, layers=2, heads=16,
+                        kv_heads=16, ff=1024, vocab=512, weight_type=Q4_0, seed=11)
+    rng = np.random.default_rng(12)
+    prompts = [rng.integers(0, 512, int(n)).tolist() for n in rng.integers(20, 90, 16)]
+    run_parity(p, prompts, steps=6, max_sessions=16, max_context=128, max_batch=16)
+
+
 def test_decode_without_graphs_matches(tiny_models):
     prompts = [[9, 8, 7], [1]]
     run_parity(tiny_models["gqa_q4_0"], prompts, steps=5, max_sessions=2, max_context=64,
