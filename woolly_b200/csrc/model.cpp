@@ -853,6 +853,7 @@ int model_load(wl_ctx* ctx, const char* path, const wl_model_options* o, wl_mode
   WL_CUDA_TRY(cudaMallocHost(&m->h_meta, (size_t)3 * MR * sizeof(int)));
   WL_CUDA_TRY(cudaMallocHost(&m->h_err, sizeof(int)));
   *m->h_err = 0;
+  WL_CUDA_TRY(cudaEventCreateWithFlags(&m->err_ev, cudaEventDisableTiming));
   WL_CUDA_TRY(cudaStreamSynchronize(m->st));
   WL_TRY(peer_setup(m.get()));
   *out = m.release();
@@ -884,6 +885,7 @@ void model_free(wl_model* m) {
   cudaFree(m->err);
   cudaFreeHost(m->h_meta);
   cudaFreeHost(m->h_err);
+  if (m->err_ev) cudaEventDestroy(m->err_ev);
   for (int r = 0; r < m->tp_size && r < kMaxPeers; r++)
     if (m->pbase[r] && m->pbase[r] != m->pmem) cudaIpcCloseMemHandle(m->pbase[r]);
   cudaFree(m->pmem);
@@ -1002,9 +1004,12 @@ int decode_step_device(wl_model* m, wl_session* const* ss, int n, const uint32_t
   WL_CHECK_ARG(n <= m->opt.max_batch, "n_sess exceeds max_batch");
   std::lock_guard<std::mutex> lk(m->mu);
   WL_CUDA_TRY(cudaSetDevice(m->dev));
-  // asynchronous API: device errors of earlier calls surface here (the pinned
-  // mirror is refreshed at the end of every call)
-  WL_TRY(take_err(m));
+  // asynchronous API: device errors of earlier calls surface here, once the
+  // copy into the pinned mirror that the previous call queued has completed
+  if (m->err_pending && cudaEventQuery(m->err_ev) == cudaSuccess) {
+    m->err_pending = false;
+    WL_TRY(take_err(m));
+  }
   cudaEvent_t ev = nullptr;
   if (user != m->st) {  // order after the caller's work (0 = the legacy default stream)
     WL_CUDA_TRY(cudaEventCreateWithFlags(&ev, cudaEventDisableTiming));
@@ -1021,7 +1026,11 @@ int decode_step_device(wl_model* m, wl_session* const* ss, int n, const uint32_t
   WL_CUDA_TRY(cudaMemcpyAsync(m->row_sess, m->h_meta + 2 * m->MR, (size_t)n * 4, cudaMemcpyHostToDevice, m->st));
   WL_TRY(decode_launch(m, n));
   WL_CUDA_TRY(cudaMemcpyAsync(d_logits, m->logits, (size_t)n * m->V * 4, cudaMemcpyDeviceToDevice, m->st));
-  WL_CUDA_TRY(cudaMemcpyAsync(m->h_err, m->err, sizeof(int), cudaMemcpyDeviceToHost, m->st));
+  if (!m->err_pending) {  // one copy in flight at a time: the host reads h_err only after it
+    WL_CUDA_TRY(cudaMemcpyAsync(m->h_err, m->err, sizeof(int), cudaMemcpyDeviceToHost, m->st));
+    WL_CUDA_TRY(cudaEventRecord(m->err_ev, m->st));
+    m->err_pending = true;
+  }
   if (ev) {
     cudaEventRecord(ev, m->st);
     cudaStreamWaitEvent(user, ev, 0);

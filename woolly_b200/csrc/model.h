@@ -98,6 +98,8 @@ struct wl_model {
   uint8_t* pmem = nullptr;
   uint8_t* pbase[wl::kMaxPeers] = {};
   int* h_err = nullptr;  // pinned mirror of err, copied after every call
+  cudaEvent_t err_ev = nullptr;  // recorded after the asynchronous step's copy into h_err
+  bool err_pending = false;      // err_ev recorded and not yet consumed
   std::mutex mu;
 };
 
