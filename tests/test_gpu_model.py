@@ -98,6 +98,34 @@ def test_wide_batch_decode_parity(tmp_path):
     run_parity(p, prompts, steps=6, max_sessions=16, max_context=128, max_batch=16)
 
 
+def test_batch_engine_matches_one_at_a_time(tiny_models):
+    """Continuous batching (woolly_b200.engine) on the GPU runtime: five greedy
+    requests through three session slots give the same tokens as generating
+    them one at a time, except where the top two logits are within 1e-3
+    (batched and single-row GEMVs sum in different orders)."""
+    from woolly_b200.engine import BatchEngine, GenerationConfig
+    rng = np.random.default_rng(21)
+    prompts = [rng.integers(3, 1024, int(n)).tolist() for n in (5, 17, 2, 33, 9)]
+    cfg = GenerationConfig(max_tokens=8, eos_below=0)
+    runs = []
+    for mb in (3, 1):
+        m = CudaTransformer(tiny_models["gqa_q4_0"], max_sessions=3, max_context=64, max_batch=3)
+        eng = BatchEngine(m, max_batch=mb, keep_logits=True)
+        ids = [eng.submit(p, cfg) for p in prompts]
+        eng.run()
+        runs.append([eng.finished[i] for i in ids])
+        eng.close()
+        m.close()
+    for a, b in zip(*runs):
+        assert len(a.tokens) == len(b.tokens) == 8
+        for t, (ta, tb) in enumerate(zip(a.tokens, b.tokens)):
+            assert np.abs(a.logits[t] - b.logits[t]).max() <= 1e-3
+            if ta != tb:
+                top2 = np.sort(b.logits[t])[-2:]
+                assert top2[1] - top2[0] <= 1e-3
+                break
+
+
 def test_decode_without_graphs_matches(tiny_models):
     prompts = [[9, 8, 7], [1]]
     run_parity(tiny_models["gqa_q4_0"], prompts, steps=5, max_sessions=2, max_context=64,

@@ -106,6 +106,16 @@ class CudaTransformer:
     def model_type(self) -> str:
         return self.config["architecture"]
 
+    @property
+    def max_batch(self) -> int:
+        """Most sessions one batched decode step takes (load option)."""
+        return int(self._opts.max_batch)
+
+    @property
+    def max_context(self) -> int:
+        """Tokens a session can hold (load option)."""
+        return int(self._opts.max_context)
+
     def vocab_size(self) -> int:
         return self.config["vocab_size"]
 
