@@ -61,3 +61,38 @@ def test_model_load_rejects_missing_file():
     h = C.c_void_p()
     st = lib.wl_model_load_gguf(None, b"/nonexistent.gguf", C.byref(model_options()), C.byref(h))
     assert st == _lib.WL_ERR_INVALID_ARGUMENT
+
+
+def test_qtile_bytes_arithmetic():
+    """Tiled decode copy size: whole (256-column, 64-row) tiles of
+    512 * block_bytes each, equal to the GGUF size for whole tiles."""
+    lib = _lib.lib()
+    for t, S in ((2, 18), (3, 20), (8, 34)):
+        assert lib.wl_qtile_bytes(t, 4096, 4096) == 4096 * 4096 // 32 * S
+        assert lib.wl_qtile_bytes(t, 80, 288) == 2 * 2 * 512 * S  # ragged: 2 groups x 2 stages
+    assert lib.wl_qtile_bytes(2, 64, 48) == 0   # N % 32 != 0
+    assert lib.wl_qtile_bytes(12, 64, 64) == 0  # Q4_K has no tiled copy
+    assert lib.wl_qtile_bytes(2, 0, 64) == 0
+
+
+def test_new_entry_points_reject_bad_arguments_on_the_host():
+    lib = _lib.lib()
+    buf = (C.c_uint8 * 64)()
+    p = C.cast(buf, C.c_void_p)
+    assert lib.wl_qtile_repack(12, p, 64, 64, p, None) == _lib.WL_ERR_UNSUPPORTED
+    assert lib.wl_qtile_repack(2, p, 64, 48, p, None) == _lib.WL_ERR_INVALID_ARGUMENT
+    assert lib.wl_qtile_repack(2, None, 64, 64, p, None) == _lib.WL_ERR_INVALID_ARGUMENT
+    assert lib.wl_qgemv_tiled(2, p, 40, 64, p, 0, 1, p, None) == _lib.WL_ERR_INVALID_ARGUMENT  # K % 16
+    assert lib.wl_qgemv_tiled(2, p, 64, 64, p, 0, 0, p, None) == _lib.WL_ERR_INVALID_ARGUMENT  # B = 0
+    # tensor-parallel reduce: 1..8 ranks, <= 32 rows, non-null buffers
+    args = dict(w=p, dim=64, eps=1e-5, slots=p, counters=p, expect=1, y=p, yp=0, err=None)
+
+    def reduce(h, rows, nranks):
+        return lib.wl_tp_reduce_rmsnorm(h, args["w"], rows, args["dim"], args["eps"], args["slots"],
+                                        nranks, args["counters"], args["expect"], args["y"],
+                                        args["yp"], args["err"], None)
+    assert reduce(None, 1, 2) == _lib.WL_ERR_INVALID_ARGUMENT
+    assert reduce(p, 1, 9) == _lib.WL_ERR_INVALID_ARGUMENT
+    assert reduce(p, 33, 2) == _lib.WL_ERR_INVALID_ARGUMENT
+    assert reduce(p, 1, 0) == _lib.WL_ERR_INVALID_ARGUMENT
+    assert lib.wl_last_error()
