@@ -726,6 +726,21 @@ static float* load_f32(const or_gguf* g, const char* name, uint64_t expect, int*
   return out;
 }
 
+/* ggml orientation: a [ne0 = K, ne1 = N] tensor holds N rows of K values
+ * (row o, column k at o*K + k); the forward reads [K][N] (k*N + o), so
+ * layout A transposes once at load.  For token_embd [d, V] this turns token
+ * rows E[t*d + j] into the reference's E[j*V + t]. */
+static int to_layout_b(float** p, size_t K, size_t N) {
+  float* t = (float*)malloc(sizeof(float) * K * N);
+  if (!t) return OR_ERR_INVALID;
+  const float* s = *p;
+  for (size_t o = 0; o < N; o++)
+    for (size_t k = 0; k < K; k++) t[k * N + o] = s[o * K + k];
+  free(*p);
+  *p = t;
+  return OR_OK;
+}
+
 void or_model_free(or_model* m) {
   if (!m) return;
   for (int l = 0; m->layers && l < m->L; l++) {
@@ -780,11 +795,13 @@ int or_model_load(const char* path, const or_opts* opts, or_model** out) {
   size_t d = (size_t)m->d, kvd = (size_t)m->kvd, ff = (size_t)m->ff, V = (size_t)m->V;
   m->embd = load_f32(g, "token_embd.weight", d * V, &st);
   if (st) goto fail;
+  if (m->opts.layout_a && (st = to_layout_b(&m->embd, d, V))) goto fail;
   m->out_norm = load_f32(g, "output_norm.weight", d, &st);
   if (st) goto fail;
   if (or_gguf_find(g, "output.weight") >= 0) {
     m->out_w = load_f32(g, "output.weight", d * V, &st);
     if (st) goto fail;
+    if (m->opts.layout_a && (st = to_layout_b(&m->out_w, d, V))) goto fail;
   } else {
     m->out_w = m->embd;
     m->tied = 1;
@@ -793,19 +810,20 @@ int or_model_load(const char* path, const or_opts* opts, or_model** out) {
   for (int l = 0; l < m->L; l++) {
     char nm[128];
     or_layer* y = &m->layers[l];
-#define LD(field, suffix, n)                                  \
-  snprintf(nm, sizeof nm, "blk.%d." suffix, l);               \
-  y->field = load_f32(g, nm, (n), &st);                       \
-  if (st) goto fail;
-    LD(attn_norm, "attn_norm.weight", d)
-    LD(ffn_norm, "ffn_norm.weight", d)
-    LD(wq, "attn_q.weight", d * d)
-    LD(wk, "attn_k.weight", d * kvd)
-    LD(wv, "attn_v.weight", d * kvd)
-    LD(wo, "attn_output.weight", d * d)
-    LD(wg, "ffn_gate.weight", d * ff)
-    LD(wu, "ffn_up.weight", d * ff)
-    LD(wd, "ffn_down.weight", ff * d)
+#define LD(field, suffix, K, N)                                                   \
+  snprintf(nm, sizeof nm, "blk.%d." suffix, l);                                   \
+  y->field = load_f32(g, nm, (K) * (N), &st);                                     \
+  if (st) goto fail;                                                              \
+  if ((N) > 1 && m->opts.layout_a && (st = to_layout_b(&y->field, (K), (N)))) goto fail;
+    LD(attn_norm, "attn_norm.weight", d, 1)
+    LD(ffn_norm, "ffn_norm.weight", d, 1)
+    LD(wq, "attn_q.weight", d, d)
+    LD(wk, "attn_k.weight", d, kvd)
+    LD(wv, "attn_v.weight", d, kvd)
+    LD(wo, "attn_output.weight", d, d)
+    LD(wg, "ffn_gate.weight", d, ff)
+    LD(wu, "ffn_up.weight", d, ff)
+    LD(wd, "ffn_down.weight", ff, d)
 #undef LD
   }
   or_gguf_close(g);

@@ -97,6 +97,8 @@ typedef struct or_opts {
   int swiglu;      /* 0 exact, 1 AVX2 approximation, 2 NEON approximation */
   int threads;     /* OpenMP threads, <=0: library default */
   int max_layers;  /* 0 = all layers; >0 loads only the first N (baseline sampling) */
+  int layout_a;    /* 0: the reference's reading of every 2-D weight as [ne0][ne1]
+                      (layout B); 1: ggml's, ne1 rows of ne0 (llama.cpp files) */
 } or_opts;
 
 typedef struct or_model or_model;

@@ -27,7 +27,7 @@ def build() -> str:
 
 class Opts(C.Structure):
     _fields_ = [("rope", C.c_int), ("window", C.c_int), ("swiglu", C.c_int),
-                ("threads", C.c_int), ("max_layers", C.c_int)]
+                ("threads", C.c_int), ("max_layers", C.c_int), ("layout_a", C.c_int)]
 
 
 _lib = None
@@ -152,8 +152,8 @@ class Model:
     """Oracle model: every weight dequantized to f32, KV-cache forward."""
 
     def __init__(self, path: str, rope: int = 0, window: int = 0, swiglu: int = 0,
-                 threads: int = 0, max_layers: int = 0):
-        self._o = Opts(rope, window, swiglu, threads, max_layers)
+                 threads: int = 0, max_layers: int = 0, layout_a: int = 0):
+        self._o = Opts(rope, window, swiglu, threads, max_layers, layout_a)
         self._h = P()
         st = lib().or_model_load(str(path).encode(), C.byref(self._o), C.byref(self._h))
         if st:

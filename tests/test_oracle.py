@@ -11,6 +11,7 @@ Python package, present in this image) and numpy's IEEE f16 widening.
 import json
 import os
 import struct
+import tempfile
 
 import numpy as np
 import pytest
@@ -231,3 +232,50 @@ def test_k_quant_short_buffer_and_zero_stubs():
         O.dequantize(b"\x00" * 209, Q6_K, 256)
     for qt in (6, 7, Q5_K, Q8_K):  # Q5_0, Q5_1, Q5_K, Q8_K: zeros (dequantize.rs:539-607)
         assert not O.dequantize(b"\x01" * 400, qt, 256).any()
+
+
+def test_layout_a_reads_ggml_rows():
+    """Oracle option layout_a (ggml orientation, llama.cpp files): an F32
+    model whose 2-D weights hold ggml rows (N rows of K for dims [K, N];
+    token_embd as one row per token) gives bit-identical logits to the same
+    weights stored in the reference's reading ([K][N]) with layout_a off."""
+    import gguf_builder as gb
+    d, L, H, KVH, ff, V = 64, 2, 4, 2, 96, 40
+    kvd = d // H * KVH
+    rng = np.random.default_rng(3)
+    meta = [("general.architecture", gb.STR, "llama"), ("llama.embedding_length", gb.U32, d),
+            ("llama.block_count", gb.U32, L), ("llama.attention.head_count", gb.U32, H),
+            ("llama.attention.head_count_kv", gb.U32, KVH), ("llama.feed_forward_length", gb.U32, ff),
+            ("llama.vocab_size", gb.U32, V), ("llama.context_length", gb.U32, 64),
+            ("llama.attention.layer_norm_epsilon", gb.F32, 1e-5)]
+    mats = [("token_embd.weight", d, V), ("output.weight", d, V)]
+    vecs = [("output_norm.weight", d)]
+    for l in range(L):
+        vecs += [(f"blk.{l}.attn_norm.weight", d), (f"blk.{l}.ffn_norm.weight", d)]
+        mats += [(f"blk.{l}.attn_q.weight", d, d), (f"blk.{l}.attn_k.weight", d, kvd),
+                 (f"blk.{l}.attn_v.weight", d, kvd), (f"blk.{l}.attn_output.weight", d, d),
+                 (f"blk.{l}.ffn_gate.weight", d, ff), (f"blk.{l}.ffn_up.weight", d, ff),
+                 (f"blk.{l}.ffn_down.weight", ff, d)]
+    tb, ta = [], []
+    for name, n in vecs:
+        v = (1 + 0.02 * rng.standard_normal(n)).astype(np.float32).tobytes()
+        tb.append((name, [n], 0, len(v), v))
+        ta.append((name, [n], 0, len(v), v))
+    for name, K, N in mats:
+        w = (0.1 * rng.standard_normal((K, N))).astype(np.float32)  # reference reading [K][N]
+        tb.append((name, [K, N], 0, w.nbytes, w.tobytes()))
+        ta.append((name, [K, N], 0, w.nbytes, np.ascontiguousarray(w.T).tobytes()))  # ggml rows
+    paths = []
+    for tag, ts in (("b", tb), ("a", ta)):
+        p = os.path.join(tempfile.mkdtemp(), f"m_{tag}.gguf")
+        with open(p, "wb") as f:
+            f.write(gb.build(meta, ts))
+        paths.append(p)
+    ids = [3, 17, 5, 39, 0, 11]
+    out = []
+    for p, la in ((paths[0], 0), (paths[1], 1), (paths[1], 0)):
+        m = O.Model(p, layout_a=la)
+        out.append(m.forward(m.new_kv(16), ids, all_rows=True))
+        m.close()
+    assert np.array_equal(out[0], out[1])
+    assert not np.allclose(out[0], out[2])  # the same bytes read the other way differ
