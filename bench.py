@@ -74,7 +74,7 @@ class Clocks:
         try:
             self.p = subprocess.Popen(
                 ["nvidia-smi", "-i", str(self.dev), f"--query-gpu={self.FIELDS}",
-                 "--format=csv,noheader,nounits", "-lms", "100"],
+                 "--format=csv,noheader,nounits", "-lms", "20"],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.t = threading.Thread(target=self._read, daemon=True)
             self.t.start()
@@ -147,18 +147,38 @@ def model_path(tmpdir, rank, ws):
 
 
 # ---------------------------------------------------------------- CPU baseline
-def cpu_baseline(path, steps=2, ctx=640):
-    """Times the CPU oracle (plain-C restatement of woolly's forward, f32
-    weights as woolly's dequantization cache holds them, OpenMP over all host
-    cores) on a bounded sample: 16 sessions x `steps` decode steps at context
-    `ctx`, once with 1 and once with 2 of 32 layers loaded; the per-step time
-    is extrapolated linearly to 32 layers."""
+def oracle_model_path(tmpdir):
+    """The same seeded 7B-shape GGUF, written by the oracle's own writer
+    (byte-identical to the product's), so the CPU legs never load the product
+    library."""
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle as O
-    cores = os.cpu_count() or 1
+    path = os.path.join(tmpdir, "llama7b_q4_0.gguf")
+    if not os.path.exists(path):
+        O.synth_gguf(path, **CFG, weight_type=O.Q4_0, context_length=4096, seed=SEED)
+    return path
+
+
+def cpu_model():
+    try:
+        with open("/proc/cpuinfo") as f:
+            for ln in f:
+                if ln.startswith("model name"):
+                    return ln.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+def cpu_step_time(path, threads, steps, ctx):
+    """Seconds per 16-session decode step of the CPU oracle, extrapolated to
+    32 layers from runs with 1 and 2 layers loaded (the per-layer cost is the
+    difference; the rest is the embedding, final norm and LM head)."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
     times = {}
     for nl in (1, 2):
-        m = O.Model(path, threads=cores, max_layers=nl)
+        m = O.Model(path, threads=threads, max_layers=nl)
         kvs = [m.new_kv(ctx + steps + 2) for _ in range(BATCH)]
         for i, kv in enumerate(kvs):
             kv.fill_synthetic(ctx, seed=i)
@@ -173,11 +193,25 @@ def cpu_baseline(path, steps=2, ctx=640):
         m.close()
     per_layer = max(times[2] - times[1], 1e-9)
     fixed = max(times[1] - per_layer, 0.0)
-    step = fixed + CFG["layers"] * per_layer
+    return fixed + CFG["layers"] * per_layer
+
+
+def cpu_baseline(path, steps=2, ctx=640):
+    """Times the CPU oracle (plain-C restatement of woolly's forward, f32
+    weights as woolly's dequantization cache holds them) on a bounded sample:
+    16 sessions x `steps` decode steps at context `ctx`, with 1 and 2 of 32
+    layers loaded, extrapolated to 32 layers; once with OpenMP over all host
+    cores (the reported value) and once on one thread (woolly's QKV loops are
+    single-threaded, tensor_utils_simd.rs:1050-1081)."""
+    cores = os.cpu_count() or 1
+    step = cpu_step_time(path, cores, steps, ctx)
+    step1 = cpu_step_time(path, 1, 1, ctx)
     return {"value": BATCH / step, "unit": "tok/s", "cores": cores, "kind": "port",
-            "sample": f"{BATCH} sessions x {steps} decode steps at context {ctx} with 1 and 2 of "
-                      f"32 layers loaded, f32 weights; step time extrapolated to 32 layers "
-                      f"({step * 1e3:.0f} ms/step)"}
+            "cpu_model": cpu_model(), "single_thread_tok_s": BATCH / step1,
+            "sample": f"{BATCH} sessions x {steps} decode steps (1 on one thread) at context {ctx} "
+                      f"with 1 and 2 of 32 layers loaded, f32 weights; step time extrapolated to "
+                      f"32 layers ({step * 1e3:.0f} ms/step on {cores} threads, "
+                      f"{step1 * 1e3:.0f} ms/step on 1)"}
 
 
 def run_reference(args):
@@ -186,7 +220,7 @@ def run_reference(args):
         return
     os.makedirs(args.tmpdir, exist_ok=True)
     with tempfile.TemporaryDirectory(dir=args.tmpdir) as td:
-        path = model_path(td, 0, 1)
+        path = oracle_model_path(td)
         steps = max(1, min(args.steps, 3))
         res = None
         t0 = time.perf_counter()

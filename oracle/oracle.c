@@ -605,24 +605,37 @@ void or_rope_neox(float* x, const size_t* positions, int batch, int seq, int hea
 static int g_threads = 0;
 
 /* Layout-B projection, tensor_utils.rs:118-157 (matmul_simple):
- * y[s, o] = sum_k x[s, k] * W[k*N + o], summed in k order per output. */
+ * y[s, o] = sum_k x[s, k] * W[k*N + o], summed in k order per output.
+ * Blocked over (row chunk, output chunk) so the accumulators stay in L1; the
+ * order of the sum for each output is unchanged (k = 0, 1, ..., K-1). */
 void or_matmul_b(const float* x, int rows, int K, const float* W, int N, float* y) {
-  const int CH = 256;
-  int nch = (N + CH - 1) / CH;
-#pragma omp parallel for schedule(static) num_threads(g_threads > 0 ? g_threads : omp_get_max_threads())
-  for (int c = 0; c < nch; c++) {
-    int o0 = c * CH, o1 = o0 + CH < N ? o0 + CH : N;
-    for (int s = 0; s < rows; s++)
-      for (int o = o0; o < o1; o++) y[(size_t)s * N + o] = 0.0f;
-    for (int k = 0; k < K; k++) {
-      const float* wr = W + (size_t)k * N;
-      for (int s = 0; s < rows; s++) {
-        float xv = x[(size_t)s * K + k];
-        float* yr = y + (size_t)s * N;
-        for (int o = o0; o < o1; o++) yr[o] += xv * wr[o];
+  enum { OC = 64, RC = 32 };
+  int noc = (N + OC - 1) / OC, nrc = (rows + RC - 1) / RC;
+#pragma omp parallel for collapse(2) schedule(dynamic) num_threads(g_threads > 0 ? g_threads : omp_get_max_threads())
+  for (int rc = 0; rc < nrc; rc++)
+    for (int c = 0; c < noc; c++) {
+      int o0 = c * OC, on = o0 + OC < N ? OC : N - o0;
+      int r0 = rc * RC, rn = r0 + RC < rows ? RC : rows - r0;
+      float acc[RC][OC];
+      for (int s = 0; s < rn; s++)
+        for (int o = 0; o < OC; o++) acc[s][o] = 0.0f;
+      for (int k = 0; k < K; k++) {
+        const float* wr = W + (size_t)k * N + o0;
+        if (on == OC) {
+          for (int s = 0; s < rn; s++) {
+            float xv = x[(size_t)(r0 + s) * K + k];
+            for (int o = 0; o < OC; o++) acc[s][o] += xv * wr[o];
+          }
+        } else {
+          for (int s = 0; s < rn; s++) {
+            float xv = x[(size_t)(r0 + s) * K + k];
+            for (int o = 0; o < on; o++) acc[s][o] += xv * wr[o];
+          }
+        }
       }
+      for (int s = 0; s < rn; s++)
+        memcpy(y + (size_t)(r0 + s) * N + o0, acc[s], sizeof(float) * (size_t)on);
     }
-  }
 }
 
 /* GQA attention with a KV cache: lazy_transformer.rs:360-434.

@@ -129,6 +129,19 @@ void or_matmul_b(const float* x, int rows, int K, const float* W, int N, float* 
 void or_attention(const float* q, const float* kc, const float* vc, int rows, int past,
                   int heads, int kv_heads, int hd, int window, float* out);
 
+
+/* ---- seeded synthetic GGUF writer (synth.c; byte-identical to the
+ * product's wl_synth_gguf for the same configuration) ---- */
+typedef struct or_synth_cfg {
+  uint32_t hidden, layers, heads, kv_heads, ff, vocab, context_length;
+  uint32_t weight_type;    /* OR_Q4_0 / OR_Q4_1 / OR_Q8_0 / OR_F32 */
+  uint32_t output_type;    /* 0xFFFFFFFF: tied (no output.weight) */
+  uint32_t sliding_window; /* 0 = none */
+  float rope_theta, norm_eps;
+  uint64_t seed;
+} or_synth_cfg;
+int or_synth_gguf(const char* path, const or_synth_cfg* cfg);
+
 #ifdef __cplusplus
 }
 #endif

@@ -19,7 +19,7 @@ F32, F16, Q4_0, Q4_1, Q8_0 = 0, 1, 2, 3, 8
 
 
 def build() -> str:
-    src = [os.path.join(HERE, f) for f in ("oracle.c", "oracle.h", "Makefile")]
+    src = [os.path.join(HERE, f) for f in ("oracle.c", "synth.c", "oracle.h", "Makefile")]
     if not os.path.exists(LIB) or os.path.getmtime(LIB) < max(map(os.path.getmtime, src)):
         subprocess.run(["make", "-s", "-C", HERE], check=True)
     return LIB
@@ -28,6 +28,14 @@ def build() -> str:
 class Opts(C.Structure):
     _fields_ = [("rope", C.c_int), ("window", C.c_int), ("swiglu", C.c_int),
                 ("threads", C.c_int), ("max_layers", C.c_int), ("layout_a", C.c_int)]
+
+
+class SynthCfg(C.Structure):
+    _fields_ = [("hidden", C.c_uint32), ("layers", C.c_uint32), ("heads", C.c_uint32),
+                ("kv_heads", C.c_uint32), ("ff", C.c_uint32), ("vocab", C.c_uint32),
+                ("context_length", C.c_uint32), ("weight_type", C.c_uint32),
+                ("output_type", C.c_uint32), ("sliding_window", C.c_uint32),
+                ("rope_theta", C.c_float), ("norm_eps", C.c_float), ("seed", C.c_uint64)]
 
 
 _lib = None
@@ -50,6 +58,7 @@ _SIGS = {
     "or_kv_fill_synthetic": (C.c_int, [P, C.c_int, C.c_uint64]),
     "or_forward": (C.c_int, [P, P, P, C.c_int, P, C.c_int]),
     "or_decode_batch": (C.c_int, [P, C.POINTER(P), C.c_int, P, P]),
+    "or_synth_gguf": (C.c_int, [C.c_char_p, C.POINTER(SynthCfg)]),
     "or_rms_norm": (None, [P, P, C.c_int, C.c_int, C.c_float, P]),
     "or_swiglu": (None, [P, P, C.c_size_t, C.c_int, P]),
     "or_rope_neox": (None, [P, P, C.c_int, C.c_int, C.c_int, C.c_int, C.c_float]),
@@ -76,6 +85,22 @@ def _f32(a) -> np.ndarray:
 
 def half_to_float(h: int) -> float:
     return lib().or_half_to_float(h)
+
+
+def synth_gguf(path: str, *, hidden: int, layers: int, heads: int, kv_heads: int, ff: int,
+               vocab: int, weight_type: int = Q4_0, output_type: int | None = None,
+               tied: bool = False, context_length: int = 4096, sliding_window: int = 0,
+               rope_theta: float = 10000.0, norm_eps: float = 1e-5, seed: int = 0) -> str:
+    """The seeded LLaMA-shape GGUF of the product's writer, written by the
+    oracle's own C writer (synth.c), so CPU-only legs never load the product
+    library."""
+    cfg = SynthCfg(hidden, layers, heads, kv_heads, ff, vocab, context_length, weight_type,
+                   0xFFFFFFFF if tied else (weight_type if output_type is None else output_type),
+                   sliding_window, rope_theta, norm_eps, seed)
+    st = lib().or_synth_gguf(str(path).encode(), C.byref(cfg))
+    if st:
+        raise ValueError(f"or_synth_gguf status {st}")
+    return str(path)
 
 
 def dequantize(data: bytes | np.ndarray, ggml_type: int, n: int) -> np.ndarray:

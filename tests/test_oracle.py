@@ -279,3 +279,24 @@ def test_layout_a_reads_ggml_rows():
         m.close()
     assert np.array_equal(out[0], out[1])
     assert not np.allclose(out[0], out[2])  # the same bytes read the other way differ
+
+
+@pytest.mark.parametrize("kw", [
+    dict(hidden=256, layers=2, heads=4, kv_heads=2, ff=512, vocab=512, weight_type=O.Q4_0, seed=3),
+    dict(hidden=256, layers=1, heads=2, kv_heads=2, ff=256, vocab=320, weight_type=O.Q4_1,
+         sliding_window=16, seed=4),
+    dict(hidden=512, layers=1, heads=4, kv_heads=1, ff=768, vocab=256, weight_type=O.Q8_0,
+         tied=True, norm_eps=1e-6, rope_theta=5e5, seed=5),
+    dict(hidden=128, layers=1, heads=2, kv_heads=1, ff=256, vocab=64, weight_type=O.F32,
+         output_type=O.Q4_0, context_length=64, seed=6),
+    # > 65536 values per tensor: several seed chunks
+    dict(hidden=512, layers=1, heads=8, kv_heads=8, ff=1024, vocab=1024, weight_type=O.Q4_0, seed=9),
+])
+def test_oracle_writer_matches_product_writer(tmp_path, kw):
+    """The oracle's own GGUF writer (used where the product library must not
+    load) writes exactly the bytes of the product's wl_synth_gguf."""
+    from woolly_b200.gguf import write_synthetic
+    a = O.synth_gguf(str(tmp_path / "oracle.gguf"), **kw)
+    b = write_synthetic(str(tmp_path / "product.gguf"), **kw)
+    with open(a, "rb") as fa, open(b, "rb") as fb:
+        assert fa.read() == fb.read()
