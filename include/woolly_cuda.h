@@ -207,9 +207,12 @@ int wl_qgemm(int ggml_type, const void* W, int K, int N, const float* x, int M, 
  *    streams, or different threads on one device) race and must be ordered by
  *    the caller; each call rewrites every element it reads, so nothing
  *    carries over between calls;
- *  - the first call on a device looks up the array's device address (once
- *    per device, with that device current); make that first call before any
- *    stream capture;
+ *  - the array's device address is looked up once per device, with that
+ *    device current: by wl_init(device) or, without it, by the first call on
+ *    the device.  That set-up may load the library's device code for the
+ *    array (lazy module loading), i.e. take device memory once, so do it
+ *    (wl_init, or a first small call) before reserving the process's memory
+ *    budget and before any stream capture; later calls allocate nothing;
  *  - N % 32 == 0, K % 16 == 0 and 16-byte aligned weight rows. */
 int wl_qgemv_noalloc(int ggml_type, const void* W, int K, int N, const float* x, int B,
                      float* y, void* stream);

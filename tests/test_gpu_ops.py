@@ -393,4 +393,21 @@ def test_tp_reduce_wait_gives_up():
     assert int(err.item()) & 8
     x = torch.ones(4, device="cuda")
     assert float((x * 2).sum().item()) == 8.0
+    # the counters re-arm to 0 (the short one does not wrap around), so the
+    # next exchange waits for its own arrivals and reads the right slots
+    assert counters.cpu().tolist() == [0] * (T + 1)
+    rng = np.random.default_rng(3)
+    parts = rng.standard_normal((T, 32, dim)).astype(np.float32)
+    h0 = rng.standard_normal((rows, dim)).astype(np.float32)
+    h.copy_(dev(h0))
+    slots.copy_(dev(parts))
+    counters[:T] = expect
+    err.zero_()
+    _tp_reduce(h, w, slots, counters, expect, err)
+    assert int(err.item()) == 0
+    ref_h = h0.copy()
+    for r in range(T):
+        ref_h = (ref_h + parts[r, :rows]).astype(np.float32)
+    assert np.array_equal(h.cpu().numpy(), ref_h)
+    assert counters.cpu().tolist() == [0] * (T + 1)
 

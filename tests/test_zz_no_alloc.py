@@ -51,6 +51,13 @@ def test_noalloc_matches_allocating_entry(qt, K, N, B):
         torch.cuda.synchronize()
         err = (got - ref).abs().max().item()
         assert err <= GEMV_TOL * ref.abs().max().item() + 1e-6, (call, err)
+    # after the first call (set-up done), a call takes no device memory:
+    # the device's free memory is unchanged across it
+    free0 = torch.cuda.mem_get_info()[0]
+    _lib.check(lib.wl_qgemv_noalloc(qt, W.data_ptr(), K, N, x.data_ptr(), B, got.data_ptr(),
+                                    stream))
+    torch.cuda.synchronize()
+    assert torch.cuda.mem_get_info()[0] == free0
 
 
 def test_noalloc_rejects_oversize():

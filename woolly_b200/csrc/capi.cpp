@@ -29,6 +29,7 @@ void session_free(wl_session*);
 int forward(wl_model*, wl_session* const*, int, const uint32_t*, const int*, float*, int);
 int decode_step_device(wl_model*, wl_session* const*, int, const uint32_t*, float*, cudaStream_t);
 int decode_kernel_count(const wl_model*, int);
+int noalloc_setup_current_device();
 int nccl_unique_id(void*);
 int nccl_comm_init(int, const void*, int, void**);
 int nccl_comm_destroy(void*);
@@ -453,6 +454,7 @@ int wl_init(int device, wl_ctx** out) {
   WL_CUDA_TRY(cudaGetDeviceProperties(&p, device));
   if (p.major < 10)
     return fail(WL_ERR_UNSUPPORTED, std::string("woolly-b200 needs an sm_100 GPU, found ") + p.name);
+  WL_TRY(noalloc_setup_current_device());
   auto* c = new wl_ctx();
   c->device = device;
   c->num_sms = p.multiProcessorCount;

@@ -451,7 +451,9 @@ static int take_err(wl_model* m) {
   const int e = *m->h_err;
   if (!e) return WL_OK;
   *m->h_err = 0;
-  cudaMemsetAsync(m->err, 0, sizeof(int), m->st);
+  // clear only the bits reported here: calls queued after the copy may have
+  // set others, which the next read reports
+  launch_err_clear(m->err, e, m->st);
   if (e & 1) return fail(WL_ERR_TOKEN_OUT_OF_RANGE, "token id exceeds vocabulary size (device check)");
   return fail(WL_ERR_TIMEOUT, "a bounded device wait gave up (flags " + std::to_string(e) +
                                   (e & 8 ? ": tensor-parallel peer exchange" : "") +
@@ -851,6 +853,8 @@ int model_load(wl_ctx* ctx, const char* path, const wl_model_options* o, wl_mode
   WL_TRY(dalloc(&m->err, 1));
   WL_CUDA_TRY(cudaMemsetAsync(m->err, 0, sizeof(int), m->st));
   WL_CUDA_TRY(cudaMallocHost(&m->h_meta, (size_t)3 * MR * sizeof(int)));
+  WL_CUDA_TRY(cudaMallocHost(&m->h_ring, (size_t)wl_model::kMetaRing * 2 * MR * sizeof(int)));
+  for (auto& e : m->ring_ev) WL_CUDA_TRY(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
   WL_CUDA_TRY(cudaMallocHost(&m->h_err, sizeof(int)));
   *m->h_err = 0;
   WL_CUDA_TRY(cudaEventCreateWithFlags(&m->err_ev, cudaEventDisableTiming));
@@ -884,6 +888,9 @@ void model_free(wl_model* m) {
   cudaFree(m->ids);
   cudaFree(m->err);
   cudaFreeHost(m->h_meta);
+  cudaFreeHost(m->h_ring);
+  for (auto& e : m->ring_ev)
+    if (e) cudaEventDestroy(e);
   cudaFreeHost(m->h_err);
   if (m->err_ev) cudaEventDestroy(m->err_ev);
   for (int r = 0; r < m->tp_size && r < kMaxPeers; r++)
@@ -1010,31 +1017,45 @@ int decode_step_device(wl_model* m, wl_session* const* ss, int n, const uint32_t
     m->err_pending = false;
     WL_TRY(take_err(m));
   }
-  cudaEvent_t ev = nullptr;
-  if (user != m->st) {  // order after the caller's work (0 = the legacy default stream)
-    WL_CUDA_TRY(cudaEventCreateWithFlags(&ev, cudaEventDisableTiming));
-    cudaEventRecord(ev, user);
-    cudaStreamWaitEvent(m->st, ev, 0);
+  // order after the caller's work (0 = the legacy default stream); the guard
+  // also orders the caller's stream after this step on every return path
+  struct StreamJoin {
+    cudaStream_t user, own;
+    cudaEvent_t ev = nullptr;
+    ~StreamJoin() {
+      if (!ev) return;
+      cudaEventRecord(ev, own);
+      cudaStreamWaitEvent(user, ev, 0);
+      cudaEventDestroy(ev);
+    }
+  } join{user, m->st};
+  if (user != m->st) {
+    WL_CUDA_TRY(cudaEventCreateWithFlags(&join.ev, cudaEventDisableTiming));
+    WL_CUDA_TRY(cudaEventRecord(join.ev, user));
+    WL_CUDA_TRY(cudaStreamWaitEvent(m->st, join.ev, 0));
   }
   for (int i = 0; i < n; i++) WL_TRY(ensure_pages(m, ss[i], ss[i]->len + 1));
+  // per-step positions go through a ring slot the previous user of which has
+  // been copied: this call returns before its copies run
+  const int k = (int)(m->ring_next++ % wl_model::kMetaRing);
+  if (m->ring_used[k]) WL_CUDA_TRY(cudaEventSynchronize(m->ring_ev[k]));
+  int* meta = m->h_ring + (size_t)k * 2 * m->MR;
   for (int i = 0; i < n; i++) {
-    m->h_meta[m->MR + i] = ss[i]->len;
-    m->h_meta[2 * m->MR + i] = ss[i]->slot;
+    meta[i] = ss[i]->len;
+    meta[m->MR + i] = ss[i]->slot;
+    m->h_meta[m->MR + i] = ss[i]->len;  // host copy read by the eager (graph-less) launch
   }
   WL_CUDA_TRY(cudaMemcpyAsync(m->ids, d_ids, (size_t)n * 4, cudaMemcpyDeviceToDevice, m->st));
-  WL_CUDA_TRY(cudaMemcpyAsync(m->row_pos, m->h_meta + m->MR, (size_t)n * 4, cudaMemcpyHostToDevice, m->st));
-  WL_CUDA_TRY(cudaMemcpyAsync(m->row_sess, m->h_meta + 2 * m->MR, (size_t)n * 4, cudaMemcpyHostToDevice, m->st));
+  WL_CUDA_TRY(cudaMemcpyAsync(m->row_pos, meta, (size_t)n * 4, cudaMemcpyHostToDevice, m->st));
+  WL_CUDA_TRY(cudaMemcpyAsync(m->row_sess, meta + m->MR, (size_t)n * 4, cudaMemcpyHostToDevice, m->st));
+  WL_CUDA_TRY(cudaEventRecord(m->ring_ev[k], m->st));
+  m->ring_used[k] = true;
   WL_TRY(decode_launch(m, n));
   WL_CUDA_TRY(cudaMemcpyAsync(d_logits, m->logits, (size_t)n * m->V * 4, cudaMemcpyDeviceToDevice, m->st));
   if (!m->err_pending) {  // one copy in flight at a time: the host reads h_err only after it
     WL_CUDA_TRY(cudaMemcpyAsync(m->h_err, m->err, sizeof(int), cudaMemcpyDeviceToHost, m->st));
     WL_CUDA_TRY(cudaEventRecord(m->err_ev, m->st));
     m->err_pending = true;
-  }
-  if (ev) {
-    cudaEventRecord(ev, m->st);
-    cudaStreamWaitEvent(user, ev, 0);
-    cudaEventDestroy(ev);
   }
   for (int i = 0; i < n; i++) ss[i]->len += 1;
   return WL_OK;

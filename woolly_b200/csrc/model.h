@@ -84,7 +84,15 @@ struct wl_model {
   uint32_t* ids = nullptr;
   int* err = nullptr;
   // pinned staging for per-step metadata
-  int* h_meta = nullptr;  // [3][MR]: ids, pos, sess
+  int* h_meta = nullptr;  // [3][MR]: ids, pos, sess (synchronous calls)
+  // asynchronous decode steps: a ring of pinned [2][MR] (pos, sess) slots; a
+  // slot is rewritten only after the event recorded behind its copies has
+  // completed, so a host that runs ahead never changes a copy still queued
+  static constexpr int kMetaRing = 8;
+  int* h_ring = nullptr;
+  cudaEvent_t ring_ev[kMetaRing] = {};
+  bool ring_used[kMetaRing] = {};
+  unsigned ring_next = 0;
   // decode graphs keyed by batch size
   std::map<int, cudaGraphExec_t> graphs;
   std::map<int, int> graph_warm;

@@ -53,6 +53,17 @@ int planes_on_current_device(__half** out) {
   return WL_OK;
 }
 
+}  // namespace
+
+// Set-up of the current device (wl_init calls it, so that the device code that
+// holds the array is loaded while the caller still budgets memory).
+int noalloc_setup_current_device() {
+  __half* p = nullptr;
+  return planes_on_current_device(&p);
+}
+
+namespace {
+
 int block_bytes(int t) { return t == WL_Q4_0 ? 18 : t == WL_Q4_1 ? 20 : t == WL_Q8_0 ? 34 : 0; }
 
 }  // namespace

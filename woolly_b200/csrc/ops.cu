@@ -341,6 +341,14 @@ int launch_rope(const float* x, float* out, const int* pos, float base, int batc
   return WL_OK;
 }
 
+__global__ void k_err_clear(int* err, int bits) { atomicAnd(err, ~bits); }
+
+int launch_err_clear(int* err, int bits, cudaStream_t st) {
+  k_err_clear<<<1, 1, 0, st>>>(err, bits);
+  WL_CUDA_TRY(cudaGetLastError());
+  return WL_OK;
+}
+
 int launch_dequant(int type, const void* blocks, size_t n, float* out, cudaStream_t st) {
   if (!n) return WL_OK;
   if (type == WL_F32) {

@@ -53,7 +53,18 @@ __device__ __forceinline__ void peer_release(const PeerReduce& pr) {
   if (threadIdx.x == 0) {
     const unsigned old = atomicAdd(pr.done, 1u);
     if (old == gridDim.x - 1) {
-      for (int s = 0; s < pr.nranks; s++) atomicSub(pr.flags + s, pr.expect);
+      // take off at most `expect`: after a wait that gave up, a counter that
+      // never reached it returns to 0 instead of wrapping around (which would
+      // let the next exchange pass its wait on stale slots)
+      for (int s = 0; s < pr.nranks; s++) {
+        unsigned* f = pr.flags + s;
+        unsigned v = *(volatile unsigned*)f;
+        for (int it = 0; it < 64; it++) {
+          const unsigned w = atomicCAS(f, v, v - min(v, pr.expect));
+          if (w == v) break;
+          v = w;
+        }
+      }
       atomicExch(pr.done, 0u);
     }
   }
