@@ -29,6 +29,11 @@
 #include <cuda_fp16.h>
 
 #include <algorithm>
+#include <climits>
+#include <cstdint>
+#include <map>
+#include <mutex>
+#include <tuple>
 #include <cstdlib>
 #include <string>
 
@@ -1128,6 +1133,66 @@ bool qgemv_a_fast_ok(int type, int K, int N, int pitch, const void* W) {
          (reinterpret_cast<uintptr_t>(W) & 15) == 0;
 }
 
+namespace {
+// Layout-B kernel instance a launch of `a` uses (as dispatch_b picks it).
+using KernB = void (*)(const GemvArgs);
+template <int T, bool TLD>
+KernB kernel_b_t(int B) {
+  switch ((B + 7) / 8) {
+    case 1: return B <= 4 ? k_qgemv_b<T, 1, true, TLD> : k_qgemv_b<T, 1, false, TLD>;
+    case 2: return k_qgemv_b<T, 2, false, TLD>;
+    case 3: return k_qgemv_b<T, 3, false, TLD>;
+    default: return k_qgemv_b<T, 4, false, TLD>;
+  }
+}
+KernB kernel_b(const GemvArgs& a) {
+  if (a.type == WL_Q4_0) return a.tiled ? kernel_b_t<WL_Q4_0, true>(a.B) : kernel_b_t<WL_Q4_0, false>(a.B);
+  if (a.type == WL_Q4_1) return a.tiled ? kernel_b_t<WL_Q4_1, true>(a.B) : kernel_b_t<WL_Q4_1, false>(a.B);
+  return a.tiled ? kernel_b_t<WL_Q8_0, true>(a.B) : kernel_b_t<WL_Q8_0, false>(a.B);
+}
+
+std::mutex g_cap_mu;
+std::map<std::tuple<int, const void*, int, int, size_t>, int> g_cap;
+
+// CTAs of (cx, cy) clusters of the kernel that can be resident at once on
+// this device (registers, shared memory and cluster placement together),
+// from the occupancy calculator; cached per (device, kernel, cluster shape).
+// A grid larger than this runs in two waves.
+int cluster_capacity(KernB k, int cx, int cy, size_t smem) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 0;
+  const auto key = std::make_tuple(dev, (const void*)k, cx, cy, smem);
+  {
+    std::lock_guard<std::mutex> lk(g_cap_mu);
+    auto it = g_cap.find(key);
+    if (it != g_cap.end()) return it->second;
+  }
+  // the launch path sets these too; the occupancy query needs them first
+  cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+  cudaFuncSetAttribute(k, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(cx, cy);
+  cfg.blockDim = dim3(kThreadsB);
+  cfg.dynamicSmemBytes = smem;
+  cudaLaunchAttribute at;
+  at.id = cudaLaunchAttributeClusterDimension;
+  at.val.clusterDim.x = cx;
+  at.val.clusterDim.y = cy;
+  at.val.clusterDim.z = 1;
+  cfg.attrs = &at;
+  cfg.numAttrs = 1;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, k, &cfg) != cudaSuccess) {
+    cudaGetLastError();
+    n = -1;  // unknown: do not constrain the plan
+  }
+  const int cap = n < 0 ? INT32_MAX : n * cx * cy;
+  std::lock_guard<std::mutex> lk(g_cap_mu);
+  g_cap[key] = cap;
+  return cap;
+}
+}  // namespace
+
 void qgemv_plan(GemvArgs& a, int layout, int num_sms) {
   int groups = 0;
   for (int s = 0; s < a.nseg; s++) groups += a.seg[s].groups;
@@ -1147,6 +1212,19 @@ void qgemv_plan(GemvArgs& a, int layout, int num_sms) {
   c = std::max(1, std::min({c, cmax, units}));
   a.kchunk = (units + c - 1) / c * gran;
   a.csplit = (a.K + a.kchunk - 1) / a.kchunk;
+  if (layout != WL_LAYOUT_B) return;
+  // clusters must also fit one wave: a GPC holds whole clusters only, so a
+  // split that fits by CTA count can still leave CTAs for a second wave
+  const int NT = (std::min(a.B, 32) + 7) / 8;
+  const size_t sm = a.type == WL_Q4_0 ? smem_b<WL_Q4_0>(NT)
+                    : a.type == WL_Q4_1 ? smem_b<WL_Q4_1>(NT) : smem_b<WL_Q8_0>(NT);
+  const int cx = a.epi.kind == EPI_SWIGLU ? 2 : 1;
+  const KernB k = kernel_b(a);
+  while (a.csplit > 1 && groups * a.csplit > cluster_capacity(k, cx, a.csplit, sm)) {
+    c = a.csplit - 1;
+    a.kchunk = (units + c - 1) / c * gran;
+    a.csplit = (a.K + a.kchunk - 1) / a.kchunk;
+  }
 }
 
 size_t qtile_bytes(int type, int K, int N) {
