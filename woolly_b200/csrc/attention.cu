@@ -31,10 +31,7 @@ namespace {
 
 constexpr int kAttnThreads = 128;
 constexpr int kPage = 16;    // tokens per KV page
-#ifndef WL_ATTN_RING
-#define WL_ATTN_RING 3
-#endif
-constexpr int kRingA = WL_ATTN_RING;            // tiles in flight per CTA
+constexpr int kRingA = 3;            // tiles in flight per CTA
 constexpr int kTile = 64;    // tokens per softmax tile (f32 path)
 
 // ---------------------------------------------------------------- mbarrier / bulk copy
@@ -296,15 +293,10 @@ __global__ void k_attn_combine(const float* part_o, const float* part_ml, int he
 
 template <int HD, int G, int TPG>
 int launch_paged_t(const AttnArgs& a, float scale, cudaStream_t st) {
-  static unsigned done = 0;
   const size_t smem = (size_t)kRingA * TPG * 2 * kPage * HD * sizeof(__half);
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (!(done >> (dev & 31) & 1u)) {
+  if (first_use_on_device((const void*)k_attn_paged<HD, G, TPG>))
     WL_CUDA_TRY(cudaFuncSetAttribute(k_attn_paged<HD, G, TPG>,
                                      cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    done |= 1u << (dev & 31);
-  }
   return launch_k(k_attn_paged<HD, G, TPG>, dim3(a.kv_heads, a.rows, a.nsplit), dim3(kAttnThreads),
                   smem, st, a, scale);
 }

@@ -5,6 +5,8 @@
 
 #include <algorithm>
 #include <cstring>
+#include <mutex>
+#include <set>
 #include <string>
 
 #include "common.h"
@@ -18,6 +20,15 @@ namespace wl {
 thread_local std::string g_err;
 void set_error(const std::string& m) { g_err = m; }
 thread_local bool g_pdl = false;
+
+bool first_use_on_device(const void* key) {
+  static std::mutex mu;
+  static std::set<std::pair<int, const void*>> seen;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::lock_guard<std::mutex> lk(mu);
+  return seen.insert({dev, key}).second;
+}
 bool pdl_enabled() { return g_pdl; }
 void set_pdl(bool on) { g_pdl = on; }
 

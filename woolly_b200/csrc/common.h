@@ -12,6 +12,9 @@ namespace wl {
 void set_error(const std::string& msg);
 // programmatic dependent launch for the kernels the calling thread enqueues
 void set_pdl(bool on);
+// true exactly once per (current device, key) across all host threads: guards
+// per-device one-time set-up such as kernel attributes
+bool first_use_on_device(const void* key);
 inline int fail(int code, const std::string& msg) {
   set_error(msg);
   return code;

@@ -798,9 +798,8 @@ int model_load(wl_ctx* ctx, const char* path, const wl_model_options* o, wl_mode
   }
   // ---- tiled decode copies (the GEMV's lane-ready layout) of every quantized projection ----
   {
-    static const bool off = getenv("WL_NO_TILED") != nullptr;
     std::vector<QMat*> mats;
-    if (!off) {
+    {
       for (Layer& y : m->layers)
         for (QMat* q : {&y.wq, &y.wk, &y.wv, &y.wo, &y.wg, &y.wu, &y.wd}) mats.push_back(q);
       mats.push_back(&m->out);

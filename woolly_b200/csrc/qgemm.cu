@@ -420,13 +420,8 @@ __global__ void __launch_bounds__(kGThreads, 1) k_qgemm_b(const GemvArgs a, int 
 
 template <int T>
 int launch_t(const GemvArgs& a, int M, int ntiles, cudaStream_t st) {
-  static unsigned attr_done = 0;
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (!(attr_done >> (dev & 31) & 1u)) {
+  if (first_use_on_device((const void*)k_qgemm_b<T>))
     WL_CUDA_TRY(cudaFuncSetAttribute(k_qgemm_b<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, kGSmem));
-    attr_done |= 1u << (dev & 31);
-  }
   return launch_k(k_qgemm_b<T>, dim3(ntiles, (M + kGM - 1) / kGM), dim3(kGThreads), (size_t)kGSmem,
                   st, a, M);
 }

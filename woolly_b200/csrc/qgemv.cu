@@ -62,29 +62,20 @@ struct QT<WL_Q8_0> {
 };
 
 constexpr int kThreads = 128;  // layout A
-#ifndef WL_GEMV_B_THREADS
-#define WL_GEMV_B_THREADS 128
-#endif
-constexpr int kThreadsB = WL_GEMV_B_THREADS;  // layout B: warps 4..7 take the second half of each stage's k-steps
+constexpr int kThreadsB = 128;  // layout B: warps 4..7 take the second half of each stage's k-steps
 constexpr int kKParts = kThreadsB / 128;
 constexpr int kRows = 64;  // matrix rows per pipeline stage
 constexpr int kStages = 4;  // layout A
-#ifndef WL_GEMV_STAGES_B
-#define WL_GEMV_STAGES_B 4
-#endif
 // layout-B pipeline depth: batch tiles of up to 16 rows keep more stages in flight
-__host__ __device__ constexpr int stages_b(int NT) { return NT <= 2 ? WL_GEMV_STAGES_B : 4; }
+__host__ __device__ constexpr int stages_b(int NT) { return 4; }
 constexpr int kGroupBlocks = 8;  // quant blocks per tile row
 constexpr int kColsB = 256;      // output columns per CTA, layout B
 constexpr int kColsA = 64;       // output rows per CTA, layout A
 constexpr int kMaxCluster = 16;
-#ifndef WL_PLAN_CTAS_PER_SM
-#define WL_PLAN_CTAS_PER_SM 3
-#endif
 // Layout-B CTAs per SM the K-split planner aims for, when their shared memory
 // fits (measured on the 7B decode step: 3 beats 2 by 5%; 4 no longer fits and
 // spills into a second wave)
-constexpr int kPlanCtasPerSm = WL_PLAN_CTAS_PER_SM;
+constexpr int kPlanCtasPerSm = 3;
 constexpr int kSmemPerSm = 228 * 1024;  // B200 shared memory per SM (1 KB of it reserved per CTA)
 
 __device__ __forceinline__ void cp_async16(void* smem, const void* gmem, int src_bytes) {
@@ -190,24 +181,6 @@ __device__ __forceinline__ void split_tile(const float* src, __half* xs, int BP,
   }
 }
 
-// Compile-time phase timeline for kernel studies (off in normal builds): thread 0
-// of each CTA stores %globaltimer at entry, first stage, loop end, cluster
-// barrier and exit.
-#ifdef WL_EXP_TIMING
-__device__ unsigned long long g_tl[8192][5];
-__device__ __forceinline__ unsigned long long gtime() {
-  unsigned long long t;
-  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
-  return t;
-}
-#define TL(i)                                                              \
-  if (threadIdx.x == 0) {                                                  \
-    const int cid = blockIdx.x + gridDim.x * blockIdx.y;                   \
-    if (cid < 8192) g_tl[cid][i] = gtime();                                \
-  }
-#else
-#define TL(i)
-#endif
 // ------------------------------------------------------------------ epilogue
 // store_out (qgemv.cuh) applies F32 / ADD / QKV outputs per element.
 
@@ -298,7 +271,6 @@ __device__ void cluster_finish(const GemvArgs& a, const ClusterRed& R, float* ti
   const int g4 = ncv / 4;
   const int hd = e.head_dim, half = hd / 2;
   asm volatile("barrier.cluster.wait.acquire.aligned;\n" ::: "memory");  // every mbarrier is set up
-  TL(3);
   // send: group q = (b, c) of this CTA's tile to its owner
   const uint32_t recv0 = (uint32_t)__cvta_generic_to_shared(R.recv);
   for (int q = threadIdx.x; q < B * g4; q += blockDim.x) {
@@ -402,7 +374,6 @@ __global__ void __launch_bounds__(kThreadsB) k_qgemv_b(const GemvArgs a) {
   constexpr int XCH = 2 * BP * (kRows / 8);     // 16-byte chunks of x per stage
   extern __shared__ __align__(16) uint8_t smem[];
   uint8_t* raw = smem;
-  TL(0);
 
   // Tiled codes enter the MMA as f16 subnormals (q * 2^-24: one LOP3 per pair,
   // no HSUB2).  Q4_1 has no offset; Q4_0's -8 and Q8_0's -128 (codes stored
@@ -524,12 +495,6 @@ __global__ void __launch_bounds__(kThreadsB) k_qgemv_b(const GemvArgs a) {
   for (int st = 0; st < nstage; st++) {
     cp_wait<SB - 2>();
     __syncthreads();
-#ifdef WL_EXP_TIMING
-    if (st == 0 && threadIdx.x == 0) {
-      const int cid = blockIdx.x + gridDim.x * blockIdx.y;
-      if (cid < 8192) g_tl[cid][1] = gtime();
-    }
-#endif
     {
       const int nx = st + SB - 1;
       if (nx < nstage) load_stage(nx, nx % SB);
@@ -693,7 +658,6 @@ __global__ void __launch_bounds__(kThreadsB) k_qgemv_b(const GemvArgs a) {
   }
   cp_wait<0>();
   __syncthreads();
-  TL(2);
 
   // accumulators -> tile[b][c] (reuses the pipeline buffers); the k-step parts
   // add up in the tile
@@ -733,7 +697,6 @@ __global__ void __launch_bounds__(kThreadsB) k_qgemv_b(const GemvArgs a) {
     __syncthreads();
   }
   cluster_finish(a, R, tile, TP, ncv, seg, lg * kColsB);
-  TL(4);
 }
 
 // ------------------------------------------------------------------ layout A
@@ -963,13 +926,12 @@ size_t smem_a(int NT) {
 
 template <class Kern>
 int launch_cluster(Kern kern, dim3 grid, int threads, size_t smem, int cx, int cy,
-                   const GemvArgs& a, cudaStream_t st, unsigned& attr_done) {
+                   const GemvArgs& a, cudaStream_t st) {
   int dev = 0;
   cudaGetDevice(&dev);
-  if (!(attr_done >> (dev & 31) & 1u)) {
+  if (first_use_on_device((const void*)kern)) {
     WL_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
     WL_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
-    attr_done |= 1u << (dev & 31);
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
@@ -1069,21 +1031,19 @@ int repack_tiled_t(const uint8_t* src, int K, int N, int pitch, uint8_t* dst, cu
 
 template <int T, int NT, bool LOC = false, bool TLD = false>
 int launch_b_t(const GemvArgs& a, cudaStream_t st) {
-  static unsigned attr_done = 0;
   int groups = 0;
   for (int s = 0; s < a.nseg; s++) groups += a.seg[s].groups;
   const bool sw = a.epi.kind == EPI_SWIGLU;
   return launch_cluster(k_qgemv_b<T, NT, LOC, TLD>, dim3(groups, a.csplit), kThreadsB, smem_b<T>(NT),
                         sw ? 2 : 1,
-                        a.csplit, a, st, attr_done);
+                        a.csplit, a, st);
 }
 
 template <int T, int NT>
 int launch_a_t(const GemvArgs& a, cudaStream_t st) {
-  static unsigned attr_done = 0;
   return launch_cluster(k_qgemv_a<T, NT>, dim3(a.seg[0].groups, a.csplit), kThreads,
                         smem_a<T>(NT), 1,
-                        a.csplit, a, st, attr_done);
+                        a.csplit, a, st);
 }
 
 template <int T, bool TLD>
