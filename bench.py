@@ -10,9 +10,13 @@ far larger than L2, so no flush is needed between steps.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
 
-Prints one JSON line (rank 0).  Under torchrun each rank runs an independent
-replica on its own GPU (weak scaling; sessions shard across GPUs with no
-collective); timing is max over ranks of the CUDA-event time.
+Prints one JSON line (rank 0).  At N = 1 the line also carries a `tp`
+sub-record: the LLaMA-2-70B shape (all 80 layers,
+Q4_0) decoded on one GPU (TP-1), the base of the tensor-parallel curve.  Under
+torchrun (N > 1) the line's value is that 70B decode, tensor-parallel over
+the N ranks (ncclAllReduce after attn_output and ffn_down), at batch 32
+(strong scaling: the same batch on more GPUs), with batch 1 beside it;
+timing is the max over ranks of the CUDA-event time.
 """
 from __future__ import annotations
 
@@ -509,6 +513,10 @@ def run_gpu(args):
             line["sweep"] = sweep
         if not args.no_cpu_baseline and ws == 1:
             line["cpu_baseline"] = cpu_baseline(path)
+    if ws == 1 and not args.no_tp:
+        torch.cuda.empty_cache()
+        line["tp"] = tp_decode(args, 1, 0, local)
+    if rank == 0:
         print(json.dumps(line), flush=True)
     barrier(ws)
     if ws > 1:
@@ -517,79 +525,142 @@ def run_gpu(args):
 
 
 CFG_70B = dict(hidden=8192, heads=64, kv_heads=8, ff=28672, vocab=32000)
+TP_METRIC = "decode tok/s, 70B-shape Q4_0 tensor-parallel (bs1/bs32)"
 
 
-def run_tp(args):
-    """Tensor-parallel decode of the 70B shape (Q4_0, `--tp-layers` of its 80
-    layers) across all ranks of the launch: per-step device time (max over
-    ranks) at bs1 and bs16, once with ncclAllReduce (the default) and once
-    with the NVLink peer exchange (WL_TP_PEER=1); one JSON line from rank 0."""
+def weight_bytes_70b(layers):
+    d, ff, V = CFG_70B["hidden"], CFG_70B["ff"], CFG_70B["vocab"]
+    kv = d // 8
+    per_layer = (2 * d * d + 2 * d * kv + 3 * d * ff) // 32 * 18
+    return layers * per_layer + d * V // 32 * 18
+
+
+def path_70b(tmpdir, layers, rank, ws):
+    """Seeded 70B-shape Q4_0 GGUF (written once per box by rank 0, reused)."""
+    from woolly_b200.gguf import write_synthetic
+    path = os.path.join(tmpdir, f"llama70b_{layers}l_q4_0.gguf")
+    if rank == 0 and not os.path.exists(path):
+        tmp = path + ".part"
+        write_synthetic(tmp, **CFG_70B, layers=layers, weight_type=2, context_length=4096, seed=SEED)
+        os.replace(tmp, path)
+    barrier(ws)
+    return path
+
+
+def tp_decode(args, ws, rank, local):
+    """LLaMA-2-70B shape (d 8192, 80 layers, 64 heads, 8
+    KV heads, FFN 28672), Q4_0, tensor-parallel over the launch's ranks
+    (column shards for q/k/v and gate/up, row shards for attn_output and
+    ffn_down, ncclAllReduce after each row-parallel projection).  32 sessions
+    each prefilled with `tp_prompt` random tokens, then teacher-forced decode
+    at batch 32 and at batch 1, device time max over ranks.  Returns the
+    per-batch results (rank 0) or None."""
     import torch
     import torch.distributed as dist
-    ws, rank, local = dist_init()
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    from woolly_b200.gguf import write_synthetic
     from woolly_b200.model import CudaTransformer, Session, nccl_communicator, nccl_destroy
+    dev = torch.device("cuda", local)
     hbm_peak, peak_kind = peaks()
-    L = args.tp_layers
+    L, P, B = args.tp_layers, args.tp_prompt, 32
     os.makedirs(args.tmpdir, exist_ok=True)
-    path = os.path.join(args.tmpdir, f"llama70b_{L}l_q4_0.gguf")
-    if rank == 0 and not os.path.exists(path):
-        write_synthetic(path, **CFG_70B, layers=L, weight_type=2, context_length=4096, seed=SEED)
-    barrier(ws)
+    path = path_70b(args.tmpdir, L, rank, ws)
     comm = nccl_communicator(rank, ws) if ws > 1 else None
-    d, ff, kv = CFG_70B["hidden"], CFG_70B["ff"], CFG_70B["hidden"] // 8
-    layer_bytes = (2 * d * d + 2 * d * kv + 3 * d * ff) // 32 * 18
-    prompt, steps = 128, 48
-    res = {}
-    for mode in ("nccl", "peer"):
-        if ws == 1 and mode == "peer":
-            break
-        if mode == "peer":
-            os.environ["WL_TP_PEER"] = "1"
-        m = CudaTransformer(path, device=local, tp_rank=rank, tp_size=ws, nccl_comm=comm,
-                            max_sessions=BATCH, max_context=prompt + 2 * steps + 16, max_batch=BATCH,
-                            max_prefill=prompt)
-        rng = np.random.default_rng(SEED)
-        sess = [Session(m) for _ in range(BATCH)]
-        for s in sess:
-            s.infer_last(rng.integers(0, CFG_70B["vocab"], prompt).tolist())
-        logits = torch.empty(BATCH, CFG_70B["vocab"], device=dev)
-        stream = torch.cuda.current_stream(dev).cuda_stream
-        out = {}
-        for B in (1, BATCH):
-            ids = torch.from_numpy(rng.integers(0, CFG_70B["vocab"], (steps + 3, B)).astype(np.int32)).to(dev)
-            for t in range(3):
-                m.decode_step_device(sess[:B], ids[t].data_ptr(), logits.data_ptr(), stream)
-            torch.cuda.synchronize()
-            barrier(ws)
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record()
-            for t in range(3, steps + 3):
-                m.decode_step_device(sess[:B], ids[t].data_ptr(), logits.data_ptr(), stream)
-            e1.record()
-            torch.cuda.synchronize()
-            ms = max_over_ranks(e0.elapsed_time(e1), ws) / steps
-            gbs = L * layer_bytes / ws / (ms / 1e3) / 1e9  # projection weights each GPU reads
-            out[f"bs{B}"] = {"ms_per_step": round(ms, 4), "us_per_layer": round(ms * 1e3 / L, 2),
-                             "tok_s_80_layers_est": round(B * 1e3 / (ms * 80 / L), 1),
-                             "weight_GBps_per_gpu": round(gbs, 1),
-                             "frac_of_measured_hbm": round(gbs / hbm_peak, 3)}
-        for s in sess:
-            s.close()
-        m.close()
-        res[mode] = out
+    steps = args.tp_steps
+    m = CudaTransformer(path, device=local, tp_rank=rank, tp_size=ws, nccl_comm=comm,
+                        max_sessions=B, max_context=P + 2 * (steps + 3) + 8, max_batch=B, max_prefill=P)
+    rng = np.random.default_rng(SEED + 7)
+    sess = [Session(m) for _ in range(B)]
+    t0 = time.perf_counter()
+    for s in sess:
+        s.infer_last(rng.integers(0, CFG_70B["vocab"], P).tolist())
+    prefill_s = time.perf_counter() - t0
+    logits = torch.empty(B, CFG_70B["vocab"], device=dev)
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    out = {}
+    wb = weight_bytes_70b(L)
+    for nb in (B, 1):
+        ids = torch.from_numpy(rng.integers(0, CFG_70B["vocab"], (steps + 3, nb)).astype(np.int32)).to(dev)
+        for t in range(3):
+            m.decode_step_device(sess[:nb], ids[t].data_ptr(), logits.data_ptr(), stream)
+        torch.cuda.synchronize()
         barrier(ws)
-    os.environ.pop("WL_TP_PEER", None)
+        ctx = [len(s) for s in sess[:nb]]
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for t in range(3, steps + 3):
+            m.decode_step_device(sess[:nb], ids[t].data_ptr(), logits.data_ptr(), stream)
+        e1.record()
+        torch.cuda.synchronize()
+        ms = max_over_ranks(e0.elapsed_time(e1), ws) / steps
+        kvb = sum(L * 2 * (c + steps / 2) * (CFG_70B["hidden"] // 8) * 2 for c in ctx)
+        per_gpu = (wb + kvb) / ws  # each GPU reads its shard of the weights and KV
+        gbs = per_gpu / (ms / 1e3) / 1e9
+        out[f"bs{nb}"] = {"tok_s": nb * 1e3 / ms, "ms_per_step": ms,
+                          "per_gpu_GBps": gbs, "per_gpu_hbm_frac_of_" + peak_kind: gbs / hbm_peak}
+    # end to end at batch 32 through the public API (host ids in, host logits out)
+    e2e_steps = 8
+    host_ids = rng.integers(0, CFG_70B["vocab"], (e2e_steps + 1, B)).astype(np.uint32)
+    m.forward_sessions(sess, [[int(i)] for i in host_ids[0]])
+    barrier(ws)
+    t0 = time.perf_counter()
+    for t in range(1, e2e_steps + 1):
+        m.forward_sessions(sess, [[int(i)] for i in host_ids[t]])
+    e2e = B * e2e_steps / max_over_ranks(time.perf_counter() - t0, ws)
+    for s in sess:
+        s.close()
+    m.close()
+    # share of a step spent in the collectives, estimated by timing the same
+    # all-reduces (2 per layer, [B, d] f32) on the launch's NCCL group
+    ar = None
+    if ws > 1:
+        x = torch.ones(B, CFG_70B["hidden"], device=dev)
+        for _ in range(5):
+            dist.all_reduce(x)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(2 * L):
+            dist.all_reduce(x)
+        e1.record()
+        torch.cuda.synchronize()
+        ar_ms = max_over_ranks(e0.elapsed_time(e1), ws)
+        ar = {"allreduce_ms_per_step_bs32": ar_ms,
+              "share_of_bs32_step": ar_ms / out[f"bs{B}"]["ms_per_step"],
+              "how": "2 x layers ncclAllReduce of [32, 8192] f32 on the launch's group, CUDA events"}
     if comm is not None:
         nccl_destroy(comm)
+    if rank != 0:
+        return None
+    return {"tp": ws, "layers": L, "prompt": P, "prefill_s": prefill_s, "timed_steps": steps,
+            "results": out, "e2e_bs32_tok_s": e2e, "collectives": ar,
+            "workload": f"llama2-70b-shape Q4_0, {L} layers, TP{ws}, 32 sessions x {P}-token prefill, "
+                        f"teacher-forced decode bs32 and bs1"}
+
+
+def run_tp_headline(args):
+    """N > 1: the 70B tensor-parallel decode is the line's value (batch 32)."""
+    import torch
+    ws, rank, local = dist_init()
+    torch.cuda.set_device(local)
+    clk = Clocks(local)
+    clk.start()
+    r = tp_decode(args, ws, rank, local)
+    clocks = clk.stop()
     if rank == 0:
-        print(json.dumps({"metric": "tensor-parallel decode step, 70B-shape Q4_0", "n_gpus": ws,
-                          "config": {"workload": f"llama2-70b-shape Q4_0, {L} of 80 layers, TP{ws}, "
-                                                 f"prompt {prompt}, {steps} timed decode steps",
-                                     "parallelism": f"tp{ws}"},
-                          "results": res, "data": "synthetic", "peak_kind": peak_kind}), flush=True)
+        b32 = r["results"]["bs32"]
+        print(json.dumps({
+            "metric": TP_METRIC, "value": b32["tok_s"], "unit": "tok/s", "n_gpus": ws,
+            "steps": args.tp_steps, "warmup": 3, "ms_per_step": b32["ms_per_step"],
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "q4_0 weights, f16 MMA operands, f32 accumulate",
+            "data": "synthetic (seeded N(0,0.02) weights, uniform random token ids)",
+            "config": {"workload": r["workload"], "model": "llama2-70b-shape", "global_batch": 32,
+                       "seq_len": args.tp_prompt, "parallelism": f"tp{ws}",
+                       "l2": "inputs larger than L2 (weights + KV per step)"},
+            "e2e": {"value": r["e2e_bs32_tok_s"], "unit": "tok/s", "h2d_bytes_per_step": 32 * 12,
+                    "d2h_bytes_per_step": 32 * CFG_70B["vocab"] * 4},
+            "tp": r, "clocks": clocks}), flush=True)
+    barrier(ws)
+    import torch.distributed as dist
     if ws > 1:
         dist.destroy_process_group()
 
@@ -603,17 +674,18 @@ def main():
     ap.add_argument("--impl", default="woolly_b200", choices=["woolly_b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-sweep", action="store_true", help="skip the GEMV/GEMM shape sweep")
-    ap.add_argument("--tp", action="store_true",
-                    help="tensor-parallel 70B-shape decode across the launch's ranks (peer vs NCCL)")
-    ap.add_argument("--tp-layers", type=int, default=8)
+    ap.add_argument("--tp-layers", type=int, default=80)
+    ap.add_argument("--tp-prompt", type=int, default=1024)
+    ap.add_argument("--tp-steps", type=int, default=32)
+    ap.add_argument("--no-tp", action="store_true", help="N=1: skip the 70B TP-1 sub-record")
     ap.add_argument("--tmpdir", default=os.environ.get("WOOLLY_BENCH_DIR", "/tmp/woolly_bench"))
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":
         run_reference(args)
-    elif args.tp:
-        run_tp(args)
+    elif int(os.environ.get("WORLD_SIZE", "1")) > 1:
+        run_tp_headline(args)
     else:
         run_gpu(args)
 
