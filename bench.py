@@ -513,6 +513,9 @@ def run_gpu(args):
             line["sweep"] = sweep
         if not args.no_cpu_baseline and ws == 1:
             line["cpu_baseline"] = cpu_baseline(path)
+    if ws == 1 and not args.no_long:
+        torch.cuda.empty_cache()
+        line["long_context"] = long_context(args, local)
     if ws == 1 and not args.no_tp:
         torch.cuda.empty_cache()
         line["tp"] = tp_decode(args, 1, 0, local)
@@ -636,6 +639,60 @@ def tp_decode(args, ws, rank, local):
                         f"teacher-forced decode bs32 and bs1"}
 
 
+CFG_MISTRAL = dict(hidden=4096, heads=32, kv_heads=8, ff=14336, vocab=32000)
+
+
+def long_context(args, local):
+    """Mistral-7B shape (d 4096, 32 heads, 8 KV heads, FFN
+    14336, sliding window 4096), Q4_1, 8 sessions each prefilled to an
+    8192-token f16 KV cache, then teacher-forced batch-8 decode (the split-K
+    attention reads the last 4096 keys of every session)."""
+    import torch
+    from woolly_b200.gguf import write_synthetic
+    from woolly_b200.model import CudaTransformer, Session
+    dev = torch.device("cuda", local)
+    hbm_peak, peak_kind = peaks()
+    L, P, B, W, steps = args.long_layers, 8192, 8, 4096, args.long_steps
+    path = os.path.join(args.tmpdir, f"mistral_{L}l_q4_1.gguf")
+    if not os.path.exists(path):
+        write_synthetic(path + ".part", **CFG_MISTRAL, layers=L, weight_type=3, sliding_window=W,
+                        context_length=16384, seed=SEED)
+        os.replace(path + ".part", path)
+    m = CudaTransformer(path, device=local, max_sessions=B, max_context=P + steps + 8, max_batch=B,
+                        max_prefill=2048)
+    rng = np.random.default_rng(SEED + 3)
+    sess = [Session(m) for _ in range(B)]
+    t0 = time.perf_counter()
+    for s in sess:
+        s.infer_last(rng.integers(0, CFG_MISTRAL["vocab"], P).tolist())
+    prefill_s = time.perf_counter() - t0
+    ids = torch.from_numpy(rng.integers(0, CFG_MISTRAL["vocab"], (steps + 3, B)).astype(np.int32)).to(dev)
+    logits = torch.empty(B, CFG_MISTRAL["vocab"], device=dev)
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    for t in range(3):
+        m.decode_step_device(sess, ids[t].data_ptr(), logits.data_ptr(), stream)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for t in range(3, steps + 3):
+        m.decode_step_device(sess, ids[t].data_ptr(), logits.data_ptr(), stream)
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    for s in sess:
+        s.close()
+    m.close()
+    d, ff, kv = CFG_MISTRAL["hidden"], CFG_MISTRAL["ff"], 1024
+    wbytes = L * (2 * d * d + 2 * d * kv + 3 * d * ff) // 32 * 20 + d * CFG_MISTRAL["vocab"] // 32 * 20
+    kvbytes = B * L * 2 * W * kv * 2  # the window's keys and values, f16
+    gbs = (wbytes + kvbytes) / (ms / 1e3) / 1e9
+    return {"workload": f"mistral-7b-shape Q4_1, {L} layers, window {W}, {B} sessions x {P}-token "
+                        f"prefill, teacher-forced decode bs{B}",
+            "tok_s": B * 1e3 / ms, "ms_per_step": ms, "prefill_s": prefill_s, "timed_steps": steps,
+            "step_bytes": wbytes + kvbytes, "kv_bytes_per_step": kvbytes,
+            "step_hbm_frac_of_" + peak_kind: gbs / hbm_peak}
+
+
 def run_tp_headline(args):
     """N > 1: the 70B tensor-parallel decode is the line's value (batch 32)."""
     import torch
@@ -678,6 +735,9 @@ def main():
     ap.add_argument("--tp-prompt", type=int, default=1024)
     ap.add_argument("--tp-steps", type=int, default=32)
     ap.add_argument("--no-tp", action="store_true", help="N=1: skip the 70B TP-1 sub-record")
+    ap.add_argument("--long-layers", type=int, default=32)
+    ap.add_argument("--long-steps", type=int, default=32)
+    ap.add_argument("--no-long", action="store_true", help="N=1: skip the long-context sub-record")
     ap.add_argument("--tmpdir", default=os.environ.get("WOOLLY_BENCH_DIR", "/tmp/woolly_bench"))
     args = ap.parse_args()
     if args.warmup < 3:
