@@ -252,6 +252,24 @@ int wl_rmsnorm_rope(const float* x, const float* w, int rows, int dim, float eps
  * (tensor_utils.rs:512-532), exact SiLU(g) * u. */
 int wl_swiglu(const float* gate, const float* up, size_t n, float* out, void* stream);
 
+/* Next-token sampling of the server's decode loop, sample_next_token
+ * (woolly-server/src/handlers/inference.rs:441-483, helpers :551-654), on the
+ * GPU: per row r of logits (row stride ld, vocab entries), softmax with
+ * max(temperature, 0.01), optional top-k and top-p filtering (renormalised;
+ * top-p keeps nothing when no prefix exceeds p, as the reference), then
+ * greedy (temperature == 0: last index of the largest probability) or the
+ * first index whose running sum exceeds the row's uniform draw u (last index
+ * when none does).  params and out_ids are device arrays of `rows` entries;
+ * vocab <= 51200.  The draw is an input: the caller owns the random stream. */
+typedef struct wl_sample_params {
+  float temperature;
+  int top_k;    /* 0 = off */
+  float top_p;  /* >= 1 = off */
+  float u;      /* uniform draw in [0, 1) */
+} wl_sample_params;
+int wl_sample(const float* logits, int rows, int vocab, int ld, const wl_sample_params* params,
+              uint32_t* out_ids, void* stream);
+
 /* RoPE::apply_f32 (woolly-tensor/src/ops/mod.rs:476-527), NeoX half split:
  * x [batch, seq, heads, head_dim] f32, positions [seq] (device int32). */
 int wl_rope(const float* x, float* out, const int* positions, float base, int batch, int seq,

@@ -57,6 +57,12 @@ class ModelConfig(C.Structure):
                 ("layer_norm_epsilon", C.c_float), ("architecture", C.c_char * 64)]
 
 
+class SampleParams(C.Structure):
+    """wl_sample_params: one row's sampling knobs and uniform draw."""
+    _fields_ = [("temperature", C.c_float), ("top_k", C.c_int), ("top_p", C.c_float),
+                ("u", C.c_float)]
+
+
 class SynthConfig(C.Structure):
     _fields_ = [("hidden", C.c_uint32), ("layers", C.c_uint32), ("heads", C.c_uint32),
                 ("kv_heads", C.c_uint32), ("ff", C.c_uint32), ("vocab", C.c_uint32),
@@ -108,6 +114,7 @@ _SIGS = {
     "wl_tp_reduce_rmsnorm": (C.c_int, [P, P, C.c_int, C.c_int, C.c_float, P, C.c_int, P, C.c_uint,
                                        P, C.c_size_t, P, P]),
     "wl_swiglu": (C.c_int, [P, P, C.c_size_t, P, P]),
+    "wl_sample": (C.c_int, [P, C.c_int, C.c_int, C.c_int, P, P, P]),
     "wl_rope": (C.c_int, [P, P, P, C.c_float, C.c_int, C.c_int, C.c_int, C.c_int, P]),
     "wl_attention": (C.c_int, [P, P, P, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int,
                                P, P]),

@@ -421,6 +421,13 @@ int wl_swiglu(const float* gate, const float* up, size_t n, float* out, void* st
   return launch_swiglu(gate, up, n, out, (cudaStream_t)stream);
 }
 
+int wl_sample(const float* logits, int rows, int vocab, int ld, const wl_sample_params* params,
+              uint32_t* out_ids, void* stream) {
+  if (rows == 0) return WL_OK;
+  if (!logits || !params || !out_ids || rows < 0) return fail(WL_ERR_INVALID_ARGUMENT, "bad argument");
+  return launch_sample(logits, rows, vocab, ld, params, out_ids, (cudaStream_t)stream);
+}
+
 int wl_rope(const float* x, float* out, const int* positions, float base, int batch, int seq,
             int heads, int head_dim, void* stream) {
   if (!x || !out || !positions || head_dim % 2 || batch < 0 || seq < 0 || heads < 0)

@@ -60,6 +60,11 @@ int launch_rope(const float* x, float* out, const int* pos, float base, int batc
                 int heads, int hd, cudaStream_t st);
 int launch_dequant(int type, const void* blocks, size_t n, float* out, cudaStream_t st);
 
+// GPU next-token sampling (sample.cu); vocab <= kSampleMaxVocab
+constexpr int kSampleMaxVocab = 51200;
+int launch_sample(const float* logits, int rows, int V, int ld, const wl_sample_params* prm,
+                  uint32_t* out, cudaStream_t st);
+
 // *err &= ~bits (stream-ordered): clears the error bits the host has reported
 int launch_err_clear(int* err, int bits, cudaStream_t st);
 

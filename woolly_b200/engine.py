@@ -124,7 +124,8 @@ class BatchEngine:
     """
 
     def __init__(self, model, max_batch: int | None = None, session_factory=None,
-                 max_context: int | None = None, keep_logits: bool = False):
+                 max_context: int | None = None, keep_logits: bool = False,
+                 device_sampling: bool = False):
         self.model = model
         self.max_batch = max_batch or model.max_batch
         if session_factory is None:
@@ -133,6 +134,10 @@ class BatchEngine:
         self.new_session = session_factory
         self.max_context = max_context or getattr(model, "max_context", None)
         self.keep_logits = keep_logits
+        # decode steps sample on the GPU (CudaTransformer.decode_sample): only
+        # token ids cross to the host; the uniform draws still come from each
+        # request's own stream, in the same order as host sampling
+        self.device_sampling = device_sampling and not keep_logits and hasattr(model, "decode_sample")
         self.waiting: list[Request] = []
         self.running: list[Request] = []
         self.finished: dict[int, Request] = {}
@@ -151,9 +156,12 @@ class BatchEngine:
     # ---------------------------------------------------------------- internals
     def _emit(self, r: Request, row: np.ndarray) -> None:
         tok = sample_next_token(row, r.cfg, r.rng)
-        r.tokens.append(tok)
         if self.keep_logits:
             r.logits.append(np.array(row, np.float32, copy=True))
+        self._emit_token(r, tok)
+
+    def _emit_token(self, r: Request, tok: int) -> None:
+        r.tokens.append(int(tok))
         if len(r.tokens) >= r.cfg.max_tokens:
             r.done, r.reason = True, "length"
         elif r.cfg.eos_below and tok < r.cfg.eos_below:
@@ -201,7 +209,18 @@ class BatchEngine:
             row = self.model.forward_sessions([r.session], [r.prompt])[0]
             self._emit(r, np.asarray(row).reshape(-1)[-self.model.vocab_size():])
             produced += 1
-        if decoding:
+        if decoding and self.device_sampling:
+            cf = [r.cfg for r in decoding]
+            u = [np.float32(r.rng.random(dtype=np.float32)) if r.cfg.temperature != 0.0 else 0.0
+                 for r in decoding]
+            toks = self.model.decode_sample([r.session for r in decoding],
+                                            [r.tokens[-1] for r in decoding],
+                                            [c.temperature for c in cf], [c.top_k for c in cf],
+                                            [c.top_p for c in cf], u)
+            for r, tok in zip(decoding, toks):
+                self._emit_token(r, tok)
+                produced += 1
+        elif decoding:
             outs = self.model.forward_sessions([r.session for r in decoding],
                                                [[r.tokens[-1]] for r in decoding])
             for r, row in zip(decoding, outs):

@@ -174,6 +174,39 @@ class CudaTransformer:
         check(lib().wl_decode_step_device(self._h, arr, len(sessions), d_ids, d_logits, stream))
 
 
+    def decode_sample(self, sessions: Sequence["Session"], ids: Sequence[int], temperature=0.0,
+                      top_k=0, top_p=1.0, u=0.0) -> np.ndarray:
+        """One batched decode step that returns the next token of every
+        session, sampled on the GPU by the server's rules (wl_sample;
+        inference.rs:441-483): the step's ids go to the device, only the
+        sampled ids come back (4 bytes per session instead of a row of
+        logits).  temperature / top_k / top_p / u are scalars or per-session
+        sequences; u is the uniform draw of each session's sampling stream."""
+        import torch
+        from . import ops
+        n = len(sessions)
+        dev = torch.device("cuda", self.ctx.device)
+        buf = getattr(self, "_ds_buf", None)
+        if buf is None or buf[0].numel() < n:
+            cap = max(n, self.max_batch)
+            buf = (torch.empty(cap, dtype=torch.int32, pin_memory=True),
+                   torch.empty(cap, dtype=torch.int32, device=dev),
+                   torch.empty(cap, self.vocab_size(), dtype=torch.float32, device=dev),
+                   torch.empty(cap, dtype=torch.int32, device=dev),
+                   torch.empty(cap, dtype=torch.int32, pin_memory=True),
+                   torch.empty(cap * 16, dtype=torch.uint8, device=dev))
+            self._ds_buf = buf
+        h_ids, d_ids, d_logits, d_next, h_next, d_prm = buf
+        h_ids[:n] = torch.from_numpy(np.asarray(ids, dtype=np.int32))
+        stream = torch.cuda.current_stream(dev)
+        d_ids[:n].copy_(h_ids[:n], non_blocking=True)
+        self.decode_step_device(sessions, d_ids.data_ptr(), d_logits.data_ptr(), stream.cuda_stream)
+        ops.sample(d_logits[:n], temperature, top_k, top_p, u, out=d_next[:n], params=d_prm)
+        h_next[:n].copy_(d_next[:n], non_blocking=True)
+        stream.synchronize()
+        return h_next[:n].numpy().copy()
+
+
 class Session:
     """A device KV cache for one sequence (InferenceSession, session.rs:193-277)."""
 

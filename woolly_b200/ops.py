@@ -5,6 +5,7 @@ a kernel of libwoolly_cuda.so and raises if the library or the GPU is missing.
 """
 from __future__ import annotations
 
+import numpy as np
 import torch
 
 from ._lib import LAYOUT_A, LAYOUT_B, ROPE_NEOX, ROPE_OFF, check, lib
@@ -188,3 +189,30 @@ def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, past: int, h
 
 __all__ = ["dequantize", "quantized_matvec", "qgemv", "rmsnorm_rope", "TransformerSIMD", "RoPE",
            "attention", "LAYOUT_A", "LAYOUT_B"]
+
+
+def sample(logits: torch.Tensor, temperature, top_k, top_p, u, out: torch.Tensor | None = None,
+           params: torch.Tensor | None = None) -> torch.Tensor:
+    """sample_next_token (inference.rs:441-483) for every row of f32 logits
+    [rows, vocab] on the GPU; temperature / top_k / top_p / u are per-row
+    sequences (or scalars).  `params` (optional): a device buffer of at least
+    rows * 16 bytes to stage them in.  Returns int32 token ids [rows]."""
+    _dev(logits, torch.float32, "logits")
+    rows, V = logits.shape
+    rec = sample_params(rows, temperature, top_k, top_p, u)
+    src = torch.from_numpy(rec.view(np.uint8))
+    if params is None:
+        params = src.to(logits.device)
+    else:
+        params[: src.numel()].copy_(src)
+    y = out if out is not None else torch.empty(rows, dtype=torch.int32, device=logits.device)
+    check(lib().wl_sample(logits.data_ptr(), rows, V, logits.stride(0), params.data_ptr(),
+                          y.data_ptr(), _stream()))
+    return y
+
+
+def sample_params(rows, temperature, top_k, top_p, u) -> "np.ndarray":
+    """Per-row knobs as an array of wl_sample_params records."""
+    rec = np.zeros(rows, dtype=[("t", "<f4"), ("k", "<i4"), ("p", "<f4"), ("u", "<f4")])
+    rec["t"], rec["k"], rec["p"], rec["u"] = temperature, top_k, top_p, u
+    return rec
