@@ -299,6 +299,11 @@ typedef struct wl_model_options {
   int use_graphs;       /* capture decode steps in CUDA graphs */
   int tp_rank, tp_size; /* tensor parallel shard (tp_size 1 = whole model) */
   void* nccl_comm;      /* ncclComm_t when tp_size > 1 */
+  int collective_timeout_ms; /* tp_size > 1: longest wait for a step (and its
+                                collectives) to finish; on expiry the NCCL
+                                communicator is aborted, the call returns
+                                WL_ERR_TIMEOUT and later calls WL_ERR_NCCL:
+                                close and reload (0 = 60000) */
 } wl_model_options;
 
 void wl_model_options_default(wl_model_options* o);
@@ -339,6 +344,9 @@ int wl_decode_kernel_count(const wl_model* m, int n_sess);
 int wl_nccl_unique_id(void* out128);
 int wl_nccl_comm_init(int nranks, const void* id128, int rank, void** comm_out);
 int wl_nccl_comm_destroy(void* comm);
+/* ncclCommAbort: ends every collective in flight on the communicator (the
+ * recovery when a rank stopped participating, see collective_timeout_ms). */
+int wl_nccl_comm_abort(void* comm);
 
 #ifdef __cplusplus
 }

@@ -75,7 +75,7 @@ class ModelOptions(C.Structure):
     _fields_ = [("rope_mode", C.c_int), ("sliding_window", C.c_int), ("max_sessions", C.c_int),
                 ("max_context", C.c_int), ("max_batch", C.c_int), ("max_prefill", C.c_int),
                 ("use_graphs", C.c_int), ("tp_rank", C.c_int), ("tp_size", C.c_int),
-                ("nccl_comm", C.c_void_p)]
+                ("nccl_comm", C.c_void_p), ("collective_timeout_ms", C.c_int)]
 
 
 P = C.c_void_p
@@ -114,6 +114,7 @@ _SIGS = {
     "wl_tp_reduce_rmsnorm": (C.c_int, [P, P, C.c_int, C.c_int, C.c_float, P, C.c_int, P, C.c_uint,
                                        P, C.c_size_t, P, P]),
     "wl_swiglu": (C.c_int, [P, P, C.c_size_t, P, P]),
+    "wl_nccl_comm_abort": (C.c_int, [P]),
     "wl_sample": (C.c_int, [P, C.c_int, C.c_int, C.c_int, P, P, P]),
     "wl_rope": (C.c_int, [P, P, P, C.c_float, C.c_int, C.c_int, C.c_int, C.c_int, P]),
     "wl_attention": (C.c_int, [P, P, P, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int,

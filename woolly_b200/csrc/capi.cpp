@@ -44,6 +44,7 @@ int noalloc_setup_current_device();
 int nccl_unique_id(void*);
 int nccl_comm_init(int, const void*, int, void**);
 int nccl_comm_destroy(void*);
+int nccl_comm_abort(void*);
 
 namespace {
 
@@ -457,6 +458,7 @@ void wl_model_options_default(wl_model_options* o) {
   o->tp_rank = 0;
   o->tp_size = 1;
   o->nccl_comm = nullptr;
+  o->collective_timeout_ms = 60000;
 }
 
 int wl_init(int device, wl_ctx** out) {
@@ -541,5 +543,6 @@ int wl_nccl_comm_init(int nranks, const void* id, int rank, void** comm) {
   return nccl_comm_init(nranks, id, rank, comm);
 }
 int wl_nccl_comm_destroy(void* comm) { return nccl_comm_destroy(comm); }
+int wl_nccl_comm_abort(void* comm) { return nccl_comm_abort(comm); }
 
 }  // extern "C"

@@ -15,6 +15,8 @@
 #include <dlfcn.h>
 
 #include <algorithm>
+#include <chrono>
+#include <thread>
 #include <cstdlib>
 #include <cstring>
 #include <string>
@@ -265,6 +267,51 @@ int nccl_comm_destroy(void* comm) {
   Nccl& n = nccl();
   if (!n.ok || !comm) return WL_OK;
   n.CommDestroy(comm);
+  return WL_OK;
+}
+
+int nccl_comm_abort(void* comm) {
+  Nccl& n = nccl();
+  if (!n.ok || !comm || !n.CommAbort) return WL_OK;
+  n.CommAbort(comm);
+  return WL_OK;
+}
+
+// Waits for everything queued on the model's stream.  Under tensor
+// parallelism a rank that stopped participating leaves the others' NCCL
+// kernels waiting forever, so the wait is bounded by the collective timeout:
+// on expiry the communicator is aborted (its kernels return), the model is
+// marked unusable and WL_ERR_TIMEOUT is returned; close and reload it.
+static int wait_for(wl_model* m, cudaEvent_t ev) {
+  if (m->tp_size == 1) {
+    WL_CUDA_TRY(cudaEventSynchronize(ev));
+    return WL_OK;
+  }
+  const int ms = m->opt.collective_timeout_ms > 0 ? m->opt.collective_timeout_ms : 60000;
+  const auto t0 = std::chrono::steady_clock::now();
+  for (;;) {
+    const cudaError_t q = cudaEventQuery(ev);
+    if (q == cudaSuccess) return WL_OK;
+    if (q != cudaErrorNotReady) WL_CUDA_TRY(q);
+    if (std::chrono::steady_clock::now() - t0 > std::chrono::milliseconds(ms)) break;
+    std::this_thread::sleep_for(std::chrono::microseconds(20));
+  }
+  nccl_comm_abort(m->nccl);
+  m->aborted = true;
+  return fail(WL_ERR_TIMEOUT, "a tensor-parallel step did not finish within " + std::to_string(ms) +
+                                  " ms (a rank stopped participating?): the NCCL communicator was "
+                                  "aborted; close and reload the model");
+}
+
+static int sync_stream(wl_model* m) {
+  WL_CUDA_TRY(cudaEventRecord(m->sync_ev, m->st));
+  return wait_for(m, m->sync_ev);
+}
+
+static int check_alive(const wl_model* m) {
+  if (m->aborted)
+    return fail(WL_ERR_NCCL, "the tensor-parallel communicator was aborted after a timeout: close "
+                             "and reload the model");
   return WL_OK;
 }
 
@@ -857,6 +904,7 @@ int model_load(wl_ctx* ctx, const char* path, const wl_model_options* o, wl_mode
   WL_CUDA_TRY(cudaMallocHost(&m->h_err, sizeof(int)));
   *m->h_err = 0;
   WL_CUDA_TRY(cudaEventCreateWithFlags(&m->err_ev, cudaEventDisableTiming));
+  WL_CUDA_TRY(cudaEventCreateWithFlags(&m->sync_ev, cudaEventDisableTiming));
   WL_CUDA_TRY(cudaStreamSynchronize(m->st));
   WL_TRY(peer_setup(m.get()));
   *out = m.release();
@@ -892,6 +940,7 @@ void model_free(wl_model* m) {
     if (e) cudaEventDestroy(e);
   cudaFreeHost(m->h_err);
   if (m->err_ev) cudaEventDestroy(m->err_ev);
+  if (m->sync_ev) cudaEventDestroy(m->sync_ev);
   for (int r = 0; r < m->tp_size && r < kMaxPeers; r++)
     if (m->pbase[r] && m->pbase[r] != m->pmem) cudaIpcCloseMemHandle(m->pbase[r]);
   cudaFree(m->pmem);
@@ -941,6 +990,7 @@ int forward(wl_model* m, wl_session* const* ss, int n, const uint32_t* ids, cons
   WL_CHECK_ARG(m && ids && n_ids && logits, "null argument");
   WL_TRY(check_sessions(m, ss, n));
   WL_CHECK_ARG(mode == WL_LOGITS_LAST || mode == WL_LOGITS_ALL, "bad logits mode");
+  WL_TRY(check_alive(m));
   std::lock_guard<std::mutex> lk(m->mu);
   WL_CUDA_TRY(cudaSetDevice(m->dev));
   size_t total = 0;
@@ -966,7 +1016,7 @@ int forward(wl_model* m, wl_session* const* ss, int n, const uint32_t* ids, cons
     WL_TRY(decode_launch(m, n));
     WL_CUDA_TRY(cudaMemcpyAsync(logits, m->logits, (size_t)n * V * 4, cudaMemcpyDeviceToHost, m->st));
     WL_CUDA_TRY(cudaMemcpyAsync(m->h_err, m->err, sizeof(int), cudaMemcpyDeviceToHost, m->st));
-    WL_CUDA_TRY(cudaStreamSynchronize(m->st));
+    WL_TRY(sync_stream(m));
     for (int i = 0; i < n; i++) ss[i]->len += 1;
     return take_err(m);
   }
@@ -994,7 +1044,7 @@ int forward(wl_model* m, wl_session* const* ss, int n, const uint32_t* ids, cons
         lg_off += (size_t)(c - lfirst) * V;
       }
       WL_CUDA_TRY(cudaMemcpyAsync(m->h_err, m->err, sizeof(int), cudaMemcpyDeviceToHost, m->st));
-      WL_CUDA_TRY(cudaStreamSynchronize(m->st));
+      WL_TRY(sync_stream(m));
       s->len += c;
       WL_TRY(take_err(m));
     }
@@ -1008,6 +1058,7 @@ int decode_step_device(wl_model* m, wl_session* const* ss, int n, const uint32_t
   WL_CHECK_ARG(m && d_ids && d_logits, "null argument");
   WL_TRY(check_sessions(m, ss, n));
   WL_CHECK_ARG(n <= m->opt.max_batch, "n_sess exceeds max_batch");
+  WL_TRY(check_alive(m));
   std::lock_guard<std::mutex> lk(m->mu);
   WL_CUDA_TRY(cudaSetDevice(m->dev));
   // asynchronous API: device errors of earlier calls surface here, once the
@@ -1037,7 +1088,7 @@ int decode_step_device(wl_model* m, wl_session* const* ss, int n, const uint32_t
   // per-step positions go through a ring slot the previous user of which has
   // been copied: this call returns before its copies run
   const int k = (int)(m->ring_next++ % wl_model::kMetaRing);
-  if (m->ring_used[k]) WL_CUDA_TRY(cudaEventSynchronize(m->ring_ev[k]));
+  if (m->ring_used[k]) WL_TRY(wait_for(m, m->ring_ev[k]));
   int* meta = m->h_ring + (size_t)k * 2 * m->MR;
   for (int i = 0; i < n; i++) {
     meta[i] = ss[i]->len;

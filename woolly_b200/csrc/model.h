@@ -108,6 +108,8 @@ struct wl_model {
   int* h_err = nullptr;  // pinned mirror of err, copied after every call
   cudaEvent_t err_ev = nullptr;  // recorded after the asynchronous step's copy into h_err
   bool err_pending = false;      // err_ev recorded and not yet consumed
+  cudaEvent_t sync_ev = nullptr;  // end of a synchronous call's work (bounded wait under TP)
+  bool aborted = false;           // the NCCL communicator was aborted after a timeout
   std::mutex mu;
 };
 
