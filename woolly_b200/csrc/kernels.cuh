@@ -65,6 +65,10 @@ constexpr int kSampleMaxVocab = 51200;
 int launch_sample(const float* logits, int rows, int V, int ld, const wl_sample_params* prm,
                   uint32_t* out, cudaStream_t st);
 
+// dst[r][t * cols + c] = src[t][r][c]: the rank-major blocks of an all-gather
+// of column shards back into whole rows
+int launch_gather_cols(const float* src, int T, int rows, int cols, float* dst, cudaStream_t st);
+
 // *err &= ~bits (stream-ordered): clears the error bits the host has reported
 int launch_err_clear(int* err, int bits, cudaStream_t st);
 

@@ -628,9 +628,18 @@ static int run_rows_body(wl_model* m, int R, int nsplit, int lfirst) {
                             0, 0.f, m->xn, 2, xpl, st));
     Epilogue e;
     e.kind = EPI_F32;
-    e.y[0] = m->logits;
-    e.ldy[0] = m->V;
+    const bool vshard = m->Vl != m->V;
+    e.y[0] = vshard ? m->logits_part : m->logits;
+    e.ldy[0] = m->Vl;
     WL_TRY(gemv(m, 1, &m->out, nl, m->xn, xpl, m->d, e));
+    if (vshard) {
+      Nccl& n = nccl();
+      const size_t cnt = (size_t)nl * m->Vl;
+      // ncclFloat32 = 7; rank r's [nl][Vl] block lands at gather + r * cnt
+      const int r = n.AllGather(m->logits_part, m->logits_gather, cnt, 7, m->nccl, st);
+      if (r) return fail(WL_ERR_NCCL, std::string("ncclAllGather: ") + n.GetErrorString(r));
+      WL_TRY(launch_gather_cols(m->logits_gather, m->tp_size, nl, m->Vl, m->logits, st));
+    }
   }
   return WL_OK;
 }
@@ -791,7 +800,13 @@ int model_load(wl_ctx* ctx, const char* path, const wl_model_options* o, wl_mode
   bool ok = ld.add_f32("token_embd.weight", (uint64_t)d * V, &off_embd) &&
             ld.add_f32("output_norm.weight", (uint64_t)d, &off_onorm);
   bool tied = ok && !g->find("output.weight");
-  if (ok && !tied) ok = ld.add_mat("output.weight", d, V, 0, d, 0, V, &m->out, &off_out);
+  // LM head under tensor parallelism: each rank keeps V / T vocabulary
+  // columns and the logit rows are gathered (ncclAllGather) after the head
+  // GEMV; replicated when V does not split into whole 32-column blocks or
+  // the head is the tied f32 embedding
+  m->Vl = V;
+  if (m->tp_size > 1 && !tied && V % (32 * m->tp_size) == 0 && nccl().AllGather) m->Vl = V / m->tp_size;
+  if (ok && !tied) ok = ld.add_mat("output.weight", d, V, 0, d, m->tp_rank * m->Vl, m->Vl, &m->out, &off_out);
   struct LOff {
     size_t an, fn, q, k, v, o, g, u, dn;
   };
@@ -890,6 +905,10 @@ int model_load(wl_ctx* ctx, const char* path, const wl_model_options* o, wl_mode
   WL_TRY(dalloc(&m->att, (size_t)2 * MR * m->Hl * m->hd));
   WL_TRY(dalloc(&m->act, (size_t)2 * MR * m->ffl));
   WL_TRY(dalloc(&m->logits, (size_t)MR * V));
+  if (m->Vl != V) {
+    WL_TRY(dalloc(&m->logits_part, (size_t)MR * m->Vl));
+    WL_TRY(dalloc(&m->logits_gather, (size_t)MR * V));
+  }
   m->part_rows = (size_t)kAttnSplitCtasPerSm * m->sms + MR;
   WL_TRY(dalloc(&m->part_o, m->part_rows * m->Hl * m->hd));
   WL_TRY(dalloc(&m->part_ml, m->part_rows * m->Hl * 2));
@@ -928,6 +947,8 @@ void model_free(wl_model* m) {
   cudaFree(m->att);
   cudaFree(m->act);
   cudaFree(m->logits);
+  cudaFree(m->logits_part);
+  cudaFree(m->logits_gather);
   cudaFree(m->part_o);
   cudaFree(m->part_ml);
   cudaFree(m->row_pos);
@@ -1116,7 +1137,7 @@ int decode_kernel_count(const wl_model* m, int n) {
   const int nsplit = attention_plan_splits(n, m->KVHl, m->opt.max_context, m->sms);
   int chunks = (n + 31) / 32;
   int per_layer = 2 + chunks * 4 + 1 + (nsplit > 1 ? 1 : 0);
-  return 1 + m->L * per_layer + 1 + chunks;
+  return 1 + m->L * per_layer + 1 + chunks + (m->Vl != m->V ? 1 : 0);
 }
 
 }  // namespace wl

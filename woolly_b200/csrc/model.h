@@ -76,6 +76,9 @@ struct wl_model {
   __half* att = nullptr;    // attention output planes [2][MR][Hl*hd]
   __half* act = nullptr;    // SwiGLU output planes [2][MR][ffl]
   float* logits = nullptr;  // [MR][V]
+  int Vl = 0;                       // vocabulary columns of this rank's LM head (V unless sharded)
+  float* logits_part = nullptr;     // [MR][Vl] this rank's logit columns (sharded head)
+  float* logits_gather = nullptr;   // [T][MR][Vl] all ranks' columns after the all-gather
   float* part_o = nullptr;  // attention split partials
   float* part_ml = nullptr;
   size_t part_rows = 0;     // capacity in rows*nsplit

@@ -341,6 +341,25 @@ int launch_rope(const float* x, float* out, const int* pos, float base, int batc
   return WL_OK;
 }
 
+__global__ void k_gather_cols(const float* src, int T, int rows, int cols, float* dst) {
+  pdl_wait();
+  pdl_trigger();
+  const size_t n = (size_t)T * rows * cols;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+    const int c = (int)(i % cols);
+    const size_t tr = i / cols;
+    const int r = (int)(tr % rows), t = (int)(tr / rows);
+    dst[((size_t)r * T + t) * cols + c] = src[i];
+  }
+}
+
+int launch_gather_cols(const float* src, int T, int rows, int cols, float* dst, cudaStream_t st) {
+  const size_t n = (size_t)T * rows * cols;
+  if (!n) return WL_OK;
+  return launch_k(k_gather_cols, dim3((unsigned)std::min<size_t>((n + 255) / 256, 4096)), dim3(256), 0,
+                  st, src, T, rows, cols, dst);
+}
+
 __global__ void k_err_clear(int* err, int bits) { atomicAnd(err, ~bits); }
 
 int launch_err_clear(int* err, int bits, cudaStream_t st) {
