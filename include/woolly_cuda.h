@@ -299,6 +299,10 @@ typedef struct wl_model_options {
   int use_graphs;       /* capture decode steps in CUDA graphs */
   int tp_rank, tp_size; /* tensor parallel shard (tp_size 1 = whole model) */
   void* nccl_comm;      /* ncclComm_t when tp_size > 1 */
+  int ggml_layout;      /* 0: the reference's reading of every 2-D weight [ne0, ne1]
+                           as [ne0][ne1] (layout B, its parity semantics); 1: ggml's
+                           orientation, ne1 rows of ne0 values and token_embd one
+                           row per token (llama.cpp checkpoints; single GPU) */
   int collective_timeout_ms; /* tp_size > 1: longest wait for a step (and its
                                 collectives) to finish; on expiry the NCCL
                                 communicator is aborted, the call returns

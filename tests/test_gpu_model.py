@@ -215,3 +215,30 @@ def test_tinyllama_config_teacher_forced(tmp_path):
     e1, t1 = compare(gp[0], op[0], "tinyllama prefill")
     e2, t2 = compare(gs, os_, "tinyllama decode")
     print(f"tinyllama parity: prefill max-abs {e1:.2e} top1 {t1:.3f}; decode max-abs {e2:.2e} top1 {t2:.3f}")
+
+
+@pytest.mark.parametrize("name", ["gqa_q4_0", "mha_q4_1", "gqa_q8_0", "tied_q4_0"])
+@pytest.mark.parametrize("rope", [0, 1])
+def test_ggml_layout_parity(tiny_models, name, rope):
+    """The forward on weights in ggml orientation (llama.cpp checkpoints:
+    every 2-D weight as ne1 rows of ne0, token_embd one row per token,
+    quantized_matvec's layout, quantization.rs:1100-1163), with and without
+    NeoX RoPE, against the oracle reading the same file the same way."""
+    prompts = [[1, 2, 3, 4, 5, 6, 7], [100, 200], list(range(40, 73))]
+    run_parity(tiny_models[name], prompts, steps=8, oracle_kw=dict(layout_a=1, rope=rope),
+               max_sessions=4, max_context=128, ggml_layout=1,
+               rope_mode=_lib.ROPE_NEOX if rope else _lib.ROPE_OFF)
+
+
+def test_ggml_layout_tinyllama_rope(tmp_path):
+    """TinyLlama shape in ggml orientation with RoPE on (how a llama.cpp
+    checkpoint of it runs), 64 prompt tokens + 32 teacher-forced steps."""
+    p = write_synthetic(str(tmp_path / "tinyllama.gguf"), hidden=2048, layers=22, heads=32,
+                        kv_heads=4, ff=5632, vocab=32000, weight_type=Q4_0, seed=3)
+    prompt = np.random.default_rng(3).integers(0, 32000, 64).tolist()
+    gp, gs, op, os_ = teacher_forced(p, [prompt], 32, seed=4, oracle_kw=dict(layout_a=1, rope=1),
+                                     max_sessions=1, max_context=128, max_batch=1, ggml_layout=1,
+                                     rope_mode=_lib.ROPE_NEOX)
+    e1, _ = compare(gp[0], op[0], "ggml tinyllama prefill")
+    e2, _ = compare(gs, os_, "ggml tinyllama decode")
+    print(f"ggml-orientation tinyllama (rope on): prefill max-abs {e1:.2e}, decode {e2:.2e}")

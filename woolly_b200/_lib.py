@@ -75,7 +75,8 @@ class ModelOptions(C.Structure):
     _fields_ = [("rope_mode", C.c_int), ("sliding_window", C.c_int), ("max_sessions", C.c_int),
                 ("max_context", C.c_int), ("max_batch", C.c_int), ("max_prefill", C.c_int),
                 ("use_graphs", C.c_int), ("tp_rank", C.c_int), ("tp_size", C.c_int),
-                ("nccl_comm", C.c_void_p), ("collective_timeout_ms", C.c_int)]
+                ("nccl_comm", C.c_void_p), ("ggml_layout", C.c_int),
+                ("collective_timeout_ms", C.c_int)]
 
 
 P = C.c_void_p

@@ -52,8 +52,14 @@ int launch_rmsnorm_peer(float* x, const float* w, int rows, int dim, float eps, 
                         size_t y_plane, const PeerReduce& pr, cudaStream_t st);
 
 // h[r][j] = E[j*V + ids[r]] (token_embd stored [d][V], lazy_transformer.rs:1252-1262)
+// token_rows: E holds one row of d values per token, h[r][j] = E[ids[r]*d + j]
+// (ggml orientation, llama.cpp files)
 int launch_embed(const float* E, int d, int V, const uint32_t* ids, int rows, float* h,
-                 int* err_flag, cudaStream_t st);
+                 int* err_flag, cudaStream_t st, int token_rows = 0);
+
+int launch_qkv_post(float* q, const float* k, const float* v, int rows, int H, int KVH, int hd,
+                    int rope, float theta, const int* row_pos, const int* row_sess, const KvPages& kv,
+                    cudaStream_t st);
 
 int launch_swiglu(const float* g, const float* u, size_t n, float* out, cudaStream_t st);
 int launch_rope(const float* x, float* out, const int* pos, float base, int batch, int seq,

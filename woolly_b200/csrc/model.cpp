@@ -187,8 +187,46 @@ struct Loader {
   }
   // layout-B matrix [K][N] (dims [K, N]); keeps rows [r0, r0+Kl) and
   // columns [c0, c0+Nl) (c0, Nl multiples of 32).
+  // ggml orientation (m->ggml): the same dims [K, N] hold N rows of K values
+  // (blocks run along K), copied whole (no tensor-parallel slicing).
   bool add_mat(const std::string& name, int K, int N, int r0, int Kl, int c0, int Nl, QMat* out,
                size_t* off) {
+    if (m->ggml) return add_rows(name, K, N, out, off);
+    return add_mat_b(name, K, N, r0, Kl, c0, Nl, out, off);
+  }
+  bool add_rows(const std::string& name, int K, int N, QMat* out, size_t* off) {
+    const GgufTensor* t = need(name);
+    if (!t) return false;
+    if (t->n_dims != 2 || t->dims[0] != (uint64_t)K || t->dims[1] != (uint64_t)N) {
+      err = name + ": expected dims [" + std::to_string(K) + ", " + std::to_string(N) + "]";
+      return false;
+    }
+    const uint8_t* src = g->data(*t);
+    if (!src) {
+      err = name + ": data out of bounds";
+      return false;
+    }
+    const int S = t->type == WL_F32 ? 0 : block_bytes(t->type);
+    if (t->type != WL_F32 && (!S || K % 32)) {
+      err = name + ": layout-A weights must be F32, Q4_0, Q4_1 or Q8_0 with K % 32 == 0";
+      return false;
+    }
+    Piece p;
+    p.src = src;
+    p.rows = (size_t)N;
+    p.src_pitch = p.row_bytes = t->type == WL_F32 ? (size_t)K * 4 : (size_t)K / 32 * S;
+    p.dst_pitch = p.row_bytes;
+    p.dst_bytes = p.dst_pitch * p.rows;
+    p.dst_off = *off = reserve(p.dst_bytes);
+    pieces.push_back(p);
+    out->type = t->type;
+    out->K = K;
+    out->N = N;
+    out->pitch = (int)p.dst_pitch;
+    return true;
+  }
+  bool add_mat_b(const std::string& name, int K, int N, int r0, int Kl, int c0, int Nl, QMat* out,
+                 size_t* off) {
     const GgufTensor* t = need(name);
     if (!t) return false;
     if (t->n_dims != 2 || t->dims[0] != (uint64_t)K || t->dims[1] != (uint64_t)N) {
@@ -521,7 +559,101 @@ static int run_rows(wl_model* m, int R, int nsplit, int lfirst) {
   return s;
 }
 
+// y[r][n] (+)= sum_k x[r][k] W[n][k] for a layout-A (ggml orientation) matrix,
+// rows in launches of 32; f32 activations.
+static int gemv_a(wl_model* m, const QMat& W, int R, const float* x, int ldx, float* y, int ldy,
+                  bool add) {
+  const bool fast = W.type != WL_F32 && qgemv_a_fast_ok(W.type, W.K, W.N, W.pitch, W.w);
+  if (!fast)
+    return launch_qgemv_generic(W.type, WL_LAYOUT_A, W.w, W.K, W.N, W.pitch, x, 0, ldx, R, y, ldy, add,
+                                m->st);
+  const int gcols = qgemv_group_cols(WL_LAYOUT_A);
+  for (int r0 = 0; r0 < R; r0 += 32) {
+    GemvArgs a;
+    a.type = (int)W.type;
+    a.nseg = 1;
+    a.seg[0].W = W.w;
+    a.seg[0].N = W.N;
+    a.seg[0].pitch = W.pitch;
+    a.seg[0].groups = (W.N + gcols - 1) / gcols;
+    a.K = W.K;
+    a.B = std::min(32, R - r0);
+    a.xkind = X_F32;
+    a.x = x + (size_t)r0 * ldx;
+    a.ldx = ldx;
+    a.epi.kind = add ? EPI_ADD : EPI_F32;
+    a.epi.y[0] = y + (size_t)r0 * ldy;
+    a.epi.ldy[0] = ldy;
+    a.err = m->err;
+    qgemv_plan(a, WL_LAYOUT_A, m->sms);
+    WL_TRY(launch_qgemv_a(a, m->st));
+  }
+  return WL_OK;
+}
+
+// The forward on weights in ggml orientation (llama.cpp checkpoints): the
+// same layer as the reference's (lazy_transformer.rs:98-258) with its
+// projections read as rows of K (quantized_matvec's layout,
+// quantization.rs:1100-1163), the embedding as one row per token, and
+// optional NeoX RoPE (embedding.rs:183-242) applied to q and k.
+static int run_rows_a(wl_model* m, int R, int nsplit, int lfirst) {
+  cudaStream_t st = m->st;
+  const int d = m->d, qd = m->Hl * m->hd, kvd = m->kvdl, ff = m->ffl;
+  WL_TRY(launch_embed(m->embd, d, m->V, m->ids, R, m->h, m->err, st, /*token_rows=*/1));
+  for (int l = 0; l < m->L; l++) {
+    const Layer& y = m->layers[l];
+    WL_TRY(launch_rmsnorm(m->h, y.attn_norm, R, d, m->eps, 0, nullptr, 0, 0.f, m->xf, 0, 0, st));
+    WL_TRY(gemv_a(m, y.wq, R, m->xf, d, m->q, qd, false));
+    WL_TRY(gemv_a(m, y.wk, R, m->xf, d, m->kf, kvd, false));
+    WL_TRY(gemv_a(m, y.wv, R, m->xf, d, m->vf, kvd, false));
+    KvPages kv;
+    const size_t layer_halves = (size_t)m->n_pages * m->page * m->kvdl;
+    kv.k = reinterpret_cast<__half*>(m->kvbuf) + (size_t)l * 2 * layer_halves;
+    kv.v = kv.k + layer_halves;
+    kv.page_table = m->d_tables;
+    kv.max_pages = m->max_pages;
+    kv.page = m->page;
+    kv.kv_heads = m->KVHl;
+    kv.head_dim = m->hd;
+    WL_TRY(launch_qkv_post(m->q, m->kf, m->vf, R, m->Hl, m->KVHl, m->hd, m->rope, m->theta,
+                           m->row_pos, m->row_sess, kv, st));
+    AttnArgs a;
+    a.q = m->q;
+    a.ldq = qd;
+    a.kv = kv;
+    a.row_pos = m->row_pos;
+    a.row_sess = m->row_sess;
+    a.rows = R;
+    a.heads = m->Hl;
+    a.kv_heads = m->KVHl;
+    a.head_dim = m->hd;
+    a.window = m->window;
+    a.nsplit = nsplit;
+    a.part_o = m->part_o;
+    a.part_ml = m->part_ml;
+    a.out = m->attf;
+    a.ldo = qd;
+    a.out_plane = 0;
+    a.err = m->err;
+    WL_TRY(launch_attention_paged(a, st));
+    WL_TRY(gemv_a(m, y.wo, R, m->attf, qd, m->h, d, true));
+    WL_TRY(launch_rmsnorm(m->h, y.ffn_norm, R, d, m->eps, 0, nullptr, 0, 0.f, m->xf, 0, 0, st));
+    WL_TRY(gemv_a(m, y.wg, R, m->xf, d, m->gf, ff, false));
+    WL_TRY(gemv_a(m, y.wu, R, m->xf, d, m->uf, ff, false));
+    WL_TRY(launch_swiglu(m->gf, m->uf, (size_t)R * ff, m->gf, st));
+    WL_TRY(gemv_a(m, y.wd, R, m->gf, ff, m->h, d, true));
+  }
+  const int nl = R - lfirst;
+  if (nl > 0) {
+    WL_TRY(launch_rmsnorm(m->h + (size_t)lfirst * d, m->out_norm, nl, d, m->eps, 0, nullptr, 0, 0.f,
+                          m->xf, 0, 0, st));
+    WL_TRY(gemv_a(m, m->out, nl, m->xf, d, m->logits, m->V, false));
+  }
+  return WL_OK;
+}
+
 static int run_rows_body(wl_model* m, int R, int nsplit, int lfirst) {
+  if (m->ggml) return run_rows_a(m, R, nsplit, lfirst);
   cudaStream_t st = m->st;
   const bool tp = m->tp_size > 1;
   const int qd = m->Hl * m->hd;
@@ -735,6 +867,9 @@ int model_load(wl_ctx* ctx, const char* path, const wl_model_options* o, wl_mode
   m->opt = opt;
   m->tp_rank = opt.tp_rank;
   m->tp_size = opt.tp_size;
+  m->ggml = opt.ggml_layout != 0;
+  if (m->ggml && m->tp_size > 1)
+    return fail(WL_ERR_UNSUPPORTED, "the ggml weight orientation is single-GPU only");
   m->nccl = opt.nccl_comm;
   if (m->tp_size > 1 && (!m->nccl || !nccl().ok))
     return fail(WL_ERR_NCCL, "tensor parallel load needs an NCCL communicator");
@@ -841,7 +976,7 @@ int model_load(wl_ctx* ctx, const char* path, const wl_model_options* o, wl_mode
     m->out.type = WL_F32;
     m->out.K = d;
     m->out.N = V;
-    m->out.pitch = V * 4;
+    m->out.pitch = m->ggml ? d * 4 : V * 4;  // ggml: one row of d per token
   } else {
     m->out.w = B + off_out;
   }
@@ -861,7 +996,7 @@ int model_load(wl_ctx* ctx, const char* path, const wl_model_options* o, wl_mode
   // ---- tiled decode copies (the GEMV's lane-ready layout) of every quantized projection ----
   {
     std::vector<QMat*> mats;
-    {
+    if (!m->ggml) {
       for (Layer& y : m->layers)
         for (QMat* q : {&y.wq, &y.wk, &y.wv, &y.wo, &y.wg, &y.wu, &y.wd}) mats.push_back(q);
       mats.push_back(&m->out);
@@ -902,6 +1037,14 @@ int model_load(wl_ctx* ctx, const char* path, const wl_model_options* o, wl_mode
   WL_TRY(dalloc(&m->h, (size_t)MR * d));
   WL_TRY(dalloc(&m->xn, (size_t)2 * MR * d));
   WL_TRY(dalloc(&m->q, (size_t)MR * m->Hl * m->hd));
+  if (m->ggml) {
+    WL_TRY(dalloc(&m->xf, (size_t)MR * d));
+    WL_TRY(dalloc(&m->kf, (size_t)MR * m->kvdl));
+    WL_TRY(dalloc(&m->vf, (size_t)MR * m->kvdl));
+    WL_TRY(dalloc(&m->attf, (size_t)MR * m->Hl * m->hd));
+    WL_TRY(dalloc(&m->gf, (size_t)MR * m->ffl));
+    WL_TRY(dalloc(&m->uf, (size_t)MR * m->ffl));
+  }
   WL_TRY(dalloc(&m->att, (size_t)2 * MR * m->Hl * m->hd));
   WL_TRY(dalloc(&m->act, (size_t)2 * MR * m->ffl));
   WL_TRY(dalloc(&m->logits, (size_t)MR * V));
@@ -947,6 +1090,7 @@ void model_free(wl_model* m) {
   cudaFree(m->att);
   cudaFree(m->act);
   cudaFree(m->logits);
+  for (float* f : {m->xf, m->kf, m->vf, m->attf, m->gf, m->uf}) cudaFree(f);
   cudaFree(m->logits_part);
   cudaFree(m->logits_gather);
   cudaFree(m->part_o);

@@ -76,6 +76,9 @@ struct wl_model {
   __half* att = nullptr;    // attention output planes [2][MR][Hl*hd]
   __half* act = nullptr;    // SwiGLU output planes [2][MR][ffl]
   float* logits = nullptr;  // [MR][V]
+  // ggml orientation (llama.cpp files): f32 rows between the layout-A GEMVs
+  bool ggml = false;
+  float *xf = nullptr, *kf = nullptr, *vf = nullptr, *attf = nullptr, *gf = nullptr, *uf = nullptr;
   int Vl = 0;                       // vocabulary columns of this rank's LM head (V unless sharded)
   float* logits_part = nullptr;     // [MR][Vl] this rank's logit columns (sharded head)
   float* logits_gather = nullptr;   // [T][MR][Vl] all ranks' columns after the all-gather

@@ -153,7 +153,7 @@ __global__ void __launch_bounds__(1024) k_rmsnorm_v(const float* x, const float*
 // h[r][j] = E[j*V + id]: token_embd is [d][V] in woolly's reading
 // (lazy_transformer.rs:1252-1262).  Out-of-range ids raise a flag and read id 0.
 __global__ void k_embed(const float* E, int d, int V, const uint32_t* ids, int rows, float* h,
-                        int* err) {
+                        int* err, int token_rows) {
   pdl_wait();
   pdl_trigger();
   const int r = blockIdx.y;
@@ -164,8 +164,58 @@ __global__ void k_embed(const float* E, int d, int V, const uint32_t* ids, int r
     if (err && j == 0) atomicOr(err, 1);
     t = 0;
   }
-  h[(size_t)r * d + j] = __ldg(E + (size_t)j * V + t);
+  h[(size_t)r * d + j] = __ldg(E + (token_rows ? (size_t)t * d + j : (size_t)j * V + t));
 }
+
+// Layout-A (ggml orientation) attention input: the q/k/v projections as f32
+// rows; NeoX RoPE (RoPE::apply_f32, woolly-tensor/src/ops/mod.rs:476-527) on
+// the q and k heads at each row's position when `rope`, q written back as
+// f32, k and v appended to the row's KV page as f16.
+__global__ void k_qkv_post(float* q, const float* k, const float* v, int rows, int H, int KVH, int hd,
+                           int rope, float theta, const int* row_pos, const int* row_sess,
+                           KvPages kv) {
+  pdl_wait();
+  pdl_trigger();
+  const int r = blockIdx.y;
+  const int half = hd / 2;
+  const int nq = H * half, nk = KVH * half;
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (r >= rows || i >= nq + 2 * nk) return;
+  const int pos = row_pos[r];
+  const int pg = kv.page_table[(size_t)row_sess[r] * kv.max_pages + pos / kv.page];
+  auto rot = [&](float a, float b, int ii, float& x1, float& x2) {
+    if (!rope) {
+      x1 = a, x2 = b;
+      return;
+    }
+    const float freq = 1.0f / powf(theta, 2.0f * (float)ii / (float)hd);
+    float sn, cs;
+    sincosf((float)pos * freq, &sn, &cs);
+    x1 = a * cs - b * sn;
+    x2 = a * sn + b * cs;
+  };
+  if (i < nq) {  // q pair (h, ii), (h, ii + hd/2)
+    const int h = i / half, ii = i % half;
+    float* qr = q + (size_t)r * H * hd + (size_t)h * hd;
+    float x1, x2;
+    rot(qr[ii], qr[ii + half], ii, x1, x2);
+    qr[ii] = x1;
+    qr[ii + half] = x2;
+  } else if (i < nq + nk) {  // k pair
+    const int j = i - nq, h = j / half, ii = j % half;
+    const float* kr = k + (size_t)r * KVH * hd + (size_t)h * hd;
+    float x1, x2;
+    rot(kr[ii], kr[ii + half], ii, x1, x2);
+    kv.k[kv_offset(kv, pg, pos % kv.page, h, ii)] = __float2half_rn(x1);
+    kv.k[kv_offset(kv, pg, pos % kv.page, h, ii + half)] = __float2half_rn(x2);
+  } else {  // v pair (no rotation)
+    const int j = i - nq - nk, h = j / half, ii = j % half;
+    const float* vr = v + (size_t)r * KVH * hd + (size_t)h * hd;
+    kv.v[kv_offset(kv, pg, pos % kv.page, h, ii)] = __float2half_rn(vr[ii]);
+    kv.v[kv_offset(kv, pg, pos % kv.page, h, ii + half)] = __float2half_rn(vr[ii + half]);
+  }
+}
+
 
 // swiglu (tensor_utils.rs:512-532): silu(g) * u with silu(g) = g * (1 / (1 + exp(-g)))
 __global__ void k_swiglu(const float* g, const float* u, size_t n, float* out) {
@@ -265,6 +315,15 @@ __global__ void k_f16_to_f32(const uint8_t* src, size_t n, float* out) {
 
 }  // namespace
 
+int launch_qkv_post(float* q, const float* k, const float* v, int rows, int H, int KVH, int hd,
+                    int rope, float theta, const int* row_pos, const int* row_sess, const KvPages& kv,
+                    cudaStream_t st) {
+  if (!rows) return WL_OK;
+  const int n = (H + 2 * KVH) * (hd / 2);
+  return launch_k(k_qkv_post, dim3((n + 255) / 256, rows), dim3(256), 0, st, q, k, v, rows, H, KVH, hd,
+                  rope, theta, row_pos, row_sess, kv);
+}
+
 static int rmsnorm_v(const float* x, const float* w, int rows, int dim, float eps, void* y,
                      int y_mode, size_t y_plane, const PeerReduce& pr, cudaStream_t st) {
   const int n4 = dim / 4;
@@ -319,10 +378,10 @@ int launch_rmsnorm(const float* x, const float* w, int rows, int dim, float eps,
 }
 
 int launch_embed(const float* E, int d, int V, const uint32_t* ids, int rows, float* h,
-                 int* err_flag, cudaStream_t st) {
+                 int* err_flag, cudaStream_t st, int token_rows) {
   if (rows <= 0) return WL_OK;
   dim3 grid((d + 255) / 256, rows);
-  return launch_k(k_embed, grid, dim3(256), 0, st, E, d, V, ids, rows, h, err_flag);
+  return launch_k(k_embed, grid, dim3(256), 0, st, E, d, V, ids, rows, h, err_flag, token_rows);
 }
 
 int launch_swiglu(const float* g, const float* u, size_t n, float* out, cudaStream_t st) {
