@@ -365,14 +365,16 @@ def gemv_gemm_sweep(torch, dev, hbm_peak, tc_peak):
             continue
         for K, N in SWEEP_SHAPES:
             ws, _ = _rand_blocks(torch, dev, qt, K, N, 1)
-            x = torch.randn(512, K, device=dev)
+            wt = ops.qtile(ws[0], qt, K, N)  # the GEMM reads the tiled copy, as in the runtime
+            planes = ops.split_planes(torch.randn(512, K, device=dev))
+            y = torch.empty(512, N, device=dev)
             for _ in range(3):
-                ops.qgemm(ws[0], qt, x, N)
+                ops.qgemm_tiled(wt, qt, planes, N, out=y)
             torch.cuda.synchronize()
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             e0.record()
             for _ in range(10):
-                ops.qgemm(ws[0], qt, x, N)
+                ops.qgemm_tiled(wt, qt, planes, N, out=y)
             e1.record()
             torch.cuda.synchronize()
             ms = e0.elapsed_time(e1) / 10

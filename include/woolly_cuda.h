@@ -182,6 +182,13 @@ size_t wl_qtile_bytes(int ggml_type, int K, int N);
 int wl_qtile_repack(int ggml_type, const void* W, int K, int N, void* dst, void* stream);
 int wl_qgemv_tiled(int ggml_type, const void* W_tiled, int K, int N, const void* x_planes,
                    size_t x_plane, int B, float* y, void* stream);
+/* Gemm::compute (woolly-tensor/src/ops/matmul.rs:83-259) for a whole prompt
+ * on the tcgen05 tensor cores, with the weights given as their tiled copy
+ * (the copy the model runtime keeps) and the M activation rows as f16 hi/lo
+ * planes (hi plane [M][K], lo plane x_plane elements later): needs
+ * K % 64 == 0, N % 128 == 0. */
+int wl_qgemm_tiled(int ggml_type, const void* W_tiled, int K, int N, const void* x_planes,
+                   size_t x_plane, int M, float* y, void* stream);
 
 /* Quantized GEMM for prompts (prefill): y[m, o] = sum_k x[m, k] * W(k, o) for
  * all M rows in one launch, layout B (W is [K][N] GGUF blocks), the

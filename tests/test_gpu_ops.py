@@ -411,3 +411,15 @@ def test_tp_reduce_wait_gives_up():
     assert np.array_equal(h.cpu().numpy(), ref_h)
     assert counters.cpu().tolist() == [0] * (T + 1)
 
+
+
+@pytest.mark.parametrize("qt", [Q4_0, Q4_1, Q8_0])
+@pytest.mark.parametrize("K,N,M", [(256, 384, 70), (1024, 512, 300)])
+def test_qgemm_tiled_vs_oracle(qt, K, N, M):
+    """wl_qgemm_tiled: the tcgen05 GEMM streaming the tiled copy (bulk copies)
+    against the restatement."""
+    raw = quant_matrix(qt, K, N, seed=K + N + M + qt + 1)
+    x = np.random.default_rng(M + 1).standard_normal((M, K)).astype(np.float32)
+    tiled = ops.qtile(dev(raw), qt, K, N)
+    y = ops.qgemm_tiled(tiled, qt, ops.split_planes(dev(x)), N).cpu().numpy()
+    check_gemv(y, ref_gemv(qt, LAYOUT_B, raw, K, N, x))

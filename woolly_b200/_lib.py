@@ -108,6 +108,7 @@ _SIGS = {
     "wl_qtile_bytes": (C.c_size_t, [C.c_int, C.c_int, C.c_int]),
     "wl_qtile_repack": (C.c_int, [C.c_int, P, C.c_int, C.c_int, P, P]),
     "wl_qgemv_tiled": (C.c_int, [C.c_int, P, C.c_int, C.c_int, P, C.c_size_t, C.c_int, P, P]),
+    "wl_qgemm_tiled": (C.c_int, [C.c_int, P, C.c_int, C.c_int, P, C.c_size_t, C.c_int, P, P]),
     "wl_qgemv_noalloc": (C.c_int, [C.c_int, P, C.c_int, C.c_int, P, C.c_int, P, P]),
     "wl_quantized_matvec": (C.c_int, [C.c_int, P, P, P, C.c_int, C.c_int, P]),
     "wl_rmsnorm_rope": (C.c_int, [P, P, C.c_int, C.c_int, C.c_float, C.c_int, P, C.c_int,

@@ -339,6 +339,29 @@ int wl_qgemv_tiled(int type, const void* Wt, int K, int N, const void* xp, size_
   return qgemv_planes_op(type, Wt, K, N, xp, x_plane, B, y, true, (cudaStream_t)stream);
 }
 
+int wl_qgemm_tiled(int type, const void* Wt, int K, int N, const void* xp, size_t x_plane, int M,
+                   float* y, void* stream) {
+  if (!Wt || !xp || !y || M <= 0) return fail(WL_ERR_INVALID_ARGUMENT, "bad argument");
+  if (!bb(type)) return fail(WL_ERR_UNSUPPORTED, "qgemm: type must be Q4_0, Q4_1 or Q8_0");
+  GemvArgs a;
+  a.type = type;
+  a.nseg = 1;
+  a.tiled = 1;
+  a.seg[0].W = (const uint8_t*)Wt;
+  a.seg[0].N = N;
+  a.seg[0].pitch = N / 32 * bb(type);
+  a.K = K;
+  a.ldx = K;
+  a.xkind = X_PLANES;
+  a.x = xp;
+  a.x_plane = x_plane;
+  a.epi.kind = EPI_F32;
+  a.epi.y[0] = y;
+  a.epi.ldy[0] = N;
+  if (!qgemm_b_ok(a, M)) return fail(WL_ERR_INVALID_ARGUMENT, "qgemm_tiled: needs K % 64 == 0, N % 128 == 0");
+  return launch_qgemm_b(a, M, (cudaStream_t)stream);
+}
+
 // Prefill GEMM (tensor_utils.rs:118-157 over a whole sequence): tcgen05 tiles
 // when the shape allows, else the GEMV in 32-row launches.
 int wl_qgemm(int type, const void* W, int K, int N, const float* x, int M, float* y, void* stream) {
@@ -367,8 +390,17 @@ int wl_qgemm(int type, const void* W, int K, int N, const float* x, int M, float
   WL_CUDA_TRY(cudaMallocAsync((void**)&planes, (size_t)2 * M * K * sizeof(__half), st));
   int s = launch_split_planes(x, planes, (size_t)M * K, (size_t)M * K, st);
   a.x = planes;
-  if (!s && qgemm_b_ok(a, M)) {
-    s = launch_qgemm_b(a, M, st);
+  GemvArgs t = a;  // the tensor-core GEMM reads the tiled copy, made here in a temporary
+  t.tiled = 1;
+  if (!s && K % 64 == 0 && N % 128 == 0) {
+    uint8_t* tiled = nullptr;
+    s = cudaMallocAsync((void**)&tiled, qtile_bytes(type, K, N), st) == cudaSuccess
+            ? WL_OK : fail(WL_ERR_OUT_OF_MEMORY, "qgemm: tiled copy");
+    if (!s) s = launch_repack_tiled(type, (const uint8_t*)W, K, N, pitch, tiled, st);
+    t.seg[0].W = tiled;
+    if (!s && qgemm_b_ok(t, M)) s = launch_qgemm_b(t, M, st);
+    else if (!s) s = fail(WL_ERR_UNSUPPORTED, "qgemm: shape");
+    if (tiled) cudaFreeAsync(tiled, st);
   } else {
     for (int r0 = 0; r0 < M && !s; r0 += 32) {
       a.B = std::min(32, M - r0);

@@ -264,14 +264,27 @@ struct Loader {
       p.dst_pitch = align_up(p.row_bytes, 16);
     }
     p.dst_bytes = p.dst_pitch * p.rows;
-    p.dst_off = *off = reserve(p.dst_bytes);
-    pieces.push_back(p);
+    // quantized projections that the runtime re-lays-out into its tiled copy
+    // (which both the decode GEMV and the prefill GEMM read) are uploaded to a
+    // staging buffer that is freed after the repack
+    if (t->type != WL_F32 && Kl % 16 == 0 && Nl % 32 == 0) {
+      p.dst_off = tcursor;
+      tcursor = align_up(tcursor + p.dst_bytes + 256, 256);
+      *off = p.dst_off | kStaged;
+      tpieces.push_back(p);
+    } else {
+      p.dst_off = *off = reserve(p.dst_bytes);
+      pieces.push_back(p);
+    }
     out->type = t->type;
     out->K = Kl;
     out->N = Nl;
     out->pitch = (int)p.dst_pitch;
     return true;
   }
+  static constexpr size_t kStaged = size_t(1) << 62;  // offset flag: in the staging buffer
+  std::vector<Piece> tpieces;
+  size_t tcursor = 0;
 };
 
 template <class T>
@@ -383,12 +396,15 @@ static int gemv(wl_model* m, int nseg, const QMat* mats, int R, const __half* x,
   if (sw && (nseg != 2 || mats[0].N != mats[1].N))
     return fail(WL_ERR_INVALID_ARGUMENT, "SwiGLU GEMV needs gate and up of equal width");
   // prompts: every row in one tensor-core GEMM launch when the shape allows
-  if (fast && R >= kGemmMinRows) {
+  bool all_tiled = true;
+  for (int s = 0; s < nseg; s++) all_tiled = all_tiled && mats[s].wt != nullptr;
+  if (fast && all_tiled && R >= kGemmMinRows) {
     GemvArgs a;
     a.type = (int)mats[0].type;
     a.nseg = nseg;
+    a.tiled = 1;
     for (int s = 0; s < nseg; s++) {
-      a.seg[s].W = mats[s].w;
+      a.seg[s].W = mats[s].wt;
       a.seg[s].N = mats[s].N;
       a.seg[s].pitch = mats[s].pitch;
     }
@@ -968,6 +984,23 @@ int model_load(wl_ctx* ctx, const char* path, const wl_model_options* o, wl_mode
     int s = upload_pieces(m->dweights, ld.pieces, m->st);
     if (s) return s;
   }
+  uint8_t* staged = nullptr;  // GGUF bytes of the re-laid-out projections, freed below
+  if (ld.tcursor) {
+    WL_CUDA_TRY(cudaMalloc(&staged, ld.tcursor));
+    const int s = upload_pieces(staged, ld.tpieces, m->st);
+    if (s) {
+      cudaFree(staged);
+      return s;
+    }
+  }
+  struct StagedFree {
+    uint8_t*& p;
+    ~StagedFree() { cudaFree(p); }
+  } staged_guard{staged};
+  uint8_t* B0 = m->dweights;
+  auto at = [&](size_t off) -> uint8_t* {
+    return (off & Loader::kStaged) ? staged + (off & ~Loader::kStaged) : B0 + off;
+  };
   uint8_t* B = m->dweights;
   m->embd = (const float*)(B + off_embd);
   m->out_norm = (const float*)(B + off_onorm);
@@ -978,20 +1011,20 @@ int model_load(wl_ctx* ctx, const char* path, const wl_model_options* o, wl_mode
     m->out.N = V;
     m->out.pitch = m->ggml ? d * 4 : V * 4;  // ggml: one row of d per token
   } else {
-    m->out.w = B + off_out;
+    m->out.w = at(off_out);
   }
   for (int l = 0; l < m->L; l++) {
     Layer& y = m->layers[l];
     LOff& z = lo[l];
     y.attn_norm = (const float*)(B + z.an);
     y.ffn_norm = (const float*)(B + z.fn);
-    y.wq.w = B + z.q;
-    y.wk.w = B + z.k;
-    y.wv.w = B + z.v;
-    y.wo.w = B + z.o;
-    y.wg.w = B + z.g;
-    y.wu.w = B + z.u;
-    y.wd.w = B + z.dn;
+    y.wq.w = at(z.q);
+    y.wk.w = at(z.k);
+    y.wv.w = at(z.v);
+    y.wo.w = at(z.o);
+    y.wg.w = at(z.g);
+    y.wu.w = at(z.u);
+    y.wd.w = at(z.dn);
   }
   // ---- tiled decode copies (the GEMV's lane-ready layout) of every quantized projection ----
   {
@@ -1008,6 +1041,7 @@ int model_load(wl_ctx* ctx, const char* path, const wl_model_options* o, wl_mode
       offs.push_back(ok ? total : SIZE_MAX);
       if (ok) total = align_up(total + qtile_bytes((int)q->type, q->K, q->N), 256);
     }
+    m->weight_bytes += total;
     if (total) {
       WL_CUDA_TRY(cudaMalloc(&m->dtiled, total));
       for (size_t i = 0; i < mats.size(); i++) {
@@ -1018,6 +1052,14 @@ int model_load(wl_ctx* ctx, const char* path, const wl_model_options* o, wl_mode
       }
       WL_CUDA_TRY(cudaStreamSynchronize(m->st));
     }
+    // every staged projection now lives only in its tiled copy
+    for (QMat* q : mats)
+      if (staged && q->w >= staged && q->w < staged + ld.tcursor) {
+        if (!q->wt) return fail(WL_ERR_CUDA, "internal: a staged projection has no tiled copy");
+        q->w = nullptr;
+      }
+    cudaFree(staged);
+    staged = nullptr;
   }
   // ---- KV page pool ----
   m->max_sessions = opt.max_sessions;

@@ -3,24 +3,25 @@
 //
 // Y[m][n] = sum_k X[m][k] * W[k][n] for M token rows at once (woolly's
 // layout-B matmul, tensor_utils.rs:118-157, applied to a whole prompt).  One
-// CTA computes 128 weight columns x 128 token rows.  Per 64-row k stage:
-//   * the 8 warps dequantize the stage's Q4_0 / Q4_1 / Q8_0 blocks straight
-//     into shared memory as f16 hi/lo pairs with W = Whi + Wlo exactly
-//     (Q4_0 / Q8_0: Whi = f16(q*d) by HMUL2, Wlo = fma(q, d, -Whi) by HFMA2,
-//     the residual being exact in f16; Q4_1 in f32), laid out N-major with
-//     the 128-byte swizzle (a layout-B row already runs along N, so no
-//     transpose);
+// CTA computes 128 weight columns x 128 token rows.  The weights are read from
+// the tiled decode copy (qtile_bytes): a 64-row stage of a 128-column tile is
+// four or six contiguous byte ranges (codes, scales, Q4_1 mins of two 64-column
+// quarters), fetched by one thread with bulk copies (cp.async.bulk, the TMA
+// engine) that complete on an mbarrier, two stages ahead.  Per stage:
+//   * 512 threads each dequantize one (quarter, unit, lane) record of 16
+//     weights from shared memory into f16 hi/lo pairs with W = Whi + Wlo
+//     exactly (Q4_0 / Q8_0: Whi = f16(q*d) by HMUL2, Wlo = fma(q, d, -Whi) by
+//     HFMA2, the residual being exact in f16; Q4_1 in f32), stored K-major with
+//     the 128-byte swizzle (4-byte k-pair stores, bank-conflict free);
 //   * the activation hi/lo planes are copied in K-major with the same swizzle;
 //   * one thread issues 3 MMAs per 16-k step into the TMEM accumulator:
 //     Xhi*Whi + Xhi*Wlo + Xlo*Whi (the dropped Xlo*Wlo term is ~2^-22 of the
 //     product), then commits the stage to an mbarrier that gates its reuse.
-// A 3-slot ring software-pipelines the stages: while stage i is dequantized
-// and multiplied, stage i+1's activation copies and raw weight loads are in
-// flight.  The epilogue reads the accumulator with tcgen05.ld (warp w owns
-// TMEM lanes 32w..32w+31 = weight columns) and applies the same F32 / ADD /
-// QKV / SwiGLU outputs as the decode GEMV.  Every mbarrier wait is bounded; on
-// expiry the kernel raises an error bit, waits (bounded) for its issued MMAs
-// and frees its TMEM before returning.
+// The epilogue reads the accumulator with tcgen05.ld (warp w owns TMEM lanes
+// 32w..32w+31 = weight columns) and applies the same F32 / ADD / QKV / SwiGLU
+// outputs as the decode GEMV.  Every mbarrier wait is bounded; on expiry the
+// kernel raises an error bit, waits (bounded) for its issued MMAs and bulk
+// copies and frees its TMEM before returning.
 #include <cuda_fp16.h>
 
 #include <cstdint>
@@ -41,7 +42,8 @@ constexpr int kGStages = 3;
 constexpr int kGThreads = 512;  // 16 warps: two per quant block of each k row
 constexpr int kGTile = 128 * kGK * 2;  // bytes of one f16 operand tile (16 KB)
 constexpr int kGStage = 4 * kGTile;    // W hi, W lo, X hi, X lo
-constexpr int kGSmem = kGStages * kGStage + 1024 + 64;  // + alignment slack + barriers
+constexpr int kGRaw = 10240;  // per-stage raw weight bytes (largest: Q8_0 9216)
+constexpr int kGSmem = kGStages * (kGStage + kGRaw) + 1024 + 64;  // + alignment slack + barriers
 constexpr int kTmemCols = kGM;                          // f32 accumulator columns (token rows)
 
 __device__ __forceinline__ uint32_t smem_addr(const void* p) {
@@ -59,10 +61,9 @@ __device__ __forceinline__ uint64_t desc_sw128(uint32_t addr, uint32_t lbo, uint
   return d;
 }
 
-// instruction descriptor, kind::f16: D f32, A and B f16, A N-major (bit 15),
-// B K-major, N = kGM (bits 17-22, /8), M = kGN (bits 24-28, /16)
-constexpr uint32_t kIdesc = (1u << 4) | (1u << 15) | ((uint32_t)(kGM >> 3) << 17) |
-                            ((uint32_t)(kGN >> 4) << 24);
+// instruction descriptor, kind::f16: D f32, A and B f16, both K-major,
+// N = kGM (bits 17-22, /8), M = kGN (bits 24-28, /16)
+constexpr uint32_t kIdesc = (1u << 4) | ((uint32_t)(kGM >> 3) << 17) | ((uint32_t)(kGN >> 4) << 24);
 
 __device__ __forceinline__ void umma_f16(uint32_t tmem, uint64_t da, uint64_t db, uint32_t acc) {
   asm volatile(
@@ -114,99 +115,94 @@ __device__ __forceinline__ void split_pair(uint32_t q, __half2 d2, uint32_t& hi,
   lo = h2u(__hfma2(u2h(q), d2, __hneg2(h)));
 }
 
-// Half a quant block's bytes held in registers as 16-bit words (blocks are only
-// 2-byte aligned in a layout-B row): the scale (Q4_1: and min) plus the code
-// words of the half.  Q4_0 / Q4_1 half p holds code bytes 8p..8p+7 (columns
-// 8p..8p+7 and 16+8p..23+8p); Q8_0 half p holds codes 16p..16p+15.
+// Bytes of one 64-column quarter of a tiled-copy stage block (see
+// qtile_bytes): the codes of its 8 (k step, block) units in the lanes'
+// fragment order, then its f16 scales (4 per lane quad and unit), then Q4_1's
+// mins in the same order.
 template <int T>
-struct RawBlock {
-  static constexpr int HDR = T == WL_Q4_1 ? 2 : 1;  // words before the codes
-  static constexpr int CW = T == WL_Q8_0 ? 8 : 4;   // code words per half
-  uint16_t w[HDR + CW];
+struct Quarter {
+  static constexpr int CB = T == WL_Q8_0 ? 16 : 8;  // code bytes per lane per unit
+  static constexpr int CODES = 8 * 32 * CB;         // 2048 (Q8_0: 4096)
+  static constexpr int SCALES = 8 * 4 * 8;          // 256
+  static constexpr int MINS = T == WL_Q4_1 ? 256 : 0;
 };
+// one stage's raw bytes for a 128-column tile: [codes q0][codes q1][scales q0][scales q1][mins q0][mins q1]
 template <int T>
-__device__ __forceinline__ void raw_load(RawBlock<T>& r, const uint8_t* blk, int part, bool live) {
-  using R = RawBlock<T>;
-  const unsigned short* p = reinterpret_cast<const unsigned short*>(blk);
-#pragma unroll
-  for (int i = 0; i < R::HDR; i++) r.w[i] = live ? __ldg(p + i) : (unsigned short)0;
-#pragma unroll
-  for (int i = 0; i < R::CW; i++) r.w[R::HDR + i] = live ? __ldg(p + R::HDR + part * R::CW + i) : (unsigned short)0;
+__host__ __device__ constexpr int raw_stage_bytes() {
+  return 2 * (Quarter<T>::CODES + Quarter<T>::SCALES + Quarter<T>::MINS);
 }
 
-// Dequantizes half (`part`) of one quant block (16 of its 32 columns) of k row
-// `kk` of the stage into the hi and lo tiles; the block is columns b*32.. of
-// the tile.
+// Thread tid dequantizes the 16 weights of one (quarter, unit, lane) of the
+// stage's raw bytes: output columns g, g+8, 16+g, 24+g of block `blk` and k
+// rows 2t, 2t+1, 2t+8, 2t+9 of k step ks, as f16 hi/lo pairs (hi + lo = w
+// exactly) into the K-major 128-byte-swizzled A tiles (one 128-byte row per
+// tile column, k contiguous): every store is one k pair (4 bytes), and the 32
+// lanes of a warp hit 32 different banks.
 template <int T>
-__device__ __forceinline__ void dequant_half(const RawBlock<T>& raw, uint8_t* whi, uint8_t* wlo,
-                                             int kk, int b, int part, bool live) {
-  constexpr int H = RawBlock<T>::HDR;
-  uint32_t hi[8], lo[8];  // two 8-column chunks: pairs 0-3 -> chunk A, 4-7 -> chunk B
-  int chA, chB;           // chunk indices (8 columns each) within the block
+__device__ __forceinline__ void dequant_frag(const uint8_t* raw, uint8_t* whi, uint8_t* wlo, int tid) {
+  using Qt = Quarter<T>;
+  const int qd = tid >> 8, rem = tid & 255, ul = rem >> 5, lane = rem & 31;
+  const int g = lane >> 2, t = lane & 3, ks = ul >> 1, blk = ul & 1;
+  const uint8_t* codes = raw + qd * Qt::CODES + ul * 32 * Qt::CB + lane * Qt::CB;
+  const uint2 sw = *reinterpret_cast<const uint2*>(raw + 2 * Qt::CODES + qd * Qt::SCALES + (ul * 4 + t) * 8);
+  const uint32_t dpair[2] = {sw.x, sw.y};  // (d(2t), d(2t+1)), (d(2t+8), d(2t+9))
+  uint32_t mpair[2] = {0u, 0u};
+  if constexpr (T == WL_Q4_1) {
+    const uint2 mw = *reinterpret_cast<const uint2*>(raw + 2 * (Qt::CODES + Qt::SCALES) + qd * Qt::MINS +
+                                                     (ul * 4 + t) * 8);
+    mpair[0] = mw.x, mpair[1] = mw.y;
+  }
+  // q pairs: qp[h][j] = codes of column os[j] at k rows (2t + 8h, +1)
+  const int os[4] = {g, 16 + g, g + 8, 24 + g};
+  uint32_t qp[2][4];
   if constexpr (T == WL_Q8_0) {
-    chA = 2 * part;
-    chB = 2 * part + 1;
-  } else {
-    chA = part;      // low nibbles: columns 8p..8p+7
-    chB = 2 + part;  // high nibbles: columns 16+8p..
-  }
-  if (!live) {
+    const uint4 c = *reinterpret_cast<const uint4*>(codes);
+    const uint32_t w[4] = {c.x, c.y, c.z, c.w};
+    // byte (mt*4 + r)*2 + e: column mt*16 + g + 8(r&1), k rows 2t + 8(r>>1) + e
 #pragma unroll
-    for (int j = 0; j < 8; j++) hi[j] = lo[j] = 0u;
-  } else if constexpr (T == WL_Q4_1) {
-    const float d = __half2float(__ushort_as_half(raw.w[0]));
-    const float m = __half2float(__ushort_as_half(raw.w[1]));
+    for (int mt = 0; mt < 2; mt++)
 #pragma unroll
-    for (int j = 0; j < 4; j++) {
-      const uint32_t w = raw.w[H + j];
-      const float q[4] = {(float)(w & 15u), (float)((w >> 8) & 15u), (float)((w >> 4) & 15u),
-                          (float)((w >> 12) & 15u)};
-      __half hh[4], hl[4];
-#pragma unroll
-      for (int u = 0; u < 4; u++) {
-        const float v = q[u] * d + m;  // q*d + m (dequantize_q4_1, dequantize.rs:372)
-        hh[u] = __float2half_rn(v);
-        hl[u] = __float2half_rn(v - __half2float(hh[u]));
+      for (int r = 0; r < 4; r++) {
+        const int idx = mt * 4 + r;  // 16-bit word index
+        const uint32_t wd = w[idx >> 1] >> (16 * (idx & 1));
+        const uint32_t v = ((wd & 0xFFu) | ((wd & 0xFF00u) << 8)) ^ 0x00800080u;
+        const uint32_t q = h2u(__hsub2(u2h(v | 0x64006400u), u2h(0x64806480u)));  // exact int8
+        const int j = mt == 0 ? ((r & 1) ? 2 : 0) : ((r & 1) ? 3 : 1);   // os index of the column
+        qp[r >> 1][j] = q;
       }
-      hi[j] = h2u(__halves2half2(hh[0], hh[1]));
-      lo[j] = h2u(__halves2half2(hl[0], hl[1]));
-      hi[4 + j] = h2u(__halves2half2(hh[2], hh[3]));
-      lo[4 + j] = h2u(__halves2half2(hl[2], hl[3]));
-    }
-  } else if constexpr (T == WL_Q8_0) {
-    const __half dh = __ushort_as_half(raw.w[0]);
-    const __half2 d2 = __halves2half2(dh, dh);
+  } else {
+    const uint2 c = *reinterpret_cast<const uint2*>(codes);
+    const uint32_t w[2] = {c.x, c.y};
 #pragma unroll
-    for (int j = 0; j < 8; j++) {
-      const uint32_t w = raw.w[H + j];  // codes of columns 16p+2j, 16p+2j+1
-      const uint32_t v = ((w & 0xFFu) | ((w & 0xFF00u) << 8)) ^ 0x00800080u;
-      const uint32_t q = h2u(__hsub2(u2h(v | 0x64006400u), u2h(0x64806480u)));  // exact int8
-      split_pair(q, d2, hi[j], lo[j]);
-    }
-  } else {  // Q4_0: (q - 8) * d (dequantize_q4_0, dequantize.rs:315-321)
-    const __half dh = __ushort_as_half(raw.w[0]);
-    const __half2 d2 = __halves2half2(dh, dh);
+    for (int h = 0; h < 2; h++)
+#pragma unroll
+      for (int j = 0; j < 4; j++) {
+        const uint32_t n = ((w[h] >> (4 * j)) & 0x000F000Fu) | 0x64006400u;  // 1024 + q per lane
+        qp[h][j] = h2u(__hsub2(u2h(n), u2h(T == WL_Q4_0 ? 0x64086408u : 0x64006400u)));
+      }
+  }
+#pragma unroll
+  for (int h = 0; h < 2; h++) {
+    const int c8 = 2 * ks + h;  // 16-byte chunk of k rows ks*16 + 8h .. +7
 #pragma unroll
     for (int j = 0; j < 4; j++) {
-      const uint32_t w = raw.w[H + j];                                     // bytes 8p+2j, +1
-      const uint32_t lo_n = (w & 0x000Fu) | ((w & 0x0F00u) << 8);         // low nibbles
-      const uint32_t hi_n = ((w & 0x00F0u) >> 4) | ((w & 0xF000u) << 4);  // high nibbles
-      const uint32_t qa = h2u(__hsub2(u2h(lo_n | 0x64006400u), u2h(0x64086408u)));
-      const uint32_t qb = h2u(__hsub2(u2h(hi_n | 0x64006400u), u2h(0x64086408u)));
-      split_pair(qa, d2, hi[j], lo[j]);
-      split_pair(qb, d2, hi[4 + j], lo[4 + j]);
+      uint32_t hi, lo;
+      if constexpr (T == WL_Q4_1) {  // q*d + m (dequantize_q4_1, dequantize.rs:372), rounded once to hi
+        const float2 qf = __half22float2(u2h(qp[h][j]));
+        const float2 df = __half22float2(u2h(dpair[h]));
+        const float2 mf = __half22float2(u2h(mpair[h]));
+        const float v0 = qf.x * df.x + mf.x, v1 = qf.y * df.y + mf.y;
+        const __half h0 = __float2half_rn(v0), h1 = __float2half_rn(v1);
+        hi = h2u(__halves2half2(h0, h1));
+        lo = h2u(__halves2half2(__float2half_rn(v0 - __half2float(h0)), __float2half_rn(v1 - __half2float(h1))));
+      } else {
+        split_pair(qp[h][j], u2h(dpair[h]), hi, lo);
+      }
+      const int row = qd * 64 + blk * 32 + os[j];
+      const uint32_t off = (uint32_t)((row << 7) + ((c8 ^ (row & 7)) << 4) + 4 * t);
+      *reinterpret_cast<uint32_t*>(whi + off) = hi;
+      *reinterpret_cast<uint32_t*>(wlo + off) = lo;
     }
-  }
-  // column c of the tile: 64-column block jb = c / 64, 16-byte chunk c8 = (c % 64) / 8;
-  // N-major 128B-swizzled atom (k group g = kk / 8, jb) holds 8 k rows of 128 bytes
-  const int g = kk >> 3, r = kk & 7;
-#pragma unroll
-  for (int q = 0; q < 2; q++) {
-    const int c = b * 32 + (q ? chB : chA) * 8;
-    const int jb = c >> 6, c8 = (c & 63) >> 3;
-    const uint32_t off = (uint32_t)(((g * 2 + jb) << 10) + (r << 7) + ((c8 ^ r) << 4));
-    *reinterpret_cast<uint4*>(whi + off) = make_uint4(hi[q * 4], hi[q * 4 + 1], hi[q * 4 + 2], hi[q * 4 + 3]);
-    *reinterpret_cast<uint4*>(wlo + off) = make_uint4(lo[q * 4], lo[q * 4 + 1], lo[q * 4 + 2], lo[q * 4 + 3]);
   }
 }
 
@@ -223,11 +219,15 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&v)[16]) {
 
 template <int T>
 __global__ void __launch_bounds__(kGThreads, 1) k_qgemm_b(const GemvArgs a, int M) {
+  using Qt = Quarter<T>;
   constexpr int S = T == WL_Q4_0 ? 18 : T == WL_Q4_1 ? 20 : 34;
+  constexpr int STB = 512 * S;  // bytes of one (256-column group, 64-row stage) block of the tiled copy
   extern __shared__ uint8_t gsm_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(gsm_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + kGStages * kGStage);
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + kGStages);
+  uint8_t* rawb = sm + kGStages * kGStage;  // [kGStages][kGRaw] bulk-copied weight bytes
+  uint64_t* bars = reinterpret_cast<uint64_t*>(rawb + kGStages * kGRaw);  // MMA done, per slot
+  uint64_t* wbars = bars + kGStages;                                       // raw bytes landed, per slot
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(wbars + kGStages);
   __shared__ int s_fail, s_issued;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -244,6 +244,15 @@ __global__ void __launch_bounds__(kGThreads, 1) k_qgemm_b(const GemvArgs a, int 
       seg++;
     }
   }
+  // the two 64-column quarters of this tile in the tiled copies: (source, group, quarter)
+  const int nk = a.K / kGK;
+  const uint8_t* qsrc[2];
+  for (int q = 0; q < 2; q++) {
+    const GemvSeg& gs = a.seg[sw ? q : seg];
+    const int c = sw ? n0 : n0 + 64 * q;  // first column of the quarter in its segment
+    qsrc[q] = gs.W + (size_t)(c / 256) * nk * STB;  // the quarter within the group: qw0 / qw1
+  }
+  const int qw0 = (n0 % 256) / 64, qw1 = sw ? qw0 : qw0 + 1;
 
   if (warp == 0) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(
@@ -253,7 +262,7 @@ __global__ void __launch_bounds__(kGThreads, 1) k_qgemm_b(const GemvArgs a, int 
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n" ::: "memory");
   }
   if (tid == 0) {
-    for (int s = 0; s < kGStages; s++)
+    for (int s = 0; s < 2 * kGStages; s++)
       asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;\n" ::"r"(smem_addr(bars + s)) : "memory");
     asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
     s_fail = 0;
@@ -263,18 +272,39 @@ __global__ void __launch_bounds__(kGThreads, 1) k_qgemm_b(const GemvArgs a, int 
   __syncthreads();
   asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory");
   const uint32_t tmem = *tmem_slot;
+
+  // stage `it`'s weight bytes of both quarters into raw slot it % kGStages with
+  // bulk copies (TMA engine), completing on wbars[slot] (thread 0 only)
+  auto issue_w = [&](int it) {
+    const int slot = it % kGStages;
+    const uint32_t dst = smem_addr(rawb + slot * kGRaw), bar = smem_addr(wbars + slot);
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(bar),
+                 "r"((uint32_t)raw_stage_bytes<T>())
+                 : "memory");
+    for (int q = 0; q < 2; q++) {
+      const int qw = q ? qw1 : qw0;
+      const uint8_t* blk = qsrc[q] + (size_t)it * STB;
+      const uint8_t* parts[3] = {blk + qw * Qt::CODES, blk + 32 * 32 * Qt::CB + qw * Qt::SCALES,
+                                 blk + 32 * 32 * Qt::CB + 1024 + qw * 256};
+      const uint32_t dsts[3] = {dst + q * Qt::CODES, dst + 2 * Qt::CODES + q * Qt::SCALES,
+                                dst + 2 * (Qt::CODES + Qt::SCALES) + q * Qt::MINS};
+      const uint32_t sizes[3] = {(uint32_t)Qt::CODES, (uint32_t)Qt::SCALES, (uint32_t)Qt::MINS};
+      for (int k = 0; k < 3; k++)
+        if (sizes[k])
+          asm volatile(
+              "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::"r"(
+                  dsts[k]),
+              "l"(parts[k]), "r"(sizes[k]), "r"(bar)
+              : "memory");
+    }
+  };
+  // the weights do not depend on earlier kernels: start them before the PDL wait
+  if (tid == 0)
+    for (int it = 0; it < 2 && it < nk; it++) issue_w(it);
   pdl_wait();
   pdl_trigger();
 
-  const int nk = a.K / kGK;
   const __half* x = reinterpret_cast<const __half*>(a.x);
-  // dequant task of this thread: half `part` of quant block b of the tile, k row kk
-  const int kk = tid >> 3, b = (tid >> 1) & 3, part = tid & 1;
-  const GemvSeg& ws = a.seg[sw ? (b >> 1) : seg];
-  const int col0 = sw ? n0 + (b & 1) * 32 : n0 + b * 32;  // first column of the block in its segment
-  const bool wlive = col0 < ws.N;
-  const uint8_t* wsrc = ws.W + (size_t)(col0 / 32) * S;
-
   // activations of stage `it` into ring slot it % kGStages (K-major, 128B swizzle):
   // this thread copies chunk c of rows rr0 + 32q (q < 4) of both planes; the
   // swizzled destination and the source row offsets do not change per stage
@@ -306,11 +336,7 @@ __global__ void __launch_bounds__(kGThreads, 1) k_qgemm_b(const GemvArgs a, int 
     return !bad;
   };
 
-  // raw weight words run two stages ahead of the dequantization
-  RawBlock<T> r0, r1, r2;
   load_x(0);
-  raw_load<T>(r0, wsrc + (size_t)kk * ws.pitch, part, wlive);
-  if (nk > 1) raw_load<T>(r1, wsrc + (size_t)(kGK + kk) * ws.pitch, part, wlive);
   for (int it = 0; it < nk; it++) {
     const int s = it % kGStages;
     uint8_t* st = sm + s * kGStage;
@@ -322,8 +348,14 @@ __global__ void __launch_bounds__(kGThreads, 1) k_qgemm_b(const GemvArgs a, int 
       }
       load_x(it + 1);
     }
-    if (it + 2 < nk) raw_load<T>(r2, wsrc + (size_t)((it + 2) * kGK + kk) * ws.pitch, part, wlive);
-    dequant_half<T>(r0, st, st + kGTile, kk, b, part, wlive);
+    // raw slot (it + 2) % kGStages last held stage it - 1, dequantized before the
+    // previous iteration's barrier
+    if (tid == 0 && it + 2 < nk) {
+      asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+      issue_w(it + 2);
+    }
+    if (!gbar_wait(smem_addr(wbars + s), (uint32_t)((it / kGStages) & 1))) s_fail = 1;
+    dequant_frag<T>(rawb + s * kGRaw, st, st + kGTile, tid);
     if (more)
       asm volatile("cp.async.wait_group 1;\n" ::: "memory");
     else
@@ -335,11 +367,10 @@ __global__ void __launch_bounds__(kGThreads, 1) k_qgemm_b(const GemvArgs a, int 
       const uint32_t wa = smem_addr(st), xa = smem_addr(st + 2 * kGTile);
 #pragma unroll
       for (int ks = 0; ks < kGK / 16; ks++) {
-        // A (weights, N-major): a k step spans 2 k-groups of 2 KB; LBO = 1 KB (64-column
-        // block), SBO = 2 KB (8-row k group)
-        const uint64_t ah = desc_sw128(wa + ks * 4096, 1024, 2048);
-        const uint64_t al = desc_sw128(wa + kGTile + ks * 4096, 1024, 2048);
-        // B (activations, K-major): 32 bytes per k step inside the swizzle row; SBO = 1 KB
+        // A (weights) and B (activations) both K-major: 32 bytes per k step
+        // inside the 128-byte swizzle row; SBO = 1 KB (8 rows)
+        const uint64_t ah = desc_sw128(wa + ks * 32, 16, 1024);
+        const uint64_t al = desc_sw128(wa + kGTile + ks * 32, 16, 1024);
         const uint64_t bh = desc_sw128(xa + ks * 32, 16, 1024);
         const uint64_t bl = desc_sw128(xa + kGTile + ks * 32, 16, 1024);
         umma_f16(tmem, ah, bh, (it > 0 || ks > 0) ? 1u : 0u);
@@ -349,8 +380,6 @@ __global__ void __launch_bounds__(kGThreads, 1) k_qgemm_b(const GemvArgs a, int 
       umma_commit(smem_addr(bars + s));
       s_issued = it + 1;
     }
-    r0 = r1;
-    r1 = r2;
   }
   asm volatile("cp.async.wait_group 0;\n" ::: "memory");
   // wait for the last issued commit (it covers every MMA issued before it); after
@@ -364,6 +393,9 @@ __global__ void __launch_bounds__(kGThreads, 1) k_qgemm_b(const GemvArgs a, int 
                    gbar_wait(smem_addr(bars + (lastc % kGStages)), (uint32_t)((lastc / kGStages) & 1));
     ok = __syncthreads_and(ok && w && n_issued == nk);
   }
+  // bulk copies still in flight (after a failure) must land before the CTA exits
+  if (tid == 0)
+    for (int it = n_issued; it < nk && it < n_issued + 2; it++) gbar_wait(smem_addr(wbars + it % kGStages), (uint32_t)((it / kGStages) & 1));
   if (!ok && a.err && tid == 0) atomicOr(a.err, 16);
   asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory");
 
@@ -429,7 +461,7 @@ int launch_t(const GemvArgs& a, int M, int ntiles, cudaStream_t st) {
 }  // namespace
 
 bool qgemm_b_ok(const GemvArgs& a, int M) {
-  if (M < 1 || a.K <= 0 || a.K % kGK) return false;
+  if (M < 1 || a.K <= 0 || a.K % kGK || !a.tiled) return false;
   if (!(a.type == WL_Q4_0 || a.type == WL_Q4_1 || a.type == WL_Q8_0)) return false;
   if (a.xkind != X_PLANES || a.ldx % 8 || a.x_plane % 8 || (reinterpret_cast<uintptr_t>(a.x) & 15))
     return false;

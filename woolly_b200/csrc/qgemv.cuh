@@ -125,7 +125,8 @@ __device__ __forceinline__ void store_out(const GemvArgs& a, int seg, int b, int
 #endif
 
 // Prefill GEMM on tcgen05 tensor cores (qgemm.cu): all M rows of x (f16 hi/lo
-// planes, a.ldx % 8 == 0) against layout-B weights in one launch.  Needs
+// planes, a.ldx % 8 == 0) against layout-B weights given as their tiled decode
+// copies (a.tiled = 1, seg[s].W from launch_repack_tiled) in one launch.  Needs
 // K % 64 == 0 and every segment's N % 128 == 0 (SwiGLU: N % 64 == 0); rope off.
 bool qgemm_b_ok(const GemvArgs& a, int M);
 int launch_qgemm_b(const GemvArgs& a, int M, cudaStream_t st);

@@ -114,6 +114,18 @@ def qgemv_tiled(tiled: torch.Tensor, ggml_type: int, planes: torch.Tensor, n: in
     return y
 
 
+def qgemm_tiled(tiled: torch.Tensor, ggml_type: int, planes: torch.Tensor, n: int,
+                out: torch.Tensor | None = None) -> torch.Tensor:
+    """The tcgen05 prefill GEMM on the tiled copy made by qtile(); planes [2, M, K]."""
+    _dev(tiled, torch.uint8, "tiled")
+    _dev(planes, torch.float16, "planes")
+    _, M, K = planes.shape
+    y = out if out is not None else torch.empty(M, n, dtype=torch.float32, device=planes.device)
+    check(lib().wl_qgemm_tiled(int(ggml_type), tiled.data_ptr(), K, n, planes.data_ptr(), M * K, M,
+                               y.data_ptr(), _stream()))
+    return y
+
+
 def rmsnorm_rope(x: torch.Tensor, w: torch.Tensor, eps: float, *, rope: bool = False,
                  positions: torch.Tensor | None = None, head_dim: int = 0, theta: float = 10000.0,
                  out_dtype=torch.float32) -> torch.Tensor:
