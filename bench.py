@@ -300,15 +300,21 @@ SWEEP_SHAPES = [(4096, 4096), (4096, 14336), (14336, 4096)]
 
 
 def _rand_blocks(torch, dev, qt, K, N, copies):
-    """Random GGUF blocks with finite, realistic scales (d ~ 0.0078; Q4_1 m too)."""
-    S = {2: 18, 3: 20, 8: 34}[qt]
-    nbytes = K * N // 32 * S
+    """Random GGUF blocks with finite, realistic scales (d ~ 0.0078; Q4_1 m
+    too; Q4_K d 1.6e-4, dmin -0.02; Q6_K d 4.7e-4)."""
+    S, E = {2: (18, 32), 3: (20, 32), 8: (34, 32), 12: (144, 256), 14: (210, 256)}[qt]
+    nbytes = K * N // E * S
     ws = []
     for _ in range(copies):
         w = torch.randint(0, 256, (nbytes,), dtype=torch.uint8, device=dev)
         v = w.view(-1, S)
-        v[:, 0] = 0
-        v[:, 1] = 0x20
+        if qt == 12:
+            v[:, 12], v[:, 13], v[:, 14], v[:, 15] = 0x3E, 0x09, 0x1F, 0xA5
+        elif qt == 14:
+            v[:, 208], v[:, 209] = 0xB3, 0x0F
+        else:
+            v[:, 0] = 0
+            v[:, 1] = 0x20
         if qt == 3:
             v[:, 2] = 0
             v[:, 3] = 0xA0  # m ~ -0.0078
@@ -339,14 +345,15 @@ def _graph_time(torch, dev, fn, reps):
 
 def gemv_gemm_sweep(torch, dev, hbm_peak, tc_peak):
     """The standalone sweep: layout-B GEMV (tiled decode copies) for
-    Q4_0/Q4_1/Q8_0 x three shapes x B in {1, 4, 16} (weights rotated over
-    copies > 4x L2, CUDA-graph timed;
-    GB/s of algorithmic bytes and fraction of the measured HBM peak), and the
+    Q4_0/Q4_1/Q8_0/Q4_K/Q6_K x three shapes x B in {1, 4, 16} (weights
+    rotated over copies > 4x L2, CUDA-graph timed; GB/s of algorithmic bytes
+    -- the GGUF bytes of the matrix; the K-quant tiled copies are 22/18 and
+    40/26.25 of that -- and fraction of the measured HBM peak), and the
     tcgen05 prefill GEMM at M = 512 (useful TFLOP/s = 2*M*K*N / time, and the
     fraction of the measured bf16 dense peak it issues with its 3 exact MMAs)."""
     from woolly_b200 import ops
     out = {"gemv_layout_b": {}, "gemm_m512": {}}
-    for qt, name in ((2, "q4_0"), (3, "q4_1"), (8, "q8_0")):
+    for qt, name in ((2, "q4_0"), (3, "q4_1"), (8, "q8_0"), (12, "q4_k"), (14, "q6_k")):
         for K, N in SWEEP_SHAPES:
             ws, nbytes = _rand_blocks(torch, dev, qt, K, N, 2)
             copies = max(2, int(600e6 // nbytes) + 1)

@@ -43,7 +43,7 @@ typedef enum wl_status {
 } wl_status;
 
 /* GGML tensor type ids (crates/woolly-gguf/src/tensor_info.rs:15-60). */
-enum { WL_F32 = 0, WL_F16 = 1, WL_Q4_0 = 2, WL_Q4_1 = 3, WL_Q8_0 = 8 };
+enum { WL_F32 = 0, WL_F16 = 1, WL_Q4_0 = 2, WL_Q4_1 = 3, WL_Q8_0 = 8, WL_Q4_K = 12, WL_Q6_K = 14 };
 
 /* Weight layouts.  LAYOUT_A is ggml's row-major [rows][K/32 blocks] used by
  * woolly-tensor's quantized_matvec (quantization.rs:1100-1163).  LAYOUT_B is
@@ -119,16 +119,19 @@ int wl_gguf_get_str(const wl_gguf* g, const char* key, const char** out, uint64_
  * with dims [in, out]; norms f32 1+N(0,0.02)). */
 typedef struct wl_synth_config {
   uint32_t hidden, layers, heads, kv_heads, ff, vocab, context_length;
-  uint32_t weight_type;   /* WL_Q4_0 / WL_Q4_1 / WL_Q8_0 / WL_F32 */
+  uint32_t weight_type;   /* WL_Q4_0 / WL_Q4_1 / WL_Q8_0 / WL_Q4_K / WL_Q6_K / WL_F32 */
   uint32_t output_type;   /* type of output.weight; 0xFFFFFFFF = tied (omit it) */
   uint32_t sliding_window; /* 0 = none; stored as {arch}.attention.sliding_window */
   float rope_theta, norm_eps;
   uint64_t seed;
+  uint32_t vd_type;       /* 0 = weight_type; else the type of attn_v and ffn_down
+                           * (the K-quant mixes keep those as Q6_K beside Q4_K) */
 } wl_synth_config;
 
 int wl_synth_gguf(const char* path, const wl_synth_config* cfg);
-/* quantize n f32 values (n % 32 == 0) into GGUF blocks (published ggml
- * absmax/min-max block schemes; woolly's own quantizers are stubs). */
+/* quantize n f32 values (n % 32 == 0; n % 256 == 0 for Q4_K / Q6_K) into
+ * GGUF blocks (published ggml absmax/min-max block schemes; woolly's own
+ * quantizers are stubs; K-quant blocks encoded for woolly's reading of them). */
 int wl_quantize(int ggml_type, const float* src, size_t n, void* dst_blocks);
 /* fill n f32 with the writer's seeded N(mean, std) stream */
 int wl_synth_normal(uint64_t seed, uint64_t stream, float mean, float std, size_t n, float* out);
@@ -153,7 +156,10 @@ int wl_dequantize(int ggml_type, const void* blocks, size_t nbytes, size_t n, fl
  *            (woolly-tensor/src/quantization.rs:869-909) generalised to B rows
  *            and to Q4_1.
  * x is f32 [B][K] (row stride K), y is f32 [B][N].  B >= 1, any size (rows are
- * processed 32 at a time). */
+ * processed 32 at a time).
+ * K-quants (WL_Q4_K, WL_Q6_K; layout B, N % 256 == 0, K % 16 == 0): W(k, o) is
+ * woolly_gguf::dequantize's value of the super-block bytes (dequantize.rs:
+ * 381-537); computed from a temporary tiled copy (wl_qtile_repack). */
 int wl_qgemv(int ggml_type, int layout, const void* W, int K, int N, const float* x, int B,
              float* y, void* stream);
 
@@ -174,7 +180,10 @@ int wl_qgemv_planes(int ggml_type, const void* W, int K, int N, const void* x_pl
  * wl_qtile_bytes: bytes of the copy (0 for an unsupported type or shape).
  * wl_qtile_repack: writes the copy of W ([K][N] GGUF blocks, N % 32 == 0,
  *   row pitch N/32 * block bytes) into dst (wl_qtile_bytes bytes, 16-byte
- *   aligned), asynchronously on `stream`.
+ *   aligned), asynchronously on `stream`.  Q4_K / Q6_K: [K][N/256]
+ *   super-blocks (N % 256 == 0); their copy keeps the codes and, per
+ *   32 (Q4_K) or 16 (Q6_K) columns, the sub-block scale d*sc as an exact f16
+ *   (hi, lo) pair (22 and 40 bytes per 32 weights).
  * wl_qgemv_tiled: wl_qgemv_planes on the tiled copy (K % 16 == 0): the same
  *   exact per-block products; the K range is split across CTAs in steps of 64
  *   rows instead of 16, so the f32 summation order (not the math) may differ. */

@@ -24,7 +24,7 @@ extern "C" {
 #endif
 
 /* GGML type ids: crates/woolly-gguf/src/tensor_info.rs:15-60 */
-enum { OR_F32 = 0, OR_F16 = 1, OR_Q4_0 = 2, OR_Q4_1 = 3, OR_Q8_0 = 8 };
+enum { OR_F32 = 0, OR_F16 = 1, OR_Q4_0 = 2, OR_Q4_1 = 3, OR_Q8_0 = 8, OR_Q4_K = 12, OR_Q6_K = 14 };
 
 /* status codes mirror woolly_gguf::Error kinds (crates/woolly-gguf/src/error.rs) */
 enum {
@@ -134,11 +134,12 @@ void or_attention(const float* q, const float* kc, const float* vc, int rows, in
  * product's wl_synth_gguf for the same configuration) ---- */
 typedef struct or_synth_cfg {
   uint32_t hidden, layers, heads, kv_heads, ff, vocab, context_length;
-  uint32_t weight_type;    /* OR_Q4_0 / OR_Q4_1 / OR_Q8_0 / OR_F32 */
+  uint32_t weight_type;    /* OR_Q4_0 / OR_Q4_1 / OR_Q8_0 / OR_Q4_K / OR_Q6_K / OR_F32 */
   uint32_t output_type;    /* 0xFFFFFFFF: tied (no output.weight) */
   uint32_t sliding_window; /* 0 = none */
   float rope_theta, norm_eps;
   uint64_t seed;
+  uint32_t vd_type;        /* 0 = weight_type; else the type of attn_v and ffn_down */
 } or_synth_cfg;
 int or_synth_gguf(const char* path, const or_synth_cfg* cfg);
 

@@ -16,6 +16,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 LIB = os.path.join(HERE, "_build", "liboracle.so")
 
 F32, F16, Q4_0, Q4_1, Q8_0 = 0, 1, 2, 3, 8
+Q4_K, Q6_K = 12, 14
 
 
 def build() -> str:
@@ -35,7 +36,8 @@ class SynthCfg(C.Structure):
                 ("kv_heads", C.c_uint32), ("ff", C.c_uint32), ("vocab", C.c_uint32),
                 ("context_length", C.c_uint32), ("weight_type", C.c_uint32),
                 ("output_type", C.c_uint32), ("sliding_window", C.c_uint32),
-                ("rope_theta", C.c_float), ("norm_eps", C.c_float), ("seed", C.c_uint64)]
+                ("rope_theta", C.c_float), ("norm_eps", C.c_float), ("seed", C.c_uint64),
+                ("vd_type", C.c_uint32)]
 
 
 _lib = None
@@ -90,13 +92,14 @@ def half_to_float(h: int) -> float:
 def synth_gguf(path: str, *, hidden: int, layers: int, heads: int, kv_heads: int, ff: int,
                vocab: int, weight_type: int = Q4_0, output_type: int | None = None,
                tied: bool = False, context_length: int = 4096, sliding_window: int = 0,
-               rope_theta: float = 10000.0, norm_eps: float = 1e-5, seed: int = 0) -> str:
+               rope_theta: float = 10000.0, norm_eps: float = 1e-5, seed: int = 0,
+               vd_type: int = 0) -> str:
     """The seeded LLaMA-shape GGUF of the product's writer, written by the
     oracle's own C writer (synth.c), so CPU-only legs never load the product
     library."""
     cfg = SynthCfg(hidden, layers, heads, kv_heads, ff, vocab, context_length, weight_type,
                    0xFFFFFFFF if tied else (weight_type if output_type is None else output_type),
-                   sliding_window, rope_theta, norm_eps, seed)
+                   sliding_window, rope_theta, norm_eps, seed, vd_type)
     st = lib().or_synth_gguf(str(path).encode(), C.byref(cfg))
     if st:
         raise ValueError(f"or_synth_gguf status {st}")

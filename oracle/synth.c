@@ -18,7 +18,12 @@
  * 303-307): Q4_0 d = vmax/-8, q = min(15, (int8)(x/d + 8.5)); Q4_1
  * d = (max-min)/15, m = min, q = min(15, (int8)((x-m)/d + 0.5)); Q8_0
  * d = amax/127, q = round(x/d); d and m stored as IEEE f16 (round to nearest
- * even).
+ * even).  K-quants are encoded for the values woolly_gguf::dequantize reads
+ * back from them (dequantize.rs:381-537; 256 values per super-block):
+ * Q4_K w = d*sc[j]*q + dmin (dmin as stored: the block minimum; d*sc[j]*15
+ * spans sub-block j's range above it; six-bit sc at the reference's bit
+ * positions); Q6_K w = d*sc[j]*(q-32)/64 with d*sc[j]/64 = absmax_j/31 and q
+ * written to the ql/qh bits the reference reads.
  */
 #include <math.h>
 #include <stdint.h>
@@ -91,6 +96,102 @@ static void enc_q8_0(const float* x, uint8_t* b) {
   for (int j = 0; j < 32; j++) b[2 + j] = (uint8_t)(int8_t)roundf(x[j] * id);
 }
 
+static float f16_to_f32(uint16_t h) {
+  uint32_t sign = (uint32_t)(h & 0x8000u) << 16, e = (h >> 10) & 31u, man = h & 1023u, x;
+  float v;
+  if (e == 0) {
+    v = (float)man * (1.0f / 16777216.0f);
+    memcpy(&x, &v, 4);
+  } else if (e == 31) {
+    x = 0x7F800000u | (man << 13);
+  } else {
+    x = ((e + 112u) << 23) | (man << 13);
+  }
+  x |= sign;
+  memcpy(&v, &x, 4);
+  return v;
+}
+
+static void enc_q4_k(const float* x, uint8_t* b) {
+  memset(b, 0, 144);
+  float mn = x[0], rng[8], rmax = 0.0f;
+  for (int i = 1; i < 256; i++)
+    if (x[i] < mn) mn = x[i];
+  uint16_t hm = f32_to_f16(mn);
+  float dmin = f16_to_f32(hm);
+  for (int j = 0; j < 8; j++) {
+    float mx = x[32 * j];
+    for (int i = 1; i < 32; i++)
+      if (x[32 * j + i] > mx) mx = x[32 * j + i];
+    rng[j] = mx - dmin > 0.0f ? mx - dmin : 0.0f;
+    if (rng[j] > rmax) rmax = rng[j];
+  }
+  uint16_t hd = f32_to_f16(rmax / 945.0f);
+  float d = f16_to_f32(hd);
+  put16(b + 12, hd);
+  put16(b + 14, hm);
+  for (int j = 0; j < 8; j++) {
+    int sc = d > 0.0f ? (int)(rng[j] / (15.0f * d) + 0.5f) : 0;
+    if (sc > 63) sc = 63;
+    int src = (j * 3) / 2;
+    if (j % 2 == 0) {
+      b[src] |= (uint8_t)sc;
+    } else {
+      b[src] |= (uint8_t)((sc & 3) << 6);
+      b[src + 1] |= (uint8_t)(sc >> 2);
+    }
+    float step = d * (float)sc, inv = step > 0.0f ? 1.0f / step : 0.0f;
+    for (int i = 32 * j; i < 32 * j + 32; i++) {
+      int q = (int)((x[i] - dmin) * inv + 0.5f);
+      q = q < 0 ? 0 : (q > 15 ? 15 : q);
+      b[16 + i / 2] |= (uint8_t)(i % 2 == 0 ? q : q << 4);
+    }
+  }
+}
+
+static void set_bits(uint8_t* p, int shift, int width, int v) {
+  int mask = ((1 << width) - 1) << shift;
+  *p = (uint8_t)((*p & ~mask) | ((v << shift) & mask));
+}
+
+static void enc_q6_k(const float* x, uint8_t* b) {
+  memset(b, 0, 210);
+  float am[16], m = 0.0f;
+  for (int j = 0; j < 16; j++) {
+    am[j] = 0.0f;
+    for (int i = 16 * j; i < 16 * j + 16; i++)
+      if (fabsf(x[i]) > am[j]) am[j] = fabsf(x[i]);
+    if (am[j] > m) m = am[j];
+  }
+  uint16_t hd = f32_to_f16(m * 64.0f / (31.0f * 255.0f));
+  float d = f16_to_f32(hd);
+  put16(b + 208, hd);
+  uint8_t *ql = b, *qh = b + 128;
+  for (int j = 0; j < 16; j++) {
+    int sc = d > 0.0f ? (int)(am[j] * 64.0f / (31.0f * d) + 0.5f) : 0;
+    if (sc > 255) sc = 255;
+    b[192 + j] = (uint8_t)sc;
+    float step = d * (float)sc / 64.0f, inv = step > 0.0f ? 1.0f / step : 0.0f;
+    for (int i = 16 * j; i < 16 * j + 16; i++) {
+      int q = (int)(x[i] * inv + 32.5f);
+      q = q < 0 ? 0 : (q > 63 ? 63 : q);
+      int ql_idx = 64 * (i / 128) + 32 * ((i % 128) / 64) + 16 * ((i % 64) / 32) + (i % 16);
+      int qh_idx = 32 * (i / 128) + 16 * ((i % 128) / 64) + 8 * ((i % 64) / 32) + (i % 32) / 4;
+      int sh = 2 * ((i % 32) % 4);
+      if (i < 128) {
+        set_bits(ql + ql_idx, 0, 4, q & 15);
+        set_bits(qh + qh_idx, sh, 2, q >> 4);
+      } else {
+        set_bits(ql + ql_idx, 4, 4, q & 15);
+        if (sh < 6)
+          set_bits(qh + qh_idx, sh + 2, 2, q >> 4);
+        else if (qh_idx + 1 < 64)
+          set_bits(qh + qh_idx + 1, 0, 2, q >> 4);
+      }
+    }
+  }
+}
+
 static uint64_t splitmix(uint64_t* s) {
   uint64_t z = (*s += 0x9E3779B97F4A7C15ull);
   z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
@@ -147,22 +248,27 @@ typedef struct {
   int kind; /* 0 weight, 1 embedding (f32), 2 norm (mean 1) */
 } tspec;
 
-static int quantized(uint32_t t) { return t == OR_Q4_0 || t == OR_Q4_1 || t == OR_Q8_0; }
+static int quantized(uint32_t t) {
+  return t == OR_Q4_0 || t == OR_Q4_1 || t == OR_Q8_0 || t == OR_Q4_K || t == OR_Q6_K;
+}
+static uint64_t blk(uint32_t t) { return t == OR_Q4_K || t == OR_Q6_K ? 256 : (t == OR_F32 ? 1 : 32); }
 static uint64_t nelems(const tspec* t) { return t->d1 ? t->d0 * t->d1 : t->d0; }
 static uint64_t nbytes(const tspec* t) {
-  return quantized(t->type) ? nelems(t) / 32 * or_type_size((int)t->type) : nelems(t) * 4;
+  return quantized(t->type) ? nelems(t) / blk(t->type) * or_type_size((int)t->type) : nelems(t) * 4;
 }
 
 int or_synth_gguf(const char* path, const or_synth_cfg* c) {
   if (!path || !c || !c->hidden || !c->layers || !c->heads || !c->kv_heads || !c->ff ||
       !c->vocab || c->hidden % c->heads || c->heads % c->kv_heads)
     return OR_ERR_INVALID;
-  uint32_t wt = c->weight_type;
-  if (!(quantized(wt) || wt == OR_F32)) return OR_ERR_UNSUPPORTED;
+  uint32_t wt = c->weight_type, vt = c->vd_type ? c->vd_type : wt;
+  if (!(quantized(wt) || wt == OR_F32) || !(quantized(vt) || vt == OR_F32)) return OR_ERR_UNSUPPORTED;
   uint64_t d = c->hidden, kvd = d / c->heads * c->kv_heads, ff = c->ff, V = c->vocab;
-  if (wt != OR_F32 && (d % 32 || kvd % 32 || ff % 32 || V % 32)) return OR_ERR_INVALID;
   int has_out = c->output_type != 0xFFFFFFFFu;
   if (has_out && !(quantized(c->output_type) || c->output_type == OR_F32)) return OR_ERR_UNSUPPORTED;
+  if (d % blk(wt) || kvd % blk(wt) || ff % blk(wt) || d % blk(vt) || kvd % blk(vt) ||
+      (has_out && V % blk(c->output_type)))
+    return OR_ERR_INVALID;
   size_t nt = 2 + 9 * (size_t)c->layers + (has_out ? 1 : 0), i = 0;
   tspec* ts = (tspec*)calloc(nt, sizeof(tspec));
   if (!ts) return OR_ERR_IO;
@@ -177,7 +283,7 @@ int or_synth_gguf(const char* path, const or_synth_cfg* c) {
     for (int j = 0; j < 9; j++) {
       char nm[64];
       snprintf(nm, sizeof nm, "blk.%u.%s.weight", l, names[j]);
-      T(nm, a[j], b[j], b[j] ? wt : OR_F32, b[j] ? 0 : 2);
+      T(nm, a[j], b[j], b[j] ? (j == 3 || j == 8 ? vt : wt) : OR_F32, b[j] ? 0 : 2);
     }
   }
   T("output_norm.weight", d, 0, OR_F32, 2);
@@ -242,7 +348,12 @@ int or_synth_gguf(const char* path, const or_synth_cfg* c) {
           continue;
         }
         normal_chunk(c->seed, i, (uint64_t)ch, mean, 0.02f, buf, k);
-        uint8_t* q = out + c0 / 32 * tsz;
+        uint8_t* q = out + c0 / blk(t->type) * tsz;
+        if (t->type == OR_Q4_K || t->type == OR_Q6_K) {
+          for (size_t b = 0; b < k / 256; b++)
+            (t->type == OR_Q4_K ? enc_q4_k : enc_q6_k)(buf + 256 * b, q + tsz * b);
+          continue;
+        }
         for (size_t b = 0; b < k / 32; b++) {
           if (t->type == OR_Q4_0) enc_q4_0(buf + 32 * b, q + tsz * b);
           else if (t->type == OR_Q4_1) enc_q4_1(buf + 32 * b, q + tsz * b);

@@ -71,7 +71,10 @@ def test_qtile_bytes_arithmetic():
         assert lib.wl_qtile_bytes(t, 4096, 4096) == 4096 * 4096 // 32 * S
         assert lib.wl_qtile_bytes(t, 80, 288) == 2 * 2 * 512 * S  # ragged: 2 groups x 2 stages
     assert lib.wl_qtile_bytes(2, 64, 48) == 0   # N % 32 != 0
-    assert lib.wl_qtile_bytes(12, 64, 64) == 0  # Q4_K has no tiled copy
+    assert lib.wl_qtile_bytes(12, 64, 64) == 0  # K-quants need N % 256 == 0
+    assert lib.wl_qtile_bytes(12, 80, 512) == 2 * 2 * 512 * 22  # Q4_K: 22 bytes per 32 weights
+    assert lib.wl_qtile_bytes(14, 64, 256) == 512 * 40          # Q6_K: 40
+    assert lib.wl_qtile_bytes(13, 64, 256) == 0                 # Q5_K: no GEMV
     assert lib.wl_qtile_bytes(2, 0, 64) == 0
 
 
@@ -79,7 +82,8 @@ def test_new_entry_points_reject_bad_arguments_on_the_host():
     lib = _lib.lib()
     buf = (C.c_uint8 * 64)()
     p = C.cast(buf, C.c_void_p)
-    assert lib.wl_qtile_repack(12, p, 64, 64, p, None) == _lib.WL_ERR_UNSUPPORTED
+    assert lib.wl_qtile_repack(13, p, 64, 256, p, None) == _lib.WL_ERR_UNSUPPORTED
+    assert lib.wl_qtile_repack(12, p, 64, 64, p, None) == _lib.WL_ERR_INVALID_ARGUMENT  # N % 256
     assert lib.wl_qtile_repack(2, p, 64, 48, p, None) == _lib.WL_ERR_INVALID_ARGUMENT
     assert lib.wl_qtile_repack(2, None, 64, 64, p, None) == _lib.WL_ERR_INVALID_ARGUMENT
     assert lib.wl_qgemv_tiled(2, p, 40, 64, p, 0, 1, p, None) == _lib.WL_ERR_INVALID_ARGUMENT  # K % 16

@@ -291,6 +291,10 @@ def test_layout_a_reads_ggml_rows():
          output_type=O.Q4_0, context_length=64, seed=6),
     # > 65536 values per tensor: several seed chunks
     dict(hidden=512, layers=1, heads=8, kv_heads=8, ff=1024, vocab=1024, weight_type=O.Q4_0, seed=9),
+    # K-quants: Q4_K with Q6_K attn_v / ffn_down / output (the usual mix), and all-Q6_K
+    dict(hidden=512, layers=1, heads=4, kv_heads=2, ff=768, vocab=1024, weight_type=O.Q4_K,
+         vd_type=O.Q6_K, output_type=O.Q6_K, seed=10),
+    dict(hidden=256, layers=1, heads=2, kv_heads=2, ff=512, vocab=512, weight_type=O.Q6_K, seed=11),
 ])
 def test_oracle_writer_matches_product_writer(tmp_path, kw):
     """The oracle's own GGUF writer (used where the product library must not
@@ -300,3 +304,24 @@ def test_oracle_writer_matches_product_writer(tmp_path, kw):
     b = write_synthetic(str(tmp_path / "product.gguf"), **kw)
     with open(a, "rb") as fa, open(b, "rb") as fb:
         assert fa.read() == fb.read()
+
+
+@pytest.mark.parametrize("ty", [O.Q4_K, O.Q6_K])
+def test_kquant_writer_blocks_read_back(ty):
+    """The K-quant encoders target woolly's reading of the blocks
+    (dequantize.rs:381-537): Q4_K reads back within one quantization step of
+    the source values; Q6_K, whose reference reading takes values i and
+    i + 16 of a 32-run from the same low nibble, still reads back values of
+    the source's scale (same sign pattern for most of them)."""
+    from woolly_b200.gguf import quantize, synth_normal
+    x = synth_normal(7, 3, 256 * 64, 0.0, 0.02)
+    q = quantize(ty, x)
+    assert q.size == x.size // 256 * (144 if ty == O.Q4_K else 210)
+    y = O.dequantize(q, ty, x.size)
+    assert np.all(np.isfinite(y))
+    if ty == O.Q4_K:
+        step = (x.reshape(-1, 256).max(1) - x.reshape(-1, 256).min(1)) / 15
+        assert np.all(np.abs(y - x).reshape(-1, 256).max(1) <= step * 1.01 + 1e-6)
+    else:
+        assert 0.5 < y.std() / x.std() < 2.0
+        assert np.mean(np.sign(y) == np.sign(x)) > 0.7

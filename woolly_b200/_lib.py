@@ -68,7 +68,8 @@ class SynthConfig(C.Structure):
                 ("kv_heads", C.c_uint32), ("ff", C.c_uint32), ("vocab", C.c_uint32),
                 ("context_length", C.c_uint32), ("weight_type", C.c_uint32),
                 ("output_type", C.c_uint32), ("sliding_window", C.c_uint32),
-                ("rope_theta", C.c_float), ("norm_eps", C.c_float), ("seed", C.c_uint64)]
+                ("rope_theta", C.c_float), ("norm_eps", C.c_float), ("seed", C.c_uint64),
+                ("vd_type", C.c_uint32)]
 
 
 class ModelOptions(C.Structure):

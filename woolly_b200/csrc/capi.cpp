@@ -299,6 +299,26 @@ int wl_dequantize(int type, const void* blocks, size_t nbytes, size_t n, float* 
 int wl_qgemv(int type, int layout, const void* W, int K, int N, const float* x, int B, float* y,
              void* stream) {
   if (!W || !x || !y) return fail(WL_ERR_INVALID_ARGUMENT, "null pointer");
+  if (kquant_type(type)) {
+    // K-quants run from the tiled copy: made here in a stream-ordered temporary
+    if (layout != WL_LAYOUT_B) return fail(WL_ERR_UNSUPPORTED, "qgemv: K-quant weights need layout B");
+    if (K <= 0 || K % 16 || N <= 0 || N % 256 || B <= 0)
+      return fail(WL_ERR_INVALID_ARGUMENT, "qgemv: K-quants need K % 16 == 0, N % 256 == 0, B > 0");
+    cudaStream_t st = (cudaStream_t)stream;
+    uint8_t* tiled = nullptr;
+    __half* planes = nullptr;
+    const size_t n = (size_t)B * K;
+    int s = cudaMallocAsync((void**)&tiled, qtile_bytes(type, K, N), st) == cudaSuccess &&
+                    cudaMallocAsync((void**)&planes, 2 * n * sizeof(__half), st) == cudaSuccess
+                ? WL_OK
+                : fail(WL_ERR_CUDA, "qgemv: out of device memory");
+    if (!s) s = launch_repack_tiled(type, (const uint8_t*)W, K, N, N / 256 * kquant_block_bytes(type), tiled, st);
+    if (!s) s = launch_split_planes(x, planes, n, n, st);
+    if (!s) s = qgemv_planes_op(type, tiled, K, N, planes, n, B, y, true, st);
+    if (tiled) cudaFreeAsync(tiled, st);
+    if (planes) cudaFreeAsync(planes, st);
+    return s;
+  }
   if (!bb(type)) return fail(WL_ERR_UNSUPPORTED, "qgemv: type must be Q4_0, Q4_1 or Q8_0");
   if (layout != WL_LAYOUT_A && layout != WL_LAYOUT_B) return fail(WL_ERR_INVALID_ARGUMENT, "bad layout");
   if (K <= 0 || N <= 0 || B <= 0) return fail(WL_ERR_INVALID_ARGUMENT, "K, N, B must be positive");
@@ -318,24 +338,27 @@ int wl_qgemv_planes(int type, const void* W, int K, int N, const void* xp, size_
 }
 
 size_t wl_qtile_bytes(int type, int K, int N) {
-  if (!bb(type) || K <= 0 || N <= 0 || N % 32) return 0;
+  if (!(bb(type) || kquant_type(type)) || K <= 0 || N <= 0 || N % (kquant_type(type) ? 256 : 32)) return 0;
   return qtile_bytes(type, K, N);
 }
 
 int wl_qtile_repack(int type, const void* W, int K, int N, void* dst, void* stream) {
   if (!W || !dst) return fail(WL_ERR_INVALID_ARGUMENT, "null pointer");
-  if (!bb(type)) return fail(WL_ERR_UNSUPPORTED, "qtile: type must be Q4_0, Q4_1 or Q8_0");
-  if (K <= 0 || N <= 0 || N % 32) return fail(WL_ERR_INVALID_ARGUMENT, "qtile: needs K > 0, N % 32 == 0");
-  return launch_repack_tiled(type, (const uint8_t*)W, K, N, N / 32 * bb(type), (uint8_t*)dst,
-                             (cudaStream_t)stream);
+  const bool kq = kquant_type(type);
+  if (!bb(type) && !kq) return fail(WL_ERR_UNSUPPORTED, "qtile: type must be Q4_0, Q4_1, Q8_0, Q4_K or Q6_K");
+  if (K <= 0 || N <= 0 || N % (kq ? 256 : 32))
+    return fail(WL_ERR_INVALID_ARGUMENT, "qtile: needs K > 0, N % 32 == 0 (N % 256 == 0 for K-quants)");
+  const int pitch = kq ? N / 256 * kquant_block_bytes(type) : N / 32 * bb(type);
+  return launch_repack_tiled(type, (const uint8_t*)W, K, N, pitch, (uint8_t*)dst, (cudaStream_t)stream);
 }
 
 int wl_qgemv_tiled(int type, const void* Wt, int K, int N, const void* xp, size_t x_plane, int B,
                    float* y, void* stream) {
   if (!Wt || !xp || !y || B <= 0) return fail(WL_ERR_INVALID_ARGUMENT, "bad argument");
-  if (!bb(type)) return fail(WL_ERR_UNSUPPORTED, "qgemv: type must be Q4_0, Q4_1 or Q8_0");
-  if (K <= 0 || K % 16 || N <= 0 || N % 32 || (reinterpret_cast<uintptr_t>(Wt) & 15))
-    return fail(WL_ERR_INVALID_ARGUMENT, "qgemv_tiled: needs K % 16 == 0, N % 32 == 0, 16-byte aligned copy");
+  const bool kq = kquant_type(type);
+  if (!bb(type) && !kq) return fail(WL_ERR_UNSUPPORTED, "qgemv: type must be Q4_0, Q4_1, Q8_0, Q4_K or Q6_K");
+  if (K <= 0 || K % 16 || N <= 0 || N % (kq ? 256 : 32) || (reinterpret_cast<uintptr_t>(Wt) & 15))
+    return fail(WL_ERR_INVALID_ARGUMENT, "qgemv_tiled: needs K % 16 == 0, N % 32 == 0 (N % 256 == 0 for K-quants), 16-byte aligned copy");
   return qgemv_planes_op(type, Wt, K, N, xp, x_plane, B, y, true, (cudaStream_t)stream);
 }
 

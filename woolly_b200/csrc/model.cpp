@@ -248,19 +248,26 @@ struct Loader {
       p.row_bytes = (size_t)Nl * 4;
       p.dst_pitch = align_up(p.row_bytes, 16);
     } else {
-      int S = block_bytes(t->type);
+      // K-quant super-blocks hold 256 columns of one row
+      const bool kq = kquant_type((int)t->type);
+      const int S = kq ? kquant_block_bytes((int)t->type) : block_bytes(t->type);
+      const int BE = kq ? 256 : 32;
       if (!S) {
         err = name + ": weight type " + std::to_string(t->type) +
-              " is not supported (F32, Q4_0, Q4_1, Q8_0)";
+              " is not supported (F32, Q4_0, Q4_1, Q8_0, Q4_K, Q6_K)";
         return false;
       }
-      if (N % 32 || c0 % 32 || Nl % 32) {
-        err = name + ": quantized columns must be multiples of 32";
+      if (N % BE || c0 % BE || Nl % BE) {
+        err = name + ": quantized columns must be multiples of " + std::to_string(BE);
         return false;
       }
-      p.src_pitch = (size_t)N / 32 * S;
-      p.col_byte0 = (size_t)c0 / 32 * S;
-      p.row_bytes = (size_t)Nl / 32 * S;
+      if (kq && Kl % 16) {
+        err = name + ": K-quant weights need a multiple of 16 rows";
+        return false;
+      }
+      p.src_pitch = (size_t)N / BE * S;
+      p.col_byte0 = (size_t)c0 / BE * S;
+      p.row_bytes = (size_t)Nl / BE * S;
       p.dst_pitch = align_up(p.row_bytes, 16);
     }
     p.dst_bytes = p.dst_pitch * p.rows;
@@ -384,12 +391,28 @@ static int gemv(wl_model* m, int nseg, const QMat* mats, int R, const __half* x,
                 int ldx, Epilogue epi, unsigned* ctas = nullptr) {
   if (epi.kind == EPI_PEER && R > kPeerRows)
     return fail(WL_ERR_INVALID_ARGUMENT, "peer exchange: more rows than one GEMV launch");
-  for (int s = 0; s < nseg; s++)
-    if (mats[s].type != mats[0].type)
-      return fail(WL_ERR_UNSUPPORTED, "fused GEMV segments must share a quantization type");
-  bool fast = block_bytes(mats[0].type) != 0;
-  for (int s = 0; s < nseg && fast; s++)
-    fast = qgemv_b_fast_ok(mats[s].type, mats[s].K, mats[s].N, mats[s].pitch, mats[s].w);
+  bool mixed = false;
+  for (int s = 1; s < nseg; s++) mixed = mixed || mats[s].type != mats[0].type;
+  if (mixed) {
+    // a fused projection over weights of different types (the K-quant mixes
+    // store attn_v as Q6_K beside Q4_K q and k) runs as one launch per
+    // segment; the other segments keep their index with zero columns, so the
+    // epilogue routes every output as in the fused launch
+    if (epi.kind == EPI_SWIGLU || epi.kind == EPI_PEER)
+      return fail(WL_ERR_UNSUPPORTED, "SwiGLU and peer GEMV segments must share a quantization type");
+    for (int s = 0; s < nseg; s++) {
+      QMat one[3];
+      for (int j = 0; j < nseg; j++) {
+        one[j] = mats[s];
+        if (j != s) one[j].N = 0;
+      }
+      WL_TRY(gemv(m, nseg, one, R, x, x_plane, ldx, epi));
+    }
+    return WL_OK;
+  }
+  bool fast = block_bytes(mats[0].type) != 0 || kquant_type((int)mats[0].type);
+  for (int s = 0; s < nseg && fast; s++)  // (zero-width segments: see the mixed-type split above)
+    fast = mats[s].N == 0 || qgemv_b_fast_ok(mats[s].type, mats[s].K, mats[s].N, mats[s].pitch, mats[s].w);
   if (!fast && (nseg != 1 || !(epi.kind == EPI_F32 || epi.kind == EPI_ADD)))
     return fail(WL_ERR_UNSUPPORTED, "GEMV: unaligned or F32 weights only support plain outputs");
   const bool sw = epi.kind == EPI_SWIGLU;
@@ -956,7 +979,11 @@ int model_load(wl_ctx* ctx, const char* path, const wl_model_options* o, wl_mode
   // GEMV; replicated when V does not split into whole 32-column blocks or
   // the head is the tied f32 embedding
   m->Vl = V;
-  if (m->tp_size > 1 && !tied && V % (32 * m->tp_size) == 0 && nccl().AllGather) m->Vl = V / m->tp_size;
+  {
+    const GgufTensor* ot = tied ? nullptr : g->find("output.weight");
+    const int vb = ot && kquant_type((int)ot->type) ? 256 : 32;
+    if (m->tp_size > 1 && !tied && V % (vb * m->tp_size) == 0 && nccl().AllGather) m->Vl = V / m->tp_size;
+  }
   if (ok && !tied) ok = ld.add_mat("output.weight", d, V, 0, d, m->tp_rank * m->Vl, m->Vl, &m->out, &off_out);
   struct LOff {
     size_t an, fn, q, k, v, o, g, u, dn;
@@ -1037,7 +1064,8 @@ int model_load(wl_ctx* ctx, const char* path, const wl_model_options* o, wl_mode
     size_t total = 0;
     std::vector<size_t> offs;
     for (QMat* q : mats) {
-      const bool ok = block_bytes(q->type) && qgemv_b_fast_ok(q->type, q->K, q->N, q->pitch, q->w);
+      const bool ok = (block_bytes(q->type) || kquant_type((int)q->type)) &&
+                      qgemv_b_fast_ok(q->type, q->K, q->N, q->pitch, q->w);
       offs.push_back(ok ? total : SIZE_MAX);
       if (ok) total = align_up(total + qtile_bytes((int)q->type, q->K, q->N), 256);
     }
@@ -1322,8 +1350,13 @@ int decode_step_device(wl_model* m, wl_session* const* ss, int n, const uint32_t
 int decode_kernel_count(const wl_model* m, int n) {
   const int nsplit = attention_plan_splits(n, m->KVHl, m->opt.max_context, m->sms);
   int chunks = (n + 31) / 32;
-  int per_layer = 2 + chunks * 4 + 1 + (nsplit > 1 ? 1 : 0);
-  return 1 + m->L * per_layer + 1 + chunks + (m->Vl != m->V ? 1 : 0);
+  int total = 1 + 1 + chunks + (m->Vl != m->V ? 1 : 0);
+  for (const Layer& y : m->layers) {
+    // q/k/v of different types (K-quant mixes) take one launch each
+    const bool mixed = y.wq.type != y.wk.type || y.wq.type != y.wv.type;
+    total += 2 + chunks * (3 + (mixed ? 3 : 1)) + 1 + (nsplit > 1 ? 1 : 0);
+  }
+  return total;
 }
 
 }  // namespace wl

@@ -60,6 +60,23 @@ template <>
 struct QT<WL_Q8_0> {
   static constexpr int S = 34, QOFF = 2, SP = 272;
 };
+// K-quants run from the tiled copy only; S is the tiled bytes per 32-column
+// unit of one k row: Q4_K 16 code bytes + the (hi, lo) f16 pair of d*sc + the
+// f16 dmin; Q6_K 32 code bytes + two (hi, lo) pairs (one per 16 columns)
+template <>
+struct QT<WL_Q4_K> {
+  static constexpr int S = 22, QOFF = 0, SP = 176;
+};
+template <>
+struct QT<WL_Q6_K> {
+  static constexpr int S = 40, QOFF = 0, SP = 320;
+};
+template <int T>
+constexpr bool kB8 = T == WL_Q8_0 || T == WL_Q6_K;  // one code byte per weight
+template <int T>
+constexpr bool kMin = T == WL_Q4_1 || T == WL_Q4_K;  // a per-block additive term
+template <int T>
+constexpr bool kKq = T == WL_Q4_K || T == WL_Q6_K;  // scale given as an exact f16 pair
 
 constexpr int kThreads = 128;  // layout A
 constexpr int kThreadsB = 128;  // layout B: warps 4..7 take the second half of each stage's k-steps
@@ -153,6 +170,17 @@ __device__ __forceinline__ void scale_split(uint32_t d, uint32_t xh, uint32_t xl
   __half2 r = __hfma2(as_h2(d), as_h2(xh), __hneg2(hh));
   hi = as_u(hh);
   lo = as_u(__hfma2(as_h2(d), as_h2(xl), r));
+}
+// The same for a scale s = sh + sl that needs more than 11 bits (the K-quant
+// sub-block scale d*sc, up to 19 bits, split exactly into two f16 at repack):
+// hi = f16(sh*xh), lo = f16(sh*xl + sl*xh + (sh*xh - hi)).
+__device__ __forceinline__ void scale_split2(uint32_t sh, uint32_t sl, uint32_t xh, uint32_t xl,
+                                             uint32_t& hi, uint32_t& lo) {
+  __half2 hh = __hmul2(as_h2(sh), as_h2(xh));
+  __half2 r = __hfma2(as_h2(sh), as_h2(xh), __hneg2(hh));
+  r = __hfma2(as_h2(sl), as_h2(xh), r);
+  hi = as_u(hh);
+  lo = as_u(__hfma2(as_h2(sh), as_h2(xl), r));
 }
 
 
@@ -379,7 +407,9 @@ __global__ void __launch_bounds__(kThreadsB) k_qgemv_b(const GemvArgs a) {
   // no HSUB2).  Q4_1 has no offset; Q4_0's -8 and Q8_0's -128 (codes stored
   // as q + 128) then cost a ones-MMA per B fragment, which pays only when LOC
   // halves the MMAs (Q4_0 decode: B = 1 +7%, B = 16 -2%).
-  constexpr bool SUBN = TLD && (T == WL_Q4_1 || LOC);
+  // K-quants: Q4_K is Q4_1 with the two-term scale; Q6_K is Q8_0-like codes
+  // (q - 32) with one scale per 16 columns, i.e. per m-tile
+  constexpr bool SUBN = TLD && (kMin<T> || (LOC && !kKq<T>));
   constexpr float kOff = T == WL_Q4_0 ? -8.0f : -128.0f;  // SUBN offset of Q4_0 / Q8_0
   const int tid = threadIdx.x, lane = tid & 31;
   const int warp = (tid >> 5) & 3, kpart = tid >> 7;  // block pair, k-step part
@@ -397,7 +427,7 @@ __global__ void __launch_bounds__(kThreadsB) k_qgemv_b(const GemvArgs a) {
   }
   const int Nseg = a.seg[seg].N, pitch = a.seg[seg].pitch;
   constexpr int STB = 512 * Q::S;                  // tiled: bytes of one (group, stage) block
-  constexpr int CODEB = 1024 * (T == WL_Q8_0 ? 16 : 8);  // tiled: code bytes of a stage block
+  constexpr int CODEB = 1024 * (kB8<T> ? 16 : 8);  // tiled: code bytes of a stage block
   const uint8_t* W = TLD ? a.seg[seg].W + ((size_t)lg * ((a.K + kRows - 1) / kRows) + split * (a.kchunk / kRows)) * STB
                          : a.seg[seg].W + (size_t)lg * kGroupBlocks * Q::S;
   const int k0 = split * a.kchunk;
@@ -521,17 +551,32 @@ __global__ void __launch_bounds__(kThreadsB) k_qgemv_b(const GemvArgs a) {
       for (int blk = 0; blk < 2; blk++) {
         uint32_t af[2][4];
         uint32_t d01, d23, m01 = 0, m23 = 0;
+        uint32_t e01 = 0, e23 = 0;                        // K-quants: lo halves of the scales
+        uint32_t d01b = 0, d23b = 0, e01b = 0, e23b = 0;  // Q6_K: scales of m-tile 1
         if constexpr (TLD) {
           const int u = (warp * 4 + ks) * 2 + blk;
-          const uint2 sw = *reinterpret_cast<const uint2*>(rs + CODEB + (u * 4 + t) * 8);
-          d01 = sw.x;
-          d23 = sw.y;
+          if constexpr (T == WL_Q6_K) {
+            const uint4 s0 = *reinterpret_cast<const uint4*>(rs + CODEB + (u * 8 + t) * 16);
+            const uint4 s1 = *reinterpret_cast<const uint4*>(rs + CODEB + (u * 8 + 4 + t) * 16);
+            d01 = s0.x, d23 = s0.y, e01 = s0.z, e23 = s0.w;
+            d01b = s1.x, d23b = s1.y, e01b = s1.z, e23b = s1.w;
+          } else if constexpr (T == WL_Q4_K) {
+            const uint4 sw = *reinterpret_cast<const uint4*>(rs + CODEB + (u * 4 + t) * 16);
+            d01 = sw.x, d23 = sw.y, e01 = sw.z, e23 = sw.w;
+            const uint2 mw = *reinterpret_cast<const uint2*>(rs + CODEB + 2048 + (u * 4 + t) * 8);
+            m01 = mw.x;
+            m23 = mw.y;
+          } else {
+            const uint2 sw = *reinterpret_cast<const uint2*>(rs + CODEB + (u * 4 + t) * 8);
+            d01 = sw.x;
+            d23 = sw.y;
+          }
           if constexpr (T == WL_Q4_1) {
             const uint2 mw = *reinterpret_cast<const uint2*>(rs + CODEB + 1024 + (u * 4 + t) * 8);
             m01 = mw.x;
             m23 = mw.y;
           }
-          if constexpr (T == WL_Q8_0) {
+          if constexpr (kB8<T>) {
             const uint4 cw = *reinterpret_cast<const uint4*>(rs + u * 512 + lane * 16);
             const uint32_t w[4] = {cw.x, cw.y, cw.z, cw.w};
 #pragma unroll
@@ -616,9 +661,28 @@ __global__ void __launch_bounds__(kThreadsB) k_qgemv_b(const GemvArgs a) {
 #pragma unroll
         for (int n = 0; n < NT; n++) {
           uint32_t bh0, bl0, bh1, bl1;
-          scale_split(d01, xh[n][0], xl[n][0], bh0, bl0);
-          scale_split(d23, xh[n][1], xl[n][1], bh1, bl1);
-          if constexpr (LOC) {
+          if constexpr (kKq<T>) {
+            scale_split2(d01, e01, xh[n][0], xl[n][0], bh0, bl0);
+            scale_split2(d23, e23, xh[n][1], xl[n][1], bh1, bl1);
+          } else {
+            scale_split(d01, xh[n][0], xl[n][0], bh0, bl0);
+            scale_split(d23, xh[n][1], xl[n][1], bh1, bl1);
+          }
+          if constexpr (T == WL_Q6_K) {  // m-tile 1 has its own scales
+            uint32_t ch0, cl0, ch1, cl1;
+            scale_split2(d01b, e01b, xh[n][0], xl[n][0], ch0, cl0);
+            scale_split2(d23b, e23b, xh[n][1], xl[n][1], ch1, cl1);
+            if constexpr (LOC) {
+              const bool loc = g >= 4;
+              mma16816(acc[blk][0][n], af[0], loc ? bl0 : bh0, loc ? bl1 : bh1);
+              mma16816(acc[blk][1][n], af[1], loc ? cl0 : ch0, loc ? cl1 : ch1);
+            } else {
+              mma16816(acc[blk][0][n], af[0], bh0, bh1);
+              mma16816(acc[blk][1][n], af[1], ch0, ch1);
+              mma16816(acc[blk][0][n], af[0], bl0, bl1);
+              mma16816(acc[blk][1][n], af[1], cl0, cl1);
+            }
+          } else if constexpr (LOC) {
             const bool loc = g >= 4;  // this lane's B column carries a lo part
             const uint32_t b0 = loc ? bl0 : bh0, b1 = loc ? bl1 : bh1;
             mma16816(acc[blk][0][n], af[0], b0, b1);
@@ -629,7 +693,7 @@ __global__ void __launch_bounds__(kThreadsB) k_qgemv_b(const GemvArgs a) {
             mma16816(acc[blk][0][n], af[0], bl0, bl1);
             mma16816(acc[blk][1][n], af[1], bl0, bl1);
           }
-          if constexpr (SUBN && T != WL_Q4_1) {  // sum_k x*d of the block, for the offset
+          if constexpr (SUBN && !kMin<T>) {  // sum_k x*d of the block, for the offset
             const uint32_t ones[4] = {kOnes, kOnes, kOnes, kOnes};
             if constexpr (LOC) {
               const bool loc = g >= 4;
@@ -639,7 +703,7 @@ __global__ void __launch_bounds__(kThreadsB) k_qgemv_b(const GemvArgs a) {
               mma16816(accm[blk][n], ones, bl0, bl1);
             }
           }
-          if constexpr (T == WL_Q4_1) {
+          if constexpr (kMin<T>) {
             const uint32_t ones[4] = {kOnes, kOnes, kOnes, kOnes};
             uint32_t mh0, ml0, mh1, ml1;
             scale_split(m01, xh[n][0], xl[n][0], mh0, ml0);
@@ -679,10 +743,12 @@ __global__ void __launch_bounds__(kThreadsB) k_qgemv_b(const GemvArgs a) {
               const int c = (warp * 2 + blk) * 32 + 16 * mt + (TLD ? g + 8 * (q >> 1) : 2 * g + (q >> 1));
               // m-tile 1 of the 4-bit types accumulated 16x the codes; the
               // subnormal codes of the tiled path carry 2^-24 (exact powers of two)
-              const float sc = SUBN ? ((T != WL_Q8_0 && mt == 1) ? 1048576.0f : 16777216.0f)
-                                    : (T != WL_Q8_0 && mt == 1) ? 0.0625f : 1.0f;
-              // accm: sum x*m (Q4_1) or, subnormal Q4_0 / Q8_0, sum x*d times the offset
-              const float cm = (SUBN && T != WL_Q4_1) ? kOff : 1.0f;
+              // (Q6_K: the scale pair is d*sc, the reference's /64 is applied here)
+              const float sc = SUBN ? ((!kB8<T> && mt == 1) ? 1048576.0f : 16777216.0f)
+                               : T == WL_Q6_K ? 0.015625f
+                                              : (!kB8<T> && mt == 1) ? 0.0625f : 1.0f;
+              // accm: sum x*m (Q4_1 / Q4_K) or, subnormal Q4_0 / Q8_0, sum x*d times the offset
+              const float cm = (SUBN && !kMin<T>) ? kOff : 1.0f;
               float v = acc[blk][mt][n][q] * sc + cm * accm[blk][n][q];
               if constexpr (LOC) {  // column b + 4 (lane t + 2) holds row b's lo part
                 v += __shfl_xor_sync(0xffffffffu, v, 2);
@@ -1019,12 +1085,114 @@ __global__ void k_repack_tiled(const uint8_t* src, int K, int N, int pitch, uint
   }
 }
 
+// K-quant super-blocks (256 columns of one k row, one GEMV group) into the
+// same tile geometry.  Codes and scales follow woolly_gguf::dequantize's own
+// reading of the blocks (dequantize.rs:381-537), so the tiled product equals
+// the dequantized matrix times x:
+//   Q4_K (144 bytes): w(i) = d*sc[i/32]*q(i) + dmin, q(i) nibble i%2 of byte
+//     16 + i/2, sc the six-bit field of byte 3j/2 (low six bits for even j,
+//     top two bits plus the next byte's low nibble for odd j), d and dmin f16
+//     at bytes 12 and 14.  Tiled: q as the Q4_1 nibbles, d*sc (exact in f32,
+//     <= 17 significant bits) as the f16 pair (hi, lo = d*sc - hi), dmin as
+//     the Q4_1 min.
+//   Q6_K (210 bytes): w(i) = d*sc[i/16]*(q(i) - 32)/64, q(i) from ql (bytes
+//     0-127) and qh (128-191) by the reference's index arithmetic, sc bytes
+//     192-207 (unsigned), d f16 at 208.  Tiled: (q - 32) as Q8_0 code bytes,
+//     d*sc (<= 19 bits) as an f16 pair per 16 columns; the 1/64 is applied
+//     to the f32 accumulator.
+// Both splits are exact: d*sc is a multiple of d's f16 quantum (>= 2^-24)
+// and has at most 19 significant bits, so lo holds the remaining <= 8 bits.
+__device__ __forceinline__ int kq_code(int T, const uint8_t* b, int i) {
+  if (T == WL_Q4_K) return (i % 2 == 0) ? (b[16 + i / 2] & 15) : (b[16 + i / 2] >> 4);
+  const uint8_t *ql = b, *qh = b + 128;
+  const int ql_idx = 64 * (i / 128) + 32 * ((i % 128) / 64) + 16 * ((i % 64) / 32) + (i % 16);
+  const int qh_idx = 32 * (i / 128) + 16 * ((i % 128) / 64) + 8 * ((i % 64) / 32) + (i % 32) / 4;
+  const int sh = 2 * ((i % 32) % 4);
+  const int qv = qh[qh_idx];
+  if (i < 128) return (ql[ql_idx] & 15) | (((qv >> sh) & 3) << 4);
+  const int ext = sh < 6 ? ((qv >> (sh + 2)) & 3) : (qh_idx + 1 < 64 ? (qh[qh_idx + 1] & 3) : 0);
+  return (ql[ql_idx] >> 4) | (ext << 4);
+}
+__device__ __forceinline__ float kq_scale(int T, const uint8_t* b, int j) {
+  if (T == WL_Q4_K) {
+    const int src = (j * 3) / 2;
+    const int sc = (j % 2 == 0) ? (b[src] & 63) : (((b[src] >> 6) | ((b[src + 1] & 15) << 2)) & 63);
+    return __fmul_rn(__half2float(__ushort_as_half((uint16_t)(b[12] | (b[13] << 8)))), (float)sc);
+  }
+  return __fmul_rn(__half2float(__ushort_as_half((uint16_t)(b[208] | (b[209] << 8)))), (float)b[192 + j]);
+}
+
+template <int T>
+__global__ void k_repack_tiled_k(const uint8_t* src, int K, int pitch, uint8_t* dst, int stages,
+                                 size_t total) {
+  constexpr int STB = 512 * QT<T>::S;
+  constexpr int CB = T == WL_Q6_K ? 16 : 8;
+  constexpr int CODEB = 1024 * CB;
+  constexpr int SBB = T == WL_Q4_K ? 144 : 210;
+  const size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
+  if (i >= total) return;
+  const int lane = (int)(i & 31), u = (int)((i >> 5) & 31);
+  const size_t gs = i >> 10;
+  const int stage = (int)(gs % stages);
+  const int group = (int)(gs / stages);  // = super-block column index
+  const int w = u >> 3, ks = (u >> 1) & 3, blk = u & 1;
+  const int j32 = w * 2 + blk;  // 32-column unit within the super-block
+  const int g = lane >> 2, t = lane & 3;
+  const int kb = stage * kRows + ks * 16;
+  uint8_t* D = dst + gs * STB;
+  auto sb = [&](int k) { return src + (size_t)k * pitch + (size_t)group * SBB; };
+  auto code = [&](int o, int k) -> uint32_t {  // output o (0..31) of the unit at k row k
+    if (k >= K) return 0u;
+    const int q = kq_code(T, sb(k), j32 * 32 + o);
+    return T == WL_Q6_K ? (uint32_t)(uint8_t)(int8_t)(q - 32) : (uint32_t)q;
+  };
+  uint8_t* C = D + u * (32 * CB) + lane * CB;
+  if (T == WL_Q6_K) {
+    for (int mt = 0; mt < 2; mt++)
+      for (int r = 0; r < 4; r++) {
+        const int o = mt * 16 + g + 8 * (r & 1), k = kb + 2 * t + 8 * (r >> 1);
+        C[(mt * 4 + r) * 2] = (uint8_t)code(o, k);
+        C[(mt * 4 + r) * 2 + 1] = (uint8_t)code(o, k + 1);
+      }
+  } else {
+    for (int wd = 0; wd < 2; wd++) {
+      const int k = kb + 2 * t + 8 * wd;
+      const int os[4] = {g, 16 + g, g + 8, 24 + g};
+      uint32_t word = 0;
+      for (int jj = 0; jj < 8; jj++) word |= code(os[jj & 3], k + (jj >> 2)) << (4 * jj);
+      for (int jj = 0; jj < 4; jj++) C[wd * 4 + jj] = (uint8_t)(word >> (8 * jj));
+    }
+  }
+  if (g != 0) return;
+  const int rows[4] = {kb + 2 * t, kb + 2 * t + 1, kb + 2 * t + 8, kb + 2 * t + 9};
+  for (int mt = 0; mt < (T == WL_Q6_K ? 2 : 1); mt++) {
+    uint16_t* sp = reinterpret_cast<uint16_t*>(D + CODEB + ((T == WL_Q6_K ? u * 8 + mt * 4 : u * 4) + t) * 16);
+    for (int r = 0; r < 4; r++) {
+      const float sv = rows[r] < K ? kq_scale(T, sb(rows[r]), T == WL_Q6_K ? j32 * 2 + mt : j32) : 0.f;
+      const __half hi = __float2half_rn(sv);
+      const __half lo = __float2half_rn(sv - __half2float(hi));
+      sp[r] = __half_as_ushort(hi);
+      sp[4 + r] = __half_as_ushort(lo);
+    }
+  }
+  if (T == WL_Q4_K) {
+    uint16_t* mp = reinterpret_cast<uint16_t*>(D + CODEB + 2048 + (u * 4 + t) * 8);
+    for (int r = 0; r < 4; r++) {
+      const uint8_t* b = rows[r] < K ? sb(rows[r]) : nullptr;
+      mp[r] = b ? (uint16_t)(b[14] | (b[15] << 8)) : (uint16_t)0;
+    }
+  }
+}
+
 template <int T>
 int repack_tiled_t(const uint8_t* src, int K, int N, int pitch, uint8_t* dst, cudaStream_t st) {
   const int groups = (N + kColsB - 1) / kColsB, stages = (K + kRows - 1) / kRows;
   const size_t total = (size_t)groups * stages * 1024;
   if (!total) return WL_OK;
-  k_repack_tiled<T><<<(unsigned)((total + 255) / 256), 256, 0, st>>>(src, K, N, pitch, dst, stages, total);
+  if constexpr (kKq<T>)
+    k_repack_tiled_k<T><<<(unsigned)((total + 255) / 256), 256, 0, st>>>(src, K, pitch, dst, stages, total);
+  else
+    k_repack_tiled<T><<<(unsigned)((total + 255) / 256), 256, 0, st>>>(src, K, N, pitch, dst, stages, total);
   WL_CUDA_TRY(cudaGetLastError());
   return WL_OK;
 }
@@ -1059,19 +1227,47 @@ int dispatch_b(const GemvArgs& a, cudaStream_t st) {
 
 template <int T, bool LB>
 int dispatch(const GemvArgs& a, cudaStream_t st) {
-  if (LB) return a.tiled ? dispatch_b<T, true>(a, st) : dispatch_b<T, false>(a, st);
-  switch ((a.B + 7) / 8) {
-    case 1: return launch_a_t<T, 1>(a, st);
-    case 2: return launch_a_t<T, 2>(a, st);
-    case 3: return launch_a_t<T, 3>(a, st);
-    case 4: return launch_a_t<T, 4>(a, st);
+  if constexpr (kKq<T>) {
+    if (!LB || !a.tiled) return fail(WL_ERR_UNSUPPORTED, "qgemv: K-quant weights run from their tiled copy only");
+    return dispatch_b<T, true>(a, st);
+  } else {
+    if (LB) return a.tiled ? dispatch_b<T, true>(a, st) : dispatch_b<T, false>(a, st);
+    switch ((a.B + 7) / 8) {
+      case 1: return launch_a_t<T, 1>(a, st);
+      case 2: return launch_a_t<T, 2>(a, st);
+      case 3: return launch_a_t<T, 3>(a, st);
+      case 4: return launch_a_t<T, 4>(a, st);
+    }
+    return fail(WL_ERR_INVALID_ARGUMENT, "qgemv: B must be 1..32 per launch");
   }
-  return fail(WL_ERR_INVALID_ARGUMENT, "qgemv: B must be 1..32 per launch");
 }
 
 int block_bytes(int type) { return type == WL_Q4_0 ? 18 : type == WL_Q4_1 ? 20 : type == WL_Q8_0 ? 34 : 0; }
+// bytes of one 32-column unit of one k row in the tiled copy
+int unit_bytes(int type) {
+  switch (type) {
+    case WL_Q4_0: return QT<WL_Q4_0>::S;
+    case WL_Q4_1: return QT<WL_Q4_1>::S;
+    case WL_Q8_0: return QT<WL_Q8_0>::S;
+    case WL_Q4_K: return QT<WL_Q4_K>::S;
+    case WL_Q6_K: return QT<WL_Q6_K>::S;
+  }
+  return 0;
+}
+size_t smem_b_type(int type, int NT) {
+  switch (type) {
+    case WL_Q4_1: return smem_b<WL_Q4_1>(NT);
+    case WL_Q8_0: return smem_b<WL_Q8_0>(NT);
+    case WL_Q4_K: return smem_b<WL_Q4_K>(NT);
+    case WL_Q6_K: return smem_b<WL_Q6_K>(NT);
+  }
+  return smem_b<WL_Q4_0>(NT);
+}
 
 }  // namespace
+
+bool kquant_type(int type) { return type == WL_Q4_K || type == WL_Q6_K; }
+int kquant_block_bytes(int type) { return type == WL_Q4_K ? 144 : type == WL_Q6_K ? 210 : 0; }
 
 int qgemv_group_cols(int layout) { return layout == WL_LAYOUT_B ? kColsB : kColsA; }
 
@@ -1079,6 +1275,8 @@ int qgemv_group_cols(int layout) { return layout == WL_LAYOUT_B ? kColsB : kCols
 // 16 readable bytes past the last row's payload (the tail chunk of a partial
 // group may straddle the end of the payload); K a multiple of 16.
 bool qgemv_b_fast_ok(int type, int K, int N, int pitch, const void* W) {
+  if (kquant_type(type))  // the repack reads any pitch; the GEMV reads the tiled copy
+    return K % 16 == 0 && K > 0 && N % 256 == 0 && N > 0 && pitch >= N / 256 * kquant_block_bytes(type);
   const int S = block_bytes(type);
   if (!S) return false;
   return K % 16 == 0 && K > 0 && N % 32 == 0 && pitch % 16 == 0 && pitch >= N / 32 * S &&
@@ -1108,6 +1306,8 @@ KernB kernel_b_t(int B) {
 KernB kernel_b(const GemvArgs& a) {
   if (a.type == WL_Q4_0) return a.tiled ? kernel_b_t<WL_Q4_0, true>(a.B) : kernel_b_t<WL_Q4_0, false>(a.B);
   if (a.type == WL_Q4_1) return a.tiled ? kernel_b_t<WL_Q4_1, true>(a.B) : kernel_b_t<WL_Q4_1, false>(a.B);
+  if (a.type == WL_Q4_K) return kernel_b_t<WL_Q4_K, true>(a.B);
+  if (a.type == WL_Q6_K) return kernel_b_t<WL_Q6_K, true>(a.B);
   return a.tiled ? kernel_b_t<WL_Q8_0, true>(a.B) : kernel_b_t<WL_Q8_0, false>(a.B);
 }
 
@@ -1161,8 +1361,7 @@ void qgemv_plan(GemvArgs& a, int layout, int num_sms) {
   int per_sm = 2;
   if (layout == WL_LAYOUT_B) {
     const int NT = (std::min(a.B, 32) + 7) / 8;
-    const size_t sm = a.type == WL_Q4_0 ? smem_b<WL_Q4_0>(NT)
-                      : a.type == WL_Q4_1 ? smem_b<WL_Q4_1>(NT) : smem_b<WL_Q8_0>(NT);
+    const size_t sm = smem_b_type(a.type, NT);
     per_sm = std::max(1, std::min(kPlanCtasPerSm, (int)(kSmemPerSm / (sm + 2048))));
   }
   const int target = per_sm * num_sms;
@@ -1176,8 +1375,7 @@ void qgemv_plan(GemvArgs& a, int layout, int num_sms) {
   // clusters must also fit one wave: a GPC holds whole clusters only, so a
   // split that fits by CTA count can still leave CTAs for a second wave
   const int NT = (std::min(a.B, 32) + 7) / 8;
-  const size_t sm = a.type == WL_Q4_0 ? smem_b<WL_Q4_0>(NT)
-                    : a.type == WL_Q4_1 ? smem_b<WL_Q4_1>(NT) : smem_b<WL_Q8_0>(NT);
+  const size_t sm = smem_b_type(a.type, NT);
   const int cx = a.epi.kind == EPI_SWIGLU ? 2 : 1;
   const KernB k = kernel_b(a);
   while (a.csplit > 1 && groups * a.csplit > cluster_capacity(k, cx, a.csplit, sm)) {
@@ -1188,7 +1386,8 @@ void qgemv_plan(GemvArgs& a, int layout, int num_sms) {
 }
 
 size_t qtile_bytes(int type, int K, int N) {
-  const int S = block_bytes(type);
+  if (kquant_type(type) && N % 256) return 0;
+  const int S = unit_bytes(type);
   return (size_t)((N + kColsB - 1) / kColsB) * ((K + kRows - 1) / kRows) * 512 * S;
 }
 
@@ -1199,6 +1398,11 @@ int launch_repack_tiled(int type, const uint8_t* src, int K, int N, int pitch, u
     case WL_Q4_0: return repack_tiled_t<WL_Q4_0>(src, K, N, pitch, dst, st);
     case WL_Q4_1: return repack_tiled_t<WL_Q4_1>(src, K, N, pitch, dst, st);
     case WL_Q8_0: return repack_tiled_t<WL_Q8_0>(src, K, N, pitch, dst, st);
+    case WL_Q4_K:
+    case WL_Q6_K:
+      if (N % 256) return fail(WL_ERR_INVALID_ARGUMENT, "repack: K-quant N % 256 != 0");
+      return type == WL_Q4_K ? repack_tiled_t<WL_Q4_K>(src, K, N, pitch, dst, st)
+                             : repack_tiled_t<WL_Q6_K>(src, K, N, pitch, dst, st);
   }
   return fail(WL_ERR_UNSUPPORTED, "repack: unsupported type " + std::to_string(type));
 }
@@ -1208,6 +1412,8 @@ int launch_qgemv_b(const GemvArgs& a, cudaStream_t st) {
     case WL_Q4_0: return dispatch<WL_Q4_0, true>(a, st);
     case WL_Q4_1: return dispatch<WL_Q4_1, true>(a, st);
     case WL_Q8_0: return dispatch<WL_Q8_0, true>(a, st);
+    case WL_Q4_K: return dispatch<WL_Q4_K, true>(a, st);
+    case WL_Q6_K: return dispatch<WL_Q6_K, true>(a, st);
   }
   return fail(WL_ERR_UNSUPPORTED, "qgemv: unsupported type " + std::to_string(a.type));
 }

@@ -142,6 +142,9 @@ int launch_qgemv_generic(int type, int layout, const uint8_t* W, int K, int N, i
 // f32 -> hi/lo f16 planes (lo plane `plane` elements after hi)
 int launch_split_planes(const float* x, __half* y, size_t n, size_t plane, cudaStream_t st);
 bool qgemv_b_fast_ok(int type, int K, int N, int pitch, const void* W);
+// Q4_K / Q6_K: run from the tiled copy only (N % 256 == 0, K % 16 == 0)
+bool kquant_type(int type);
+int kquant_block_bytes(int type);  // GGUF bytes of one 256-value super-block
 bool qgemv_a_fast_ok(int type, int K, int N, int pitch, const void* W);
 // picks csplit / kchunk for a launch (fills the GPU)
 void qgemv_plan(GemvArgs& a, int layout, int num_sms);

@@ -6,6 +6,7 @@
 //   Q4_0: d = v_absmax / -8, q = clamp(trunc(x/d + 8.5), 0, 15)
 //   Q4_1: d = (max - min) / 15, m = min, q = clamp(trunc((x - m)/d + 0.5), 0, 15)
 //   Q8_0: d = absmax / 127, q = round(x / d)
+// (K-quant encoders below, for the reference's own reading of those blocks)
 // with d (and m) stored as IEEE f16.  The file layout follows the GGUF v3
 // container that woolly-gguf reads (and its MockGGUFBuilder writes,
 // woolly-gguf/tests/load_model.rs:51-144), with every tensor offset aligned
@@ -88,7 +89,118 @@ static void quant_q8_0(const float* x, uint8_t* b) {
   for (int j = 0; j < 32; j++) b[2 + j] = (uint8_t)(int8_t)roundf(x[j] * id);
 }
 
+static float f16_to_f32(uint16_t h) {
+  const uint32_t sign = (uint32_t)(h & 0x8000u) << 16, e = (h >> 10) & 31u, man = h & 1023u;
+  float v;
+  if (e == 0) {
+    v = (float)man * (1.0f / 16777216.0f);  // subnormal: man * 2^-24 (exact)
+  } else if (e == 31) {
+    uint32_t x = 0x7F800000u | (man << 13);
+    memcpy(&v, &x, 4);
+  } else {
+    uint32_t x = ((e + 112u) << 23) | (man << 13);
+    memcpy(&v, &x, 4);
+  }
+  uint32_t x;
+  memcpy(&x, &v, 4);
+  x |= sign;
+  memcpy(&v, &x, 4);
+  return v;
+}
+
+// K-quant encoders for the values woolly_gguf::dequantize reads back
+// (dequantize.rs:381-537), 256 values per super-block:
+//   Q4_K: w = d*sc[j]*q + dmin (dmin added as stored), so dmin = the block
+//     minimum, d*sc[j]*15 spans sub-block j's range above it, q = round((x -
+//     dmin)/(d*sc[j])); sc[j] six bits at the reference's bit positions.
+//   Q6_K: w = d*sc[j]*(q - 32)/64 with unsigned sc per 16 values, d*sc[j]/64
+//     = absmax_j/31, q = round(x/step) + 32 written to the ql/qh bits the
+//     reference reads (values whose bits it reads from one place share them).
+static void quant_q4_k(const float* x, uint8_t* b) {
+  memset(b, 0, 144);
+  float mn = x[0];
+  for (int i = 1; i < 256; i++) mn = x[i] < mn ? x[i] : mn;
+  const uint16_t hm = f32_to_f16(mn);
+  const float dmin = f16_to_f32(hm);
+  float rng[8], rmax = 0.0f;
+  for (int j = 0; j < 8; j++) {
+    float mx = x[32 * j];
+    for (int i = 1; i < 32; i++) mx = x[32 * j + i] > mx ? x[32 * j + i] : mx;
+    rng[j] = mx - dmin > 0.0f ? mx - dmin : 0.0f;
+    rmax = rng[j] > rmax ? rng[j] : rmax;
+  }
+  const uint16_t hd = f32_to_f16(rmax / 945.0f);
+  const float d = f16_to_f32(hd);
+  put16(b + 12, hd);
+  put16(b + 14, hm);
+  for (int j = 0; j < 8; j++) {
+    int sc = d > 0.0f ? (int)(rng[j] / (15.0f * d) + 0.5f) : 0;
+    sc = sc > 63 ? 63 : sc;
+    const int src = (j * 3) / 2;
+    if (j % 2 == 0) {
+      b[src] = (uint8_t)(b[src] | sc);
+    } else {
+      b[src] = (uint8_t)(b[src] | ((sc & 3) << 6));
+      b[src + 1] = (uint8_t)(b[src + 1] | (sc >> 2));
+    }
+    const float step = d * (float)sc, inv = step > 0.0f ? 1.0f / step : 0.0f;
+    for (int i = 32 * j; i < 32 * j + 32; i++) {
+      int q = (int)((x[i] - dmin) * inv + 0.5f);
+      q = q < 0 ? 0 : q > 15 ? 15 : q;
+      b[16 + i / 2] = (uint8_t)(b[16 + i / 2] | (i % 2 == 0 ? q : q << 4));
+    }
+  }
+}
+
+static void set_bits(uint8_t* p, int shift, int width, int v) {
+  const int mask = ((1 << width) - 1) << shift;
+  *p = (uint8_t)((*p & ~mask) | ((v << shift) & mask));
+}
+
+static void quant_q6_k(const float* x, uint8_t* b) {
+  memset(b, 0, 210);
+  float am[16], m = 0.0f;
+  for (int j = 0; j < 16; j++) {
+    am[j] = 0.0f;
+    for (int i = 16 * j; i < 16 * j + 16; i++) am[j] = fabsf(x[i]) > am[j] ? fabsf(x[i]) : am[j];
+    m = am[j] > m ? am[j] : m;
+  }
+  const uint16_t hd = f32_to_f16(m * 64.0f / (31.0f * 255.0f));
+  const float d = f16_to_f32(hd);
+  put16(b + 208, hd);
+  uint8_t *ql = b, *qh = b + 128;
+  for (int j = 0; j < 16; j++) {
+    int sc = d > 0.0f ? (int)(am[j] * 64.0f / (31.0f * d) + 0.5f) : 0;
+    sc = sc > 255 ? 255 : sc;
+    b[192 + j] = (uint8_t)sc;
+    const float step = d * (float)sc / 64.0f, inv = step > 0.0f ? 1.0f / step : 0.0f;
+    for (int i = 16 * j; i < 16 * j + 16; i++) {
+      int q = (int)(x[i] * inv + 32.5f);
+      q = q < 0 ? 0 : q > 63 ? 63 : q;
+      const int ql_idx = 64 * (i / 128) + 32 * ((i % 128) / 64) + 16 * ((i % 64) / 32) + (i % 16);
+      const int qh_idx = 32 * (i / 128) + 16 * ((i % 128) / 64) + 8 * ((i % 64) / 32) + (i % 32) / 4;
+      const int sh = 2 * ((i % 32) % 4);
+      if (i < 128) {
+        set_bits(ql + ql_idx, 0, 4, q & 15);
+        set_bits(qh + qh_idx, sh, 2, q >> 4);
+      } else {
+        set_bits(ql + ql_idx, 4, 4, q & 15);
+        if (sh < 6)
+          set_bits(qh + qh_idx, sh + 2, 2, q >> 4);
+        else if (qh_idx + 1 < 64)
+          set_bits(qh + qh_idx + 1, 0, 2, q >> 4);
+      }
+    }
+  }
+}
+
 static int quantize_blocks(uint32_t type, const float* src, size_t n, uint8_t* dst) {
+  if (type == WL_Q4_K || type == WL_Q6_K) {
+    const size_t ts = type_size(type);
+    for (size_t i = 0; i < n / 256; i++)
+      (type == WL_Q4_K ? quant_q4_k : quant_q6_k)(src + 256 * i, dst + ts * i);
+    return WL_OK;
+  }
   size_t nb = n / 32, ts = type_size(type);
   for (size_t i = 0; i < nb; i++) {
     if (type == WL_Q4_0)
@@ -188,7 +300,7 @@ struct TSpec {
   uint64_t nelems() const { return d1 ? d0 * d1 : d0; }
   uint64_t nbytes() const {
     uint64_t n = nelems();
-    return type_quantized(type) ? n / 32 * type_size(type) : n * type_size(type);
+    return type_quantized(type) ? n / type_block_size(type) * type_size(type) : n * type_size(type);
   }
 };
 
@@ -197,12 +309,19 @@ int synth_gguf(const char* path, const wl_synth_config* c) {
   if (!c->hidden || !c->layers || !c->heads || !c->kv_heads || !c->ff || !c->vocab ||
       c->hidden % c->heads || c->heads % c->kv_heads)
     return fail(WL_ERR_INVALID_ARGUMENT, "synth_gguf: inconsistent shape");
-  uint32_t wt = c->weight_type;
-  if (!(wt == WL_Q4_0 || wt == WL_Q4_1 || wt == WL_Q8_0 || wt == WL_F32))
-    return fail(WL_ERR_UNSUPPORTED, "synth_gguf: weight type must be F32/Q4_0/Q4_1/Q8_0");
+  auto ok_type = [](uint32_t t) {
+    return t == WL_Q4_0 || t == WL_Q4_1 || t == WL_Q8_0 || t == WL_Q4_K || t == WL_Q6_K || t == WL_F32;
+  };
+  uint32_t wt = c->weight_type, vt = c->vd_type ? c->vd_type : wt;
+  if (!ok_type(wt) || !ok_type(vt))
+    return fail(WL_ERR_UNSUPPORTED, "synth_gguf: weight type must be F32/Q4_0/Q4_1/Q8_0/Q4_K/Q6_K");
   uint64_t d = c->hidden, hd = d / c->heads, kvd = hd * c->kv_heads, ff = c->ff, V = c->vocab;
-  if (wt != WL_F32 && (d % 32 || kvd % 32 || ff % 32 || V % 32))
-    return fail(WL_ERR_INVALID_ARGUMENT, "synth_gguf: quantized dims must be multiples of 32");
+  // quantization blocks run along the output columns (the second dim)
+  auto blk = [](uint32_t t) -> uint64_t { return t == WL_F32 ? 1 : type_block_size(t); };
+  if (d % blk(wt) || kvd % blk(wt) || ff % blk(wt) || d % blk(vt) || kvd % blk(vt) ||
+      (c->output_type != 0xFFFFFFFFu && ok_type(c->output_type) && V % blk(c->output_type)))
+    return fail(WL_ERR_INVALID_ARGUMENT,
+                "synth_gguf: quantized output dims must be multiples of the block size (32; 256 for K-quants)");
   std::vector<TSpec> ts;
   ts.push_back({"token_embd.weight", d, V, WL_F32, 1});
   for (uint32_t l = 0; l < c->layers; l++) {
@@ -210,18 +329,18 @@ int synth_gguf(const char* path, const wl_synth_config* c) {
     ts.push_back({p + "attn_norm.weight", d, 0, WL_F32, 2});
     ts.push_back({p + "attn_q.weight", d, d, wt, 0});
     ts.push_back({p + "attn_k.weight", d, kvd, wt, 0});
-    ts.push_back({p + "attn_v.weight", d, kvd, wt, 0});
+    ts.push_back({p + "attn_v.weight", d, kvd, vt, 0});
     ts.push_back({p + "attn_output.weight", d, d, wt, 0});
     ts.push_back({p + "ffn_norm.weight", d, 0, WL_F32, 2});
     ts.push_back({p + "ffn_gate.weight", d, ff, wt, 0});
     ts.push_back({p + "ffn_up.weight", d, ff, wt, 0});
-    ts.push_back({p + "ffn_down.weight", ff, d, wt, 0});
+    ts.push_back({p + "ffn_down.weight", ff, d, vt, 0});
   }
   ts.push_back({"output_norm.weight", d, 0, WL_F32, 2});
   if (c->output_type != 0xFFFFFFFFu) {
     uint32_t ot = c->output_type;
-    if (!(ot == WL_Q4_0 || ot == WL_Q4_1 || ot == WL_Q8_0 || ot == WL_F32))
-      return fail(WL_ERR_UNSUPPORTED, "synth_gguf: output type must be F32/Q4_0/Q4_1/Q8_0");
+    if (!ok_type(ot))
+      return fail(WL_ERR_UNSUPPORTED, "synth_gguf: output type must be F32/Q4_0/Q4_1/Q8_0/Q4_K/Q6_K");
     ts.push_back({"output.weight", d, V, ot, 0});
   }
   FILE* f = fopen(path, "wb");
@@ -273,7 +392,8 @@ int synth_gguf(const char* path, const wl_synth_config* c) {
       int err = WL_OK;
       parallel_chunks(nch, [&](size_t ch) {
         size_t o = ch * kChunk, k = n - o < kChunk ? (size_t)(n - o) : kChunk;
-        int s = quantize_blocks(t.type, buf.data() + o, k, q.data() + o / 32 * type_size(t.type));
+        int s = quantize_blocks(t.type, buf.data() + o, k,
+                                q.data() + o / type_block_size(t.type) * type_size(t.type));
         if (s) err = s;
       });
       if (err) {
@@ -301,6 +421,8 @@ extern "C" int wl_synth_gguf(const char* path, const wl_synth_config* cfg) {
 
 extern "C" int wl_quantize(int type, const float* src, size_t n, void* dst) {
   if (!src || !dst || n % 32) return wl::fail(WL_ERR_INVALID_ARGUMENT, "wl_quantize: n % 32 != 0");
+  if ((type == WL_Q4_K || type == WL_Q6_K) && n % 256)
+    return wl::fail(WL_ERR_INVALID_ARGUMENT, "wl_quantize: K-quants need n % 256 == 0");
   int s = wl::quantize_blocks((uint32_t)type, src, n, (uint8_t*)dst);
   if (s) return wl::fail(s, "wl_quantize: unsupported type " + std::to_string(type));
   return WL_OK;

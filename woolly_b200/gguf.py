@@ -188,13 +188,16 @@ def config_dict(c: _lib.ModelConfig) -> dict:
 def write_synthetic(path: str, *, hidden: int, layers: int, heads: int, kv_heads: int, ff: int,
                     vocab: int, weight_type: int = _lib.Q4_0, output_type: int | None = None,
                     tied: bool = False, context_length: int = 4096, sliding_window: int = 0,
-                    rope_theta: float = 10000.0, norm_eps: float = 1e-5, seed: int = 0) -> str:
-    """Writes the seeded LLaMA-shape GGUF used by the tests and benchmarks."""
+                    rope_theta: float = 10000.0, norm_eps: float = 1e-5, seed: int = 0,
+                    vd_type: int = 0) -> str:
+    """Writes the seeded LLaMA-shape GGUF used by the tests and benchmarks.
+    vd_type (0 = weight_type) is the type of attn_v and ffn_down, as the
+    K-quant mixes store them (Q6_K beside Q4_K)."""
     cfg = _lib.SynthConfig(hidden, layers, heads, kv_heads, ff, vocab, context_length,
                            weight_type,
                            0xFFFFFFFF if tied else (weight_type if output_type is None
                                                     else output_type),
-                           sliding_window, rope_theta, norm_eps, seed)
+                           sliding_window, rope_theta, norm_eps, seed, vd_type)
     check(lib().wl_synth_gguf(str(path).encode(), C.byref(cfg)))
     return str(path)
 
@@ -202,7 +205,7 @@ def write_synthetic(path: str, *, hidden: int, layers: int, heads: int, kv_heads
 def quantize(ggml_type: int, values: np.ndarray) -> np.ndarray:
     """Encodes f32 values (len % 32 == 0) into GGUF blocks."""
     v = np.ascontiguousarray(values, dtype=np.float32).ravel()
-    nb = v.size // 32 * int(lib().wl_type_size(ggml_type))
+    nb = v.size // int(lib().wl_block_size(ggml_type)) * int(lib().wl_type_size(ggml_type))
     out = np.zeros(nb, dtype=np.uint8)
     check(lib().wl_quantize(ggml_type, v.ctypes.data, v.size, out.ctypes.data))
     return out
