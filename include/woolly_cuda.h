@@ -195,7 +195,7 @@ int wl_qgemv_tiled(int ggml_type, const void* W_tiled, int K, int N, const void*
  * on the tcgen05 tensor cores, with the weights given as their tiled copy
  * (the copy the model runtime keeps) and the M activation rows as f16 hi/lo
  * planes (hi plane [M][K], lo plane x_plane elements later): needs
- * K % 64 == 0, N % 128 == 0. */
+ * K % 64 == 0, N % 128 == 0 (Q4_K / Q6_K: N % 256 == 0). */
 int wl_qgemm_tiled(int ggml_type, const void* W_tiled, int K, int N, const void* x_planes,
                    size_t x_plane, int M, float* y, void* stream);
 

@@ -365,14 +365,16 @@ int wl_qgemv_tiled(int type, const void* Wt, int K, int N, const void* xp, size_
 int wl_qgemm_tiled(int type, const void* Wt, int K, int N, const void* xp, size_t x_plane, int M,
                    float* y, void* stream) {
   if (!Wt || !xp || !y || M <= 0) return fail(WL_ERR_INVALID_ARGUMENT, "bad argument");
-  if (!bb(type)) return fail(WL_ERR_UNSUPPORTED, "qgemm: type must be Q4_0, Q4_1 or Q8_0");
+  const bool kq = kquant_type(type);
+  if (!bb(type) && !kq) return fail(WL_ERR_UNSUPPORTED, "qgemm: type must be Q4_0, Q4_1, Q8_0, Q4_K or Q6_K");
+  if (kq && N % 256) return fail(WL_ERR_INVALID_ARGUMENT, "qgemm_tiled: K-quants need N % 256 == 0");
   GemvArgs a;
   a.type = type;
   a.nseg = 1;
   a.tiled = 1;
   a.seg[0].W = (const uint8_t*)Wt;
   a.seg[0].N = N;
-  a.seg[0].pitch = N / 32 * bb(type);
+  a.seg[0].pitch = kq ? N / 256 * kquant_block_bytes(type) : N / 32 * bb(type);
   a.K = K;
   a.ldx = K;
   a.xkind = X_PLANES;
@@ -389,11 +391,13 @@ int wl_qgemm_tiled(int type, const void* Wt, int K, int N, const void* xp, size_
 // when the shape allows, else the GEMV in 32-row launches.
 int wl_qgemm(int type, const void* W, int K, int N, const float* x, int M, float* y, void* stream) {
   if (!W || !x || !y) return fail(WL_ERR_INVALID_ARGUMENT, "null pointer");
-  if (!bb(type)) return fail(WL_ERR_UNSUPPORTED, "qgemm: type must be Q4_0, Q4_1 or Q8_0");
-  if (K <= 0 || N <= 0 || M <= 0 || N % 32) return fail(WL_ERR_INVALID_ARGUMENT, "qgemm: bad shape");
+  const bool kq = kquant_type(type);
+  if (!bb(type) && !kq) return fail(WL_ERR_UNSUPPORTED, "qgemm: type must be Q4_0, Q4_1, Q8_0, Q4_K or Q6_K");
+  if (K <= 0 || N <= 0 || M <= 0 || N % (kq ? 256 : 32) || (kq && K % 16))
+    return fail(WL_ERR_INVALID_ARGUMENT, "qgemm: bad shape");
   cudaStream_t st = (cudaStream_t)stream;
-  const int pitch = N / 32 * bb(type);
-  const bool aligned = pitch % 16 == 0 && (reinterpret_cast<uintptr_t>(W) & 15) == 0;
+  const int pitch = kq ? N / 256 * kquant_block_bytes(type) : N / 32 * bb(type);
+  const bool aligned = kq || (pitch % 16 == 0 && (reinterpret_cast<uintptr_t>(W) & 15) == 0);
   if (!aligned || K % 16) return qgemv_op(type, WL_LAYOUT_B, (const uint8_t*)W, K, N, x, M, y, st);
   GemvArgs a;
   a.type = type;
@@ -413,17 +417,21 @@ int wl_qgemm(int type, const void* W, int K, int N, const float* x, int M, float
   WL_CUDA_TRY(cudaMallocAsync((void**)&planes, (size_t)2 * M * K * sizeof(__half), st));
   int s = launch_split_planes(x, planes, (size_t)M * K, (size_t)M * K, st);
   a.x = planes;
-  GemvArgs t = a;  // the tensor-core GEMM reads the tiled copy, made here in a temporary
-  t.tiled = 1;
-  if (!s && K % 64 == 0 && N % 128 == 0) {
-    uint8_t* tiled = nullptr;
+  // the tensor-core GEMM (and any K-quant GEMV) reads the tiled copy, made here in a temporary
+  const bool gemm = K % 64 == 0 && N % 128 == 0;
+  uint8_t* tiled = nullptr;
+  if (!s && (gemm || kq)) {
     s = cudaMallocAsync((void**)&tiled, qtile_bytes(type, K, N), st) == cudaSuccess
             ? WL_OK : fail(WL_ERR_OUT_OF_MEMORY, "qgemm: tiled copy");
     if (!s) s = launch_repack_tiled(type, (const uint8_t*)W, K, N, pitch, tiled, st);
-    t.seg[0].W = tiled;
-    if (!s && qgemm_b_ok(t, M)) s = launch_qgemm_b(t, M, st);
-    else if (!s) s = fail(WL_ERR_UNSUPPORTED, "qgemm: shape");
-    if (tiled) cudaFreeAsync(tiled, st);
+    if (!s) {
+      a.seg[0].W = tiled;
+      a.tiled = 1;
+    }
+  }
+  if (!s && gemm) {
+    if (qgemm_b_ok(a, M)) s = launch_qgemm_b(a, M, st);
+    else s = fail(WL_ERR_UNSUPPORTED, "qgemm: shape");
   } else {
     for (int r0 = 0; r0 < M && !s; r0 += 32) {
       a.B = std::min(32, M - r0);
@@ -433,6 +441,7 @@ int wl_qgemm(int type, const void* W, int K, int N, const float* x, int M, float
       s = launch_qgemv_b(a, st);
     }
   }
+  if (tiled) cudaFreeAsync(tiled, st);
   cudaFreeAsync(planes, st);
   return s;
 }

@@ -119,12 +119,18 @@ __device__ __forceinline__ void split_pair(uint32_t q, __half2 d2, uint32_t& hi,
 // qtile_bytes): the codes of its 8 (k step, block) units in the lanes'
 // fragment order, then its f16 scales (4 per lane quad and unit), then Q4_1's
 // mins in the same order.
+// K-quants (the tiled copy of k_repack_tiled_k): Q4_K scales are (hi, lo)
+// f16 pairs of d*sc (16 bytes per lane quad and unit) followed by dmin as
+// Q4_1's mins; Q6_K codes are (q - 32) bytes as Q8_0's, with one (hi, lo)
+// scale pair per 16 columns (32 bytes per lane quad and unit).
 template <int T>
 struct Quarter {
-  static constexpr int CB = T == WL_Q8_0 ? 16 : 8;  // code bytes per lane per unit
-  static constexpr int CODES = 8 * 32 * CB;         // 2048 (Q8_0: 4096)
-  static constexpr int SCALES = 8 * 4 * 8;          // 256
-  static constexpr int MINS = T == WL_Q4_1 ? 256 : 0;
+  static constexpr bool B8 = T == WL_Q8_0 || T == WL_Q6_K;
+  static constexpr int CB = B8 ? 16 : 8;     // code bytes per lane per unit
+  static constexpr int CODES = 8 * 32 * CB;  // 2048 (8-bit codes: 4096)
+  static constexpr int SCALES = 8 * 4 * (T == WL_Q6_K ? 32 : T == WL_Q4_K ? 16 : 8);
+  static constexpr int MINS = (T == WL_Q4_1 || T == WL_Q4_K) ? 256 : 0;
+  static constexpr int UNIT = T == WL_Q4_0 ? 18 : T == WL_Q4_1 ? 20 : T == WL_Q8_0 ? 34 : T == WL_Q4_K ? 22 : 40;
 };
 // one stage's raw bytes for a 128-column tile: [codes q0][codes q1][scales q0][scales q1][mins q0][mins q1]
 template <int T>
@@ -144,10 +150,25 @@ __device__ __forceinline__ void dequant_frag(const uint8_t* raw, uint8_t* whi, u
   const int qd = tid >> 8, rem = tid & 255, ul = rem >> 5, lane = rem & 31;
   const int g = lane >> 2, t = lane & 3, ks = ul >> 1, blk = ul & 1;
   const uint8_t* codes = raw + qd * Qt::CODES + ul * 32 * Qt::CB + lane * Qt::CB;
-  const uint2 sw = *reinterpret_cast<const uint2*>(raw + 2 * Qt::CODES + qd * Qt::SCALES + (ul * 4 + t) * 8);
-  const uint32_t dpair[2] = {sw.x, sw.y};  // (d(2t), d(2t+1)), (d(2t+8), d(2t+9))
+  // (d(2t), d(2t+1)), (d(2t+8), d(2t+9)); K-quants also the lo halves, Q6_K per m-tile
+  uint32_t dpair[2][2], epair[2][2] = {{0u, 0u}, {0u, 0u}};
+  if constexpr (T == WL_Q6_K) {
+#pragma unroll
+    for (int mt = 0; mt < 2; mt++) {
+      const uint4 sw = *reinterpret_cast<const uint4*>(raw + 2 * Qt::CODES + qd * Qt::SCALES +
+                                                       ((ul * 2 + mt) * 4 + t) * 16);
+      dpair[mt][0] = sw.x, dpair[mt][1] = sw.y, epair[mt][0] = sw.z, epair[mt][1] = sw.w;
+    }
+  } else if constexpr (T == WL_Q4_K) {
+    const uint4 sw = *reinterpret_cast<const uint4*>(raw + 2 * Qt::CODES + qd * Qt::SCALES + (ul * 4 + t) * 16);
+    dpair[0][0] = dpair[1][0] = sw.x, dpair[0][1] = dpair[1][1] = sw.y;
+    epair[0][0] = epair[1][0] = sw.z, epair[0][1] = epair[1][1] = sw.w;
+  } else {
+    const uint2 sw = *reinterpret_cast<const uint2*>(raw + 2 * Qt::CODES + qd * Qt::SCALES + (ul * 4 + t) * 8);
+    dpair[0][0] = dpair[1][0] = sw.x, dpair[0][1] = dpair[1][1] = sw.y;
+  }
   uint32_t mpair[2] = {0u, 0u};
-  if constexpr (T == WL_Q4_1) {
+  if constexpr (Qt::MINS) {
     const uint2 mw = *reinterpret_cast<const uint2*>(raw + 2 * (Qt::CODES + Qt::SCALES) + qd * Qt::MINS +
                                                      (ul * 4 + t) * 8);
     mpair[0] = mw.x, mpair[1] = mw.y;
@@ -155,7 +176,7 @@ __device__ __forceinline__ void dequant_frag(const uint8_t* raw, uint8_t* whi, u
   // q pairs: qp[h][j] = codes of column os[j] at k rows (2t + 8h, +1)
   const int os[4] = {g, 16 + g, g + 8, 24 + g};
   uint32_t qp[2][4];
-  if constexpr (T == WL_Q8_0) {
+  if constexpr (Qt::B8) {
     const uint4 c = *reinterpret_cast<const uint4*>(codes);
     const uint32_t w[4] = {c.x, c.y, c.z, c.w};
     // byte (mt*4 + r)*2 + e: column mt*16 + g + 8(r&1), k rows 2t + 8(r>>1) + e
@@ -187,16 +208,24 @@ __device__ __forceinline__ void dequant_frag(const uint8_t* raw, uint8_t* whi, u
 #pragma unroll
     for (int j = 0; j < 4; j++) {
       uint32_t hi, lo;
-      if constexpr (T == WL_Q4_1) {  // q*d + m (dequantize_q4_1, dequantize.rs:372), rounded once to hi
+      const int mt = j & 1;  // os[j] = g, 16+g, g+8, 24+g: m-tile 0, 1, 0, 1
+      if constexpr (T == WL_Q4_1 || T == WL_Q4_K || T == WL_Q6_K) {
+        // in f32, rounded once to hi: Q4_1 q*d + m (dequantize_q4_1, dequantize.rs:372);
+        // Q4_K q*(d*sc) + dmin (:404-462); Q6_K (q-32)*(d*sc)/64 (:465-537)
         const float2 qf = __half22float2(u2h(qp[h][j]));
-        const float2 df = __half22float2(u2h(dpair[h]));
+        float2 df = __half22float2(u2h(dpair[mt][h]));
+        if constexpr (T != WL_Q4_1) {
+          const float2 ef = __half22float2(u2h(epair[mt][h]));
+          df.x += ef.x, df.y += ef.y;  // exact: the pair splits d*sc
+        }
         const float2 mf = __half22float2(u2h(mpair[h]));
-        const float v0 = qf.x * df.x + mf.x, v1 = qf.y * df.y + mf.y;
+        float v0 = qf.x * df.x + mf.x, v1 = qf.y * df.y + mf.y;
+        if constexpr (T == WL_Q6_K) v0 *= 0.015625f, v1 *= 0.015625f;
         const __half h0 = __float2half_rn(v0), h1 = __float2half_rn(v1);
         hi = h2u(__halves2half2(h0, h1));
         lo = h2u(__halves2half2(__float2half_rn(v0 - __half2float(h0)), __float2half_rn(v1 - __half2float(h1))));
       } else {
-        split_pair(qp[h][j], u2h(dpair[h]), hi, lo);
+        split_pair(qp[h][j], u2h(dpair[0][h]), hi, lo);
       }
       const int row = qd * 64 + blk * 32 + os[j];
       const uint32_t off = (uint32_t)((row << 7) + ((c8 ^ (row & 7)) << 4) + 4 * t);
@@ -220,8 +249,8 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&v)[16]) {
 template <int T>
 __global__ void __launch_bounds__(kGThreads, 1) k_qgemm_b(const GemvArgs a, int M) {
   using Qt = Quarter<T>;
-  constexpr int S = T == WL_Q4_0 ? 18 : T == WL_Q4_1 ? 20 : 34;
-  constexpr int STB = 512 * S;  // bytes of one (256-column group, 64-row stage) block of the tiled copy
+  static_assert(raw_stage_bytes<T>() <= kGRaw, "raw stage slot too small");
+  constexpr int STB = 512 * Qt::UNIT;  // bytes of one (256-column group, 64-row stage) block of the tiled copy
   extern __shared__ uint8_t gsm_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(gsm_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* rawb = sm + kGStages * kGStage;  // [kGStages][kGRaw] bulk-copied weight bytes
@@ -285,7 +314,7 @@ __global__ void __launch_bounds__(kGThreads, 1) k_qgemm_b(const GemvArgs a, int 
       const int qw = q ? qw1 : qw0;
       const uint8_t* blk = qsrc[q] + (size_t)it * STB;
       const uint8_t* parts[3] = {blk + qw * Qt::CODES, blk + 32 * 32 * Qt::CB + qw * Qt::SCALES,
-                                 blk + 32 * 32 * Qt::CB + 1024 + qw * 256};
+                                 blk + 32 * 32 * Qt::CB + 4 * Qt::SCALES + qw * 256};
       const uint32_t dsts[3] = {dst + q * Qt::CODES, dst + 2 * Qt::CODES + q * Qt::SCALES,
                                 dst + 2 * (Qt::CODES + Qt::SCALES) + q * Qt::MINS};
       const uint32_t sizes[3] = {(uint32_t)Qt::CODES, (uint32_t)Qt::SCALES, (uint32_t)Qt::MINS};
@@ -462,7 +491,8 @@ int launch_t(const GemvArgs& a, int M, int ntiles, cudaStream_t st) {
 
 bool qgemm_b_ok(const GemvArgs& a, int M) {
   if (M < 1 || a.K <= 0 || a.K % kGK || !a.tiled) return false;
-  if (!(a.type == WL_Q4_0 || a.type == WL_Q4_1 || a.type == WL_Q8_0)) return false;
+  if (!(a.type == WL_Q4_0 || a.type == WL_Q4_1 || a.type == WL_Q8_0 || a.type == WL_Q4_K || a.type == WL_Q6_K))
+    return false;
   if (a.xkind != X_PLANES || a.ldx % 8 || a.x_plane % 8 || (reinterpret_cast<uintptr_t>(a.x) & 15))
     return false;
   if (a.epi.kind == EPI_QKV && a.epi.rope) return false;
@@ -484,6 +514,8 @@ int launch_qgemm_b(const GemvArgs& a, int M, cudaStream_t st) {
     case WL_Q4_0: return launch_t<WL_Q4_0>(a, M, ntiles, st);
     case WL_Q4_1: return launch_t<WL_Q4_1>(a, M, ntiles, st);
     case WL_Q8_0: return launch_t<WL_Q8_0>(a, M, ntiles, st);
+    case WL_Q4_K: return launch_t<WL_Q4_K>(a, M, ntiles, st);
+    case WL_Q6_K: return launch_t<WL_Q6_K>(a, M, ntiles, st);
   }
   return fail(WL_ERR_UNSUPPORTED, "qgemm: unsupported type");
 }
