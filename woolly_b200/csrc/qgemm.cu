@@ -39,11 +39,13 @@ constexpr int kGN = 128;  // weight columns per CTA (MMA M)
 constexpr int kGM = 128;  // token rows per CTA (MMA N)
 constexpr int kGK = 64;   // k rows per stage (one 128-byte swizzle row of f16)
 constexpr int kGStages = 3;
-constexpr int kGThreads = 512;  // 16 warps: two per quant block of each k row
+constexpr int kGDeq = 512;                // dequantizing threads: 16 warps, two per quant block of each k row
+constexpr int kGThreads = kGDeq + 32;     // + one control warp (bulk copies, MMA issue)
+constexpr int kGCtl = kGDeq / 32;         // the control warp
 constexpr int kGTile = 128 * kGK * 2;  // bytes of one f16 operand tile (16 KB)
 constexpr int kGStage = 4 * kGTile;    // W hi, W lo, X hi, X lo
 constexpr int kGRaw = 10240;  // per-stage raw weight bytes (largest: Q8_0 9216)
-constexpr int kGSmem = kGStages * (kGStage + kGRaw) + 1024 + 64;  // + alignment slack + barriers
+constexpr int kGSmem = kGStages * (kGStage + kGRaw) + 1024 + 128;  // + alignment slack + barriers
 constexpr int kTmemCols = kGM;                          // f32 accumulator columns (token rows)
 
 __device__ __forceinline__ uint32_t smem_addr(const void* p) {
@@ -256,7 +258,8 @@ __global__ void __launch_bounds__(kGThreads, 1) k_qgemm_b(const GemvArgs a, int 
   uint8_t* rawb = sm + kGStages * kGStage;  // [kGStages][kGRaw] bulk-copied weight bytes
   uint64_t* bars = reinterpret_cast<uint64_t*>(rawb + kGStages * kGRaw);  // MMA done, per slot
   uint64_t* wbars = bars + kGStages;                                       // raw bytes landed, per slot
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(wbars + kGStages);
+  uint64_t* fbars = wbars + kGStages;  // slot dequantized and its activations landed (16 warp arrivals)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(fbars + kGStages);
   __shared__ int s_fail, s_issued;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -293,6 +296,9 @@ __global__ void __launch_bounds__(kGThreads, 1) k_qgemm_b(const GemvArgs a, int 
   if (tid == 0) {
     for (int s = 0; s < 2 * kGStages; s++)
       asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;\n" ::"r"(smem_addr(bars + s)) : "memory");
+    for (int s = 0; s < kGStages; s++)
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(smem_addr(fbars + s)), "r"(kGDeq / 32)
+                   : "memory");
     asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
     s_fail = 0;
     s_issued = 0;
@@ -327,90 +333,105 @@ __global__ void __launch_bounds__(kGThreads, 1) k_qgemm_b(const GemvArgs a, int 
               : "memory");
     }
   };
-  // the weights do not depend on earlier kernels: start them before the PDL wait
-  if (tid == 0)
-    for (int it = 0; it < 2 && it < nk; it++) issue_w(it);
+  // Warp-specialised pipeline.  The control warp (lane 0) keeps the bulk
+  // weight copies three stages ahead, waits until the 16 dequantizing warps
+  // have filled a ring slot (fbars), issues its MMAs and commits them to the
+  // slot's `bars` barrier; the dequantizing warps wait on that barrier only
+  // before reusing the slot.  No CTA-wide barrier inside the K loop.
+  const bool ctl = warp == kGCtl;
+  if (ctl && lane == 0)  // the weights do not depend on earlier kernels: start them before the PDL wait
+    for (int it = 0; it < kGStages && it < nk; it++) issue_w(it);
   pdl_wait();
   pdl_trigger();
 
-  const __half* x = reinterpret_cast<const __half*>(a.x);
-  // activations of stage `it` into ring slot it % kGStages (K-major, 128B swizzle):
-  // this thread copies chunk c of rows rr0 + 32q (q < 4) of both planes; the
-  // swizzled destination and the source row offsets do not change per stage
-  const int xc = tid & 7, xr0 = tid >> 3;  // rows xr0, xr0 + 64
-  uint32_t xdst[4];
-  const __half* xsrc[4];
-  bool xok[4];
+  if (ctl) {
+    if (lane == 0) {
+      int issued = 0;
+      for (int it = 0; it < nk; it++) {
+        const int s = it % kGStages;
+        if (!gbar_wait(smem_addr(fbars + s), (uint32_t)((it / kGStages) & 1))) {
+          s_fail = 1;
+          break;
+        }
+        asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory");
+        const uint32_t wa = smem_addr(sm + s * kGStage), xa = wa + 2 * kGTile;
 #pragma unroll
-  for (int q = 0; q < 4; q++) {
-    const int pl = q >> 1, rr = xr0 + (q & 1) * 64;
-    xok[q] = m0 + rr < M;
-    xdst[q] = (uint32_t)((2 + pl) * kGTile + (rr << 7) + ((xc ^ (rr & 7)) << 4));
-    xsrc[q] = x + (size_t)pl * a.x_plane + (size_t)(xok[q] ? m0 + rr : 0) * a.ldx + xc * 8;
-  }
-  const uint32_t smb = smem_addr(sm);
-  auto load_x = [&](int it) {
-    const uint32_t st = smb + (uint32_t)((it % kGStages) * kGStage);
-    const int k0 = it * kGK;
+        for (int ks = 0; ks < kGK / 16; ks++) {
+          // A (weights) and B (activations) both K-major: 32 bytes per k step
+          // inside the 128-byte swizzle row; SBO = 1 KB (8 rows)
+          const uint64_t ah = desc_sw128(wa + ks * 32, 16, 1024);
+          const uint64_t al = desc_sw128(wa + kGTile + ks * 32, 16, 1024);
+          const uint64_t bh = desc_sw128(xa + ks * 32, 16, 1024);
+          const uint64_t bl = desc_sw128(xa + kGTile + ks * 32, 16, 1024);
+          umma_f16(tmem, ah, bh, (it > 0 || ks > 0) ? 1u : 0u);
+          umma_f16(tmem, al, bh, 1u);
+          umma_f16(tmem, ah, bl, 1u);
+        }
+        umma_commit(smem_addr(bars + s));
+        issued = it + 1;
+        // fbars[s] also says the raw slot s (stage it) has been read: refill it
+        if (it + kGStages < nk) {
+          asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+          issue_w(it + kGStages);
+        }
+      }
+      s_issued = issued;
+    }
+    __syncwarp();
+  } else {
+    const __half* x = reinterpret_cast<const __half*>(a.x);
+    // activations of stage `it` into ring slot it % kGStages (K-major, 128B swizzle):
+    // this thread copies chunk c of rows rr0 + 32q (q < 4) of both planes; the
+    // swizzled destination and the source row offsets do not change per stage
+    const int xc = tid & 7, xr0 = tid >> 3;  // rows xr0, xr0 + 64
+    uint32_t xdst[4];
+    const __half* xsrc[4];
+    bool xok[4];
 #pragma unroll
-    for (int q = 0; q < 4; q++) cp16(st + xdst[q], xsrc[q] + k0, xok[q]);
-    asm volatile("cp.async.commit_group;\n" ::: "memory");
-  };
-  // waits until the MMAs that last read ring slot (it % kGStages) are done (uniform result)
-  auto slot_free = [&](int it) -> bool {
-    if (it < kGStages) return true;
-    const bool w = gbar_wait(smem_addr(bars + it % kGStages), (uint32_t)((it / kGStages - 1) & 1));
-    const bool bad = __syncthreads_or(!w);
-    asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory");
-    return !bad;
-  };
-
-  load_x(0);
-  for (int it = 0; it < nk; it++) {
-    const int s = it % kGStages;
-    uint8_t* st = sm + s * kGStage;
-    const bool more = it + 1 < nk;
-    if (more) {
-      if (!slot_free(it + 1)) {  // uniform: every thread leaves together
-        if (tid == 0) s_fail = 1;
+    for (int q = 0; q < 4; q++) {
+      const int pl = q >> 1, rr = xr0 + (q & 1) * 64;
+      xok[q] = m0 + rr < M;
+      xdst[q] = (uint32_t)((2 + pl) * kGTile + (rr << 7) + ((xc ^ (rr & 7)) << 4));
+      xsrc[q] = x + (size_t)pl * a.x_plane + (size_t)(xok[q] ? m0 + rr : 0) * a.ldx + xc * 8;
+    }
+    const uint32_t smb = smem_addr(sm);
+    auto load_x = [&](int it) {
+      const uint32_t st = smb + (uint32_t)((it % kGStages) * kGStage);
+      const int k0 = it * kGK;
+#pragma unroll
+      for (int q = 0; q < 4; q++) cp16(st + xdst[q], xsrc[q] + k0, xok[q]);
+      asm volatile("cp.async.commit_group;\n" ::: "memory");
+    };
+    load_x(0);
+    for (int it = 0; it < nk; it++) {
+      const int s = it % kGStages;
+      uint8_t* st = sm + s * kGStage;
+      const bool more = it + 1 < nk;
+      if (more) {
+        // slot (it + 1) % kGStages last fed the MMAs of stage it + 1 - kGStages
+        const int nx = it + 1;
+        if (nx >= kGStages &&
+            !gbar_wait(smem_addr(bars + nx % kGStages), (uint32_t)((nx / kGStages - 1) & 1))) {
+          s_fail = 1;
+          break;
+        }
+        load_x(nx);
+      }
+      if (!gbar_wait(smem_addr(wbars + s), (uint32_t)((it / kGStages) & 1))) {
+        s_fail = 1;
         break;
       }
-      load_x(it + 1);
-    }
-    // raw slot (it + 2) % kGStages last held stage it - 1, dequantized before the
-    // previous iteration's barrier
-    if (tid == 0 && it + 2 < nk) {
+      dequant_frag<T>(rawb + s * kGRaw, st, st + kGTile, tid);
+      if (more)
+        asm volatile("cp.async.wait_group 1;\n" ::: "memory");
+      else
+        asm volatile("cp.async.wait_group 0;\n" ::: "memory");
       asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
-      issue_w(it + 2);
+      __syncwarp();
+      if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(smem_addr(fbars + s)) : "memory");
     }
-    if (!gbar_wait(smem_addr(wbars + s), (uint32_t)((it / kGStages) & 1))) s_fail = 1;
-    dequant_frag<T>(rawb + s * kGRaw, st, st + kGTile, tid);
-    if (more)
-      asm volatile("cp.async.wait_group 1;\n" ::: "memory");
-    else
-      asm volatile("cp.async.wait_group 0;\n" ::: "memory");
-    asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
-    __syncthreads();
-    if (tid == 0) {
-      asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory");
-      const uint32_t wa = smem_addr(st), xa = smem_addr(st + 2 * kGTile);
-#pragma unroll
-      for (int ks = 0; ks < kGK / 16; ks++) {
-        // A (weights) and B (activations) both K-major: 32 bytes per k step
-        // inside the 128-byte swizzle row; SBO = 1 KB (8 rows)
-        const uint64_t ah = desc_sw128(wa + ks * 32, 16, 1024);
-        const uint64_t al = desc_sw128(wa + kGTile + ks * 32, 16, 1024);
-        const uint64_t bh = desc_sw128(xa + ks * 32, 16, 1024);
-        const uint64_t bl = desc_sw128(xa + kGTile + ks * 32, 16, 1024);
-        umma_f16(tmem, ah, bh, (it > 0 || ks > 0) ? 1u : 0u);
-        umma_f16(tmem, al, bh, 1u);
-        umma_f16(tmem, ah, bl, 1u);
-      }
-      umma_commit(smem_addr(bars + s));
-      s_issued = it + 1;
-    }
+    asm volatile("cp.async.wait_group 0;\n" ::: "memory");
   }
-  asm volatile("cp.async.wait_group 0;\n" ::: "memory");
   // wait for the last issued commit (it covers every MMA issued before it); after
   // a failed wait this still drains the issued MMAs before TMEM is freed
   __syncthreads();
@@ -424,7 +445,8 @@ __global__ void __launch_bounds__(kGThreads, 1) k_qgemm_b(const GemvArgs a, int 
   }
   // bulk copies still in flight (after a failure) must land before the CTA exits
   if (tid == 0)
-    for (int it = n_issued; it < nk && it < n_issued + 2; it++) gbar_wait(smem_addr(wbars + it % kGStages), (uint32_t)((it / kGStages) & 1));
+    for (int it = n_issued; it < nk && it < n_issued + kGStages; it++)
+      gbar_wait(smem_addr(wbars + it % kGStages), (uint32_t)((it / kGStages) & 1));
   if (!ok && a.err && tid == 0) atomicOr(a.err, 16);
   asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory");
 
