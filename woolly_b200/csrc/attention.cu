@@ -20,6 +20,7 @@
 #include <cuda_fp16.h>
 
 #include <cmath>
+#include <cstring>
 #include <string>
 
 #include "common.h"
@@ -337,6 +338,259 @@ int launch_paged_hd(const AttnArgs& a, int G, float scale, cudaStream_t st) {
   return WL_OK;
 }
 
+// ---------------------------------------------------------------- prefill on tensor cores
+// Prompt rows of one session (consecutive positions; the model's prefill
+// chunks) on mma.sync m16n8k16, flash-attention style.  One CTA per (64
+// MMA rows, KV head): an MMA row is a (query row, head of the group) pair,
+// 16 per warp (16 / G query rows x G heads), so the CTA shares every K / V
+// block among its four warps and the G heads.  Keys stream in blocks of 64
+// (four pages) through a two-stage cp.async ring, stored with the 16-byte
+// chunks of each key row XOR-swizzled so that the ldmatrix reads of K (and the
+// transposed reads of V) are bank-conflict free; chunks of pages past the
+// last query position are zero-filled.  Exactness as elsewhere: q = qhi + qlo
+// and p = phi + plo as f16 pairs (~22 bits) against the f16 K / V cache, two
+// MMAs per product, f32 accumulation; the online softmax (max subtraction,
+// expf, rescale) runs in f32 on the accumulator fragments.  Scores are
+// (q.k) * hd^-1/2 with the causal bound and the optional window, as the
+// paged kernel applies them.
+constexpr int kPfThreads = 128;
+constexpr int kPfKeys = 64;
+
+__device__ __forceinline__ void pf_cp16(uint32_t dst, const void* src, bool ok) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(dst), "l"(src), "r"(ok ? 16 : 0)
+               : "memory");
+}
+__device__ __forceinline__ void pf_mma(float* c, const uint32_t* a, uint32_t b0, uint32_t b1) {
+  asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};\n"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ void pf_ldsm4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2,
+                                         uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+__device__ __forceinline__ void pf_ldsm4t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2,
+                                          uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+// (x0, x1) -> f16 pairs hi = f16(x), lo = f16(x - hi)
+__device__ __forceinline__ void pf_split(float x0, float x1, uint32_t& hi, uint32_t& lo) {
+  const __half h0 = __float2half_rn(x0), h1 = __float2half_rn(x1);
+  const __half2 h = __halves2half2(h0, h1);
+  const __half2 l = __halves2half2(__float2half_rn(x0 - __half2float(h0)), __float2half_rn(x1 - __half2float(h1)));
+  memcpy(&hi, &h, 4);
+  memcpy(&lo, &l, 4);
+}
+
+template <int HD, int G>
+__global__ void __launch_bounds__(kPfThreads) k_attn_prefill(const AttnArgs a, float scale) {
+  constexpr int QR = 16 / G;  // query rows per warp
+  constexpr int CR = 4 * QR;  // query rows per CTA
+  constexpr int KS = HD / 16;
+  constexpr int NT = HD / 8;
+  constexpr int CH = HD / 8;  // 16-byte chunks per key row
+  constexpr int BLK = kPfKeys * HD;  // halves of one K (or V) block
+  extern __shared__ __align__(128) __half pf_s[];  // [2 stages][K, V][64 keys][HD] swizzled
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int g = lane >> 2, t = lane & 3;
+  const int kvh = blockIdx.y, row0 = blockIdx.x * CR;
+  pdl_wait();
+  pdl_trigger();
+  if (row0 >= a.rows) return;
+  const int nrows = min(CR, a.rows - row0);
+  const int sess = a.row_sess[row0];
+  const int* table = a.kv.page_table + (size_t)sess * a.kv.max_pages;
+  const int pos_first = a.row_pos[row0], pos_last = a.row_pos[row0 + nrows - 1];
+  const int jlo = (a.window > 0 && pos_first - a.window + 1 > 0) ? pos_first - a.window + 1 : 0;
+  const int blo = jlo / kPfKeys, bhi = pos_last / kPfKeys;
+  const int last_page = pos_last / kPage;
+
+  // this lane's two MMA rows (g, g + 8): query row and head
+  int qrow[2], qpos[2], qhead[2];
+  bool qok[2];
+#pragma unroll
+  for (int h = 0; h < 2; h++) {
+    const int i = g + 8 * h;
+    qrow[h] = warp * QR + i / G;
+    qhead[h] = kvh * G + i % G;
+    qok[h] = qrow[h] < nrows;
+    qpos[h] = qok[h] ? a.row_pos[row0 + qrow[h]] : -1;
+  }
+  const int wpos_max = max(qpos[0], qpos[1]);  // per lane; the warp max below
+  int warp_max = wpos_max;
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) warp_max = max(warp_max, __shfl_xor_sync(0xffffffffu, warp_max, off));
+
+  // Q fragments (A operand, m16 x k16 per k step) as f16 hi / lo pairs
+  uint32_t qh[KS][4], ql[KS][4];
+#pragma unroll
+  for (int ks = 0; ks < KS; ks++)
+#pragma unroll
+    for (int r = 0; r < 4; r++) {
+      const int h = r & 1, d = ks * 16 + 2 * t + 8 * (r >> 1);
+      float x0 = 0.f, x1 = 0.f;
+      if (qok[h]) {
+        const float* qp = a.q + (size_t)(row0 + qrow[h]) * a.ldq + (size_t)qhead[h] * HD + d;
+        x0 = qp[0], x1 = qp[1];
+      }
+      pf_split(x0, x1, qh[ks][r], ql[ks][r]);
+    }
+
+  const uint32_t sbase = (uint32_t)__cvta_generic_to_shared(pf_s);
+  auto load_block = [&](int b, int stage) {
+    // 2 * 64 * CH chunks: K then V; chunk (key kk, c) lands at kk*CH + (c ^ (kk & 7))
+    for (int i = tid; i < 2 * kPfKeys * CH; i += kPfThreads) {
+      const int kv = i / (kPfKeys * CH), rem = i - kv * kPfKeys * CH;
+      const int kk = rem / CH, c = rem - kk * CH;
+      const int pgi = (b * kPfKeys + kk) / kPage;
+      const bool ok = pgi <= last_page;
+      const int pg = ok ? table[pgi] : 0;
+      const __half* src = (kv ? a.kv.v : a.kv.k) +
+                          (((size_t)pg * a.kv.kv_heads + kvh) * kPage + (kk % kPage)) * HD + c * 8;
+      const uint32_t dst = sbase + (uint32_t)(((stage * 2 + kv) * BLK + (kk * CH + (c ^ (kk & 7))) * 8) * 2);
+      pf_cp16(dst, src, ok);
+    }
+    asm volatile("cp.async.commit_group;\n" ::: "memory");
+  };
+
+  float o[NT][4];
+#pragma unroll
+  for (int n = 0; n < NT; n++) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+  float mrow[2] = {-INFINITY, -INFINITY}, lrow[2] = {0.f, 0.f};
+
+  load_block(blo, 0);
+  for (int b = blo; b <= bhi; b++) {
+    const int stage = (b - blo) & 1;
+    if (b + 1 <= bhi) {
+      load_block(b + 1, stage ^ 1);
+      asm volatile("cp.async.wait_group 1;\n" ::: "memory");
+    } else {
+      asm volatile("cp.async.wait_group 0;\n" ::: "memory");
+    }
+    __syncthreads();
+    const int key0 = b * kPfKeys;
+    if (key0 <= warp_max) {  // blocks wholly past this warp's rows are all masked
+      const uint32_t ks_base = sbase + (uint32_t)((stage * 2 + 0) * BLK * 2);
+      const uint32_t vs_base = sbase + (uint32_t)((stage * 2 + 1) * BLK * 2);
+      float sc[8][4];
+#pragma unroll
+      for (int n = 0; n < 8; n++) sc[n][0] = sc[n][1] = sc[n][2] = sc[n][3] = 0.f;
+      const int mi = lane >> 3, lr = lane & 7;
+#pragma unroll
+      for (int ks = 0; ks < KS; ks++)
+#pragma unroll
+        for (int jp = 0; jp < 4; jp++) {
+          const int kk = jp * 16 + (mi >> 1) * 8 + lr, c = ks * 2 + (mi & 1);
+          uint32_t b0, b1, b2, b3;
+          pf_ldsm4(ks_base + (uint32_t)((kk * CH + (c ^ (kk & 7))) * 16), b0, b1, b2, b3);
+          pf_mma(sc[2 * jp], qh[ks], b0, b1);
+          pf_mma(sc[2 * jp], ql[ks], b0, b1);
+          pf_mma(sc[2 * jp + 1], qh[ks], b2, b3);
+          pf_mma(sc[2 * jp + 1], ql[ks], b2, b3);
+        }
+      // mask, scale, online softmax (rows g and g + 8)
+      float mx[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+      for (int n = 0; n < 8; n++)
+#pragma unroll
+        for (int e = 0; e < 4; e++) {
+          const int h = e >> 1, j = key0 + n * 8 + 2 * t + (e & 1);
+          const bool ok = qok[h] && j <= qpos[h] && (a.window <= 0 || j > qpos[h] - a.window);
+          sc[n][e] = ok ? sc[n][e] * scale : -INFINITY;
+          mx[h] = fmaxf(mx[h], sc[n][e]);
+        }
+      float alpha[2];
+#pragma unroll
+      for (int h = 0; h < 2; h++) {
+        mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffffu, mx[h], 1));
+        mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffffu, mx[h], 2));
+        const float mnew = fmaxf(mrow[h], mx[h]);
+        alpha[h] = mrow[h] == -INFINITY ? 0.f : expf(mrow[h] - mnew);
+        mrow[h] = mnew;
+      }
+      float sum[2] = {0.f, 0.f};
+#pragma unroll
+      for (int n = 0; n < 8; n++)
+#pragma unroll
+        for (int e = 0; e < 4; e++) {
+          const int h = e >> 1;
+          const float p = sc[n][e] == -INFINITY ? 0.f : expf(sc[n][e] - mrow[h]);
+          sc[n][e] = p;
+          sum[h] += p;
+        }
+#pragma unroll
+      for (int h = 0; h < 2; h++) {
+        sum[h] += __shfl_xor_sync(0xffffffffu, sum[h], 1);
+        sum[h] += __shfl_xor_sync(0xffffffffu, sum[h], 2);
+        lrow[h] = lrow[h] * alpha[h] + sum[h];
+      }
+#pragma unroll
+      for (int n = 0; n < NT; n++) {
+        o[n][0] *= alpha[0], o[n][1] *= alpha[0];
+        o[n][2] *= alpha[1], o[n][3] *= alpha[1];
+      }
+      // O += P V over the block's four 16-key steps
+#pragma unroll
+      for (int kc = 0; kc < 4; kc++) {
+        uint32_t ph[4], pl[4];
+        pf_split(sc[2 * kc][0], sc[2 * kc][1], ph[0], pl[0]);
+        pf_split(sc[2 * kc][2], sc[2 * kc][3], ph[1], pl[1]);
+        pf_split(sc[2 * kc + 1][0], sc[2 * kc + 1][1], ph[2], pl[2]);
+        pf_split(sc[2 * kc + 1][2], sc[2 * kc + 1][3], ph[3], pl[3]);
+#pragma unroll
+        for (int n = 0; n < NT; n += 2) {
+          const int kk = kc * 16 + (mi & 1) * 8 + lr, c = n + (mi >> 1);
+          uint32_t b0, b1, b2, b3;
+          pf_ldsm4t(vs_base + (uint32_t)((kk * CH + (c ^ (kk & 7))) * 16), b0, b1, b2, b3);
+          pf_mma(o[n], ph, b0, b1);
+          pf_mma(o[n], pl, b0, b1);
+          pf_mma(o[n + 1], ph, b2, b3);
+          pf_mma(o[n + 1], pl, b2, b3);
+        }
+      }
+    }
+    __syncthreads();  // the stage is rewritten by the load two blocks on
+  }
+#pragma unroll
+  for (int h = 0; h < 2; h++) {
+    if (!qok[h]) continue;
+    const float inv = lrow[h] > 0.f ? 1.0f / lrow[h] : 0.f;
+    const size_t ob = (size_t)(row0 + qrow[h]) * a.ldo + (size_t)qhead[h] * HD;
+#pragma unroll
+    for (int n = 0; n < NT; n++) {
+      put_out(a.out, a.out_plane, ob + n * 8 + 2 * t, o[n][2 * h] * inv);
+      put_out(a.out, a.out_plane, ob + n * 8 + 2 * t + 1, o[n][2 * h + 1] * inv);
+    }
+  }
+}
+
+template <int HD, int G>
+int launch_prefill_t(const AttnArgs& a, float scale, cudaStream_t st) {
+  const size_t smem = (size_t)2 * 2 * kPfKeys * HD * sizeof(__half);
+  if (first_use_on_device((const void*)k_attn_prefill<HD, G>))
+    WL_CUDA_TRY(cudaFuncSetAttribute(k_attn_prefill<HD, G>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)smem));
+  constexpr int CR = 4 * (16 / G);
+  return launch_k(k_attn_prefill<HD, G>, dim3((a.rows + CR - 1) / CR, a.kv_heads), dim3(kPfThreads), smem,
+                  st, a, scale);
+}
+
+template <int HD>
+int launch_prefill_hd(const AttnArgs& a, int G, float scale, cudaStream_t st) {
+  switch (G) {
+    case 1: return launch_prefill_t<HD, 1>(a, scale, st);
+    case 2: return launch_prefill_t<HD, 2>(a, scale, st);
+    case 4: return launch_prefill_t<HD, 4>(a, scale, st);
+    case 8: return launch_prefill_t<HD, 8>(a, scale, st);
+  }
+  return fail(WL_ERR_UNSUPPORTED, "prefill attention: heads per KV head must be 1, 2, 4 or 8");
+}
+
 // ---------------------------------------------------------------- contiguous f32 KV (op API)
 template <int HD, int G>
 __global__ void __launch_bounds__(kAttnThreads)
@@ -482,6 +736,22 @@ int launch_attention_paged(const AttnArgs& a, cudaStream_t st) {
     case 256: return launch_paged_hd<256>(a, G, scale, st);
   }
   return fail(WL_ERR_UNSUPPORTED, "attention: head_dim must be 64, 128 or 256");
+}
+
+bool attention_prefill_ok(int heads, int kv_heads, int head_dim) {
+  if (kv_heads <= 0 || heads % kv_heads) return false;
+  const int G = heads / kv_heads;
+  return (head_dim == 64 || head_dim == 128) && (G == 1 || G == 2 || G == 4 || G == 8);
+}
+
+int launch_attention_prefill(const AttnArgs& a, cudaStream_t st) {
+  if (a.kv.page != kPage) return fail(WL_ERR_UNSUPPORTED, "attention: KV page must be 16 tokens");
+  if (!attention_prefill_ok(a.heads, a.kv_heads, a.head_dim))
+    return fail(WL_ERR_UNSUPPORTED, "prefill attention: head_dim 64 / 128 and 1, 2, 4 or 8 heads per KV head");
+  if (a.rows <= 0) return WL_OK;
+  const int G = a.heads / a.kv_heads;
+  const float scale = 1.0f / sqrtf((float)a.head_dim);
+  return a.head_dim == 64 ? launch_prefill_hd<64>(a, G, scale, st) : launch_prefill_hd<128>(a, G, scale, st);
 }
 
 int launch_attention_f32(const float* q, const float* k, const float* v, int rows, int past,

@@ -27,6 +27,12 @@ struct AttnArgs {
   int* err = nullptr;        // set (bit 1) if a bounded wait gave up
 };
 int launch_attention_paged(const AttnArgs& a, cudaStream_t st);
+// Prompt rows of ONE session at consecutive positions (a prefill chunk) on
+// tensor cores (mma.sync, flash-attention style); same math and outputs as
+// launch_attention_paged (nsplit / part buffers unused).  Needs head_dim 64 or
+// 128 and 1, 2, 4 or 8 heads per KV head (attention_prefill_ok).
+bool attention_prefill_ok(int heads, int kv_heads, int head_dim);
+int launch_attention_prefill(const AttnArgs& a, cudaStream_t st);
 
 // Same math over contiguous f32 K/V [past+rows][KVH*hd] (the reference's KV
 // cache layout, lazy_transformer.rs:322-434).

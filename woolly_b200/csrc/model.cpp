@@ -630,6 +630,15 @@ static int gemv_a(wl_model* m, const QMat& W, int R, const float* x, int ldx, fl
   return WL_OK;
 }
 
+// Prompt chunks of >= kPrefillMmaRows rows run attention on tensor cores;
+// decode rows (one per session) and short chunks the flash-decoding kernel.
+constexpr int kPrefillMmaRows = 16;
+static int attention(const wl_model* m, const AttnArgs& a, cudaStream_t st) {
+  if (m->prefill_chunk && a.rows >= kPrefillMmaRows && attention_prefill_ok(a.heads, a.kv_heads, a.head_dim))
+    return launch_attention_prefill(a, st);
+  return launch_attention_paged(a, st);
+}
+
 // The forward on weights in ggml orientation (llama.cpp checkpoints): the
 // same layer as the reference's (lazy_transformer.rs:98-258) with its
 // projections read as rows of K (quantized_matvec's layout,
@@ -674,7 +683,7 @@ static int run_rows_a(wl_model* m, int R, int nsplit, int lfirst) {
     a.ldo = qd;
     a.out_plane = 0;
     a.err = m->err;
-    WL_TRY(launch_attention_paged(a, st));
+    WL_TRY(attention(m, a, st));
     WL_TRY(gemv_a(m, y.wo, R, m->attf, qd, m->h, d, true));
     WL_TRY(launch_rmsnorm(m->h, y.ffn_norm, R, d, m->eps, 0, nullptr, 0, 0.f, m->xf, 0, 0, st));
     WL_TRY(gemv_a(m, y.wg, R, m->xf, d, m->gf, ff, false));
@@ -754,7 +763,7 @@ static int run_rows_body(wl_model* m, int R, int nsplit, int lfirst) {
       a.ldo = qd;
       a.out_plane = apl;
       a.err = m->err;
-      WL_TRY(launch_attention_paged(a, st));
+      WL_TRY(attention(m, a, st));
     }
     if (peer) {
       WL_TRY(gemv(m, 1, &y.wo, R, m->att, apl, qd, peer_push(m, 0), &ctas_o));
@@ -1272,7 +1281,10 @@ int forward(wl_model* m, wl_session* const* ss, int n, const uint32_t* ids, cons
       const bool last_chunk = c0 + c == cnt;
       int lfirst = mode == WL_LOGITS_ALL ? 0 : (last_chunk ? c - 1 : c);
       const int nsplit = attention_plan_splits(c, m->KVHl, s->len + c, m->sms);
-      WL_TRY(run_rows(m, c, nsplit, lfirst));
+      m->prefill_chunk = true;
+      const int rs = run_rows(m, c, nsplit, lfirst);
+      m->prefill_chunk = false;
+      WL_TRY(rs);
       if (c - lfirst > 0) {
         WL_CUDA_TRY(cudaMemcpyAsync(logits + lg_off, m->logits, (size_t)(c - lfirst) * V * 4,
                                     cudaMemcpyDeviceToHost, m->st));

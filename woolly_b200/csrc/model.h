@@ -78,6 +78,9 @@ struct wl_model {
   float* logits = nullptr;  // [MR][V]
   // ggml orientation (llama.cpp files): f32 rows between the layout-A GEMVs
   bool ggml = false;
+  // set while run_rows processes one session's prompt chunk (consecutive
+  // positions): attention then takes the tensor-core prefill kernel
+  bool prefill_chunk = false;
   float *xf = nullptr, *kf = nullptr, *vf = nullptr, *attf = nullptr, *gf = nullptr, *uf = nullptr;
   int Vl = 0;                       // vocabulary columns of this rank's LM head (V unless sharded)
   float* logits_part = nullptr;     // [MR][Vl] this rank's logit columns (sharded head)
