@@ -301,18 +301,30 @@ __device__ void cluster_finish(const GemvArgs& a, const ClusterRed& R, float* ti
   asm volatile("barrier.cluster.wait.acquire.aligned;\n" ::: "memory");  // every mbarrier is set up
   // send: group q = (b, c) of this CTA's tile to its owner
   const uint32_t recv0 = (uint32_t)__cvta_generic_to_shared(R.recv);
-  for (int q = threadIdx.x; q < B * g4; q += blockDim.x) {
-    const int b = q / g4, c = (q - b * g4) * 4;
-    int item = q, part = 0;
-    if (P == 2) {
-      const int h = c / hd, w = c - h * hd;
-      part = w >= half;
-      item = b * (g4 / 2) + h * (half / 4) + (w - part * half) / 4;
+  if (P == 1) {
+    // item = q: owner q % C, slot q / C, row q / g4 -- stepped incrementally
+    // (q advances by blockDim.x), no integer division per item
+    const int step = (int)blockDim.x;
+    const int so = step % C, sj = step / C, sb = step / g4, sc = step % g4;
+    int q = threadIdx.x, owner = q % C, j = q / C, b = q / g4, c4 = q % g4;
+    for (; q < B * g4; q += step) {
+      const float4 v = *reinterpret_cast<const float4*>(tile + b * tp + c4 * 4);
+      st_async4(mapa(recv0 + (uint32_t)((r * R.ipr + j) * 16), owner), v, mapa(R.bar, owner));
+      owner += so, j += sj, b += sb, c4 += sc;
+      if (owner >= C) owner -= C, j++;
+      if (c4 >= g4) c4 -= g4, b++;
     }
-    const int owner = item % C, j = item / C;
-    const float4 v = *reinterpret_cast<const float4*>(tile + b * tp + c);
-    st_async4(mapa(recv0 + (uint32_t)(((r * R.ipr + j) * P + part) * 16), owner), v,
-              mapa(R.bar, owner));
+  } else {
+    for (int q = threadIdx.x; q < B * g4; q += blockDim.x) {
+      const int b = q / g4, c = (q - b * g4) * 4;
+      const int h = c / hd, w = c - h * hd;
+      const int part = w >= half;
+      const int item = b * (g4 / 2) + h * (half / 4) + (w - part * half) / 4;
+      const int owner = item % C, j = item / C;
+      const float4 v = *reinterpret_cast<const float4*>(tile + b * tp + c);
+      st_async4(mapa(recv0 + (uint32_t)(((r * R.ipr + j) * P + part) * 16), owner), v,
+                mapa(R.bar, owner));
+    }
   }
   const bool got = red_wait(R.bar);
   if (!got && a.err && threadIdx.x == 0) atomicOr(a.err, 4);
