@@ -153,6 +153,25 @@ def test_long_prefill_chunked_and_paged(tiny_models):
                max_prefill=64)
 
 
+@pytest.mark.parametrize("spec", [
+    # 8 query heads per KV head (the 70B grouping), head_dim 128, window 100
+    dict(hidden=1024, layers=1, heads=8, kv_heads=1, ff=512, vocab=512, weight_type=Q4_0,
+         sliding_window=100, seed=31),
+    # MHA, head_dim 64, no window
+    dict(hidden=512, layers=1, heads=8, kv_heads=8, ff=512, vocab=512, weight_type=Q4_0, seed=32),
+])
+def test_prefill_attention_tensor_core_parity(tmp_path, spec):
+    """Prompt chunks of >= 16 rows take the tensor-core prefill attention:
+    chunks of 90, 90 and 21 rows (max_prefill 90) and a 17-row prompt, whose
+    key ranges start mid-block, cross the window and end inside a 64-key
+    block, against the oracle's full-prefix forward."""
+    p = write_synthetic(str(tmp_path / "pf.gguf"), **spec)
+    rng = np.random.default_rng(spec["seed"])
+    prompts = [rng.integers(0, spec["vocab"], 201).tolist(), rng.integers(0, spec["vocab"], 17).tolist()]
+    okw = dict(window=spec["sliding_window"]) if spec.get("sliding_window") else None
+    run_parity(p, prompts, steps=4, oracle_kw=okw, max_sessions=2, max_context=256, max_prefill=90)
+
+
 def test_device_step_matches_host_step(tiny_models):
     m = CudaTransformer(tiny_models["gqa_q4_0"], max_sessions=4, max_context=64)
     a = [Session(m) for _ in range(3)]
