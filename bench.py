@@ -573,7 +573,7 @@ def path_70b(tmpdir, layers, rank, ws):
     return path
 
 
-def tp_decode(args, ws, rank, local):
+def tp_decode(args, ws, rank, local, steps=None, warmup=3):
     """LLaMA-2-70B shape (d 8192, 80 layers, 64 heads, 8
     KV heads, FFN 28672), Q4_0, tensor-parallel over the launch's ranks
     (column shards for q/k/v and gate/up, row shards for attn_output and
@@ -590,9 +590,10 @@ def tp_decode(args, ws, rank, local):
     os.makedirs(args.tmpdir, exist_ok=True)
     path = path_70b(args.tmpdir, L, rank, ws)
     comm = nccl_communicator(rank, ws) if ws > 1 else None
-    steps = args.tp_steps
+    steps = steps or args.tp_steps
+    W = max(1, warmup)
     m = CudaTransformer(path, device=local, tp_rank=rank, tp_size=ws, nccl_comm=comm,
-                        max_sessions=B, max_context=P + 2 * (steps + 3) + 8, max_batch=B, max_prefill=P)
+                        max_sessions=B, max_context=P + 2 * (steps + W) + 8, max_batch=B, max_prefill=P)
     rng = np.random.default_rng(SEED + 7)
     sess = [Session(m) for _ in range(B)]
     t0 = time.perf_counter()
@@ -603,16 +604,17 @@ def tp_decode(args, ws, rank, local):
     stream = torch.cuda.current_stream(dev).cuda_stream
     out = {}
     wb = weight_bytes_70b(L)
+    launches = m.decode_kernel_count(B) * steps  # this library's kernels in the bs32 timed loop
     for nb in (B, 1):
-        ids = torch.from_numpy(rng.integers(0, CFG_70B["vocab"], (steps + 3, nb)).astype(np.int32)).to(dev)
-        for t in range(3):
+        ids = torch.from_numpy(rng.integers(0, CFG_70B["vocab"], (steps + W, nb)).astype(np.int32)).to(dev)
+        for t in range(W):
             m.decode_step_device(sess[:nb], ids[t].data_ptr(), logits.data_ptr(), stream)
         torch.cuda.synchronize()
         barrier(ws)
         ctx = [len(s) for s in sess[:nb]]
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
-        for t in range(3, steps + 3):
+        for t in range(W, steps + W):
             m.decode_step_device(sess[:nb], ids[t].data_ptr(), logits.data_ptr(), stream)
         e1.record()
         torch.cuda.synchronize()
@@ -657,6 +659,7 @@ def tp_decode(args, ws, rank, local):
     if rank != 0:
         return None
     return {"tp": ws, "layers": L, "prompt": P, "prefill_s": prefill_s, "timed_steps": steps,
+            "gpu_launches_bs32": launches,
             "results": out, "e2e_bs32_tok_s": e2e, "collectives": ar,
             "workload": f"llama2-70b-shape Q4_0, {L} layers, TP{ws}, 32 sessions x {P}-token prefill, "
                         f"teacher-forced decode bs32 and bs1"}
@@ -723,13 +726,14 @@ def run_tp_headline(args):
     torch.cuda.set_device(local)
     clk = Clocks(local)
     clk.start()
-    r = tp_decode(args, ws, rank, local)
+    # the line times exactly the driver's K steps after its W warm-up steps
+    r = tp_decode(args, ws, rank, local, steps=args.steps, warmup=args.warmup)
     clocks = clk.stop()
     if rank == 0:
         b32 = r["results"]["bs32"]
         print(json.dumps({
             "metric": TP_METRIC, "value": b32["tok_s"], "unit": "tok/s", "n_gpus": ws,
-            "steps": args.tp_steps, "warmup": 3, "ms_per_step": b32["ms_per_step"],
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": b32["ms_per_step"],
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
             "dtype": "q4_0 weights, f16 MMA operands, f32 accumulate",
             "data": "synthetic (seeded N(0,0.02) weights, uniform random token ids)",
@@ -738,7 +742,7 @@ def run_tp_headline(args):
                        "l2": "inputs larger than L2 (weights + KV per step)"},
             "e2e": {"value": r["e2e_bs32_tok_s"], "unit": "tok/s", "h2d_bytes_per_step": 32 * 12,
                     "d2h_bytes_per_step": 32 * CFG_70B["vocab"] * 4},
-            "tp": r, "clocks": clocks}), flush=True)
+            "gpu_launches": r["gpu_launches_bs32"], "tp": r, "clocks": clocks}), flush=True)
     barrier(ws)
     import torch.distributed as dist
     if ws > 1:
