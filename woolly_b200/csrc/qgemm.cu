@@ -5,18 +5,22 @@
 // layout-B matmul, tensor_utils.rs:118-157, applied to a whole prompt).  One
 // CTA computes 128 weight columns x 128 token rows.  The weights are read from
 // the tiled decode copy (qtile_bytes): a 64-row stage of a 128-column tile is
-// four or six contiguous byte ranges (codes, scales, Q4_1 mins of two 64-column
-// quarters), fetched by one thread with bulk copies (cp.async.bulk, the TMA
-// engine) that complete on an mbarrier, two stages ahead.  Per stage:
-//   * 512 threads each dequantize one (quarter, unit, lane) record of 16
-//     weights from shared memory into f16 hi/lo pairs with W = Whi + Wlo
-//     exactly (Q4_0 / Q8_0: Whi = f16(q*d) by HMUL2, Wlo = fma(q, d, -Whi) by
-//     HFMA2, the residual being exact in f16; Q4_1 in f32), stored K-major with
-//     the 128-byte swizzle (4-byte k-pair stores, bank-conflict free);
-//   * the activation hi/lo planes are copied in K-major with the same swizzle;
-//   * one thread issues 3 MMAs per 16-k step into the TMEM accumulator:
-//     Xhi*Whi + Xhi*Wlo + Xlo*Whi (the dropped Xlo*Wlo term is ~2^-22 of the
-//     product), then commits the stage to an mbarrier that gates its reuse.
+// four or six contiguous byte ranges (codes, scales, mins of two 64-column
+// quarters).  Warp-specialised, no CTA-wide barrier inside the K loop:
+//   * a control warp keeps bulk copies (cp.async.bulk, the TMA engine) of
+//     those ranges three stages ahead, completing on per-slot mbarriers; it
+//     waits until the dequantizing warps have filled a stage slot, issues 3
+//     MMAs per 16-k step into the TMEM accumulator, Xhi*Whi + Xhi*Wlo +
+//     Xlo*Whi (the dropped Xlo*Wlo term is ~2^-22 of the product), and
+//     commits them to the slot's mbarrier;
+//   * 16 dequantizing warps (512 threads) each turn one (quarter, unit, lane)
+//     record of 16 weights into f16 hi/lo pairs with W = Whi + Wlo exactly
+//     (Q4_0 / Q8_0: Whi = f16(q*d) by HMUL2, Wlo = fma(q, d, -Whi) by HFMA2,
+//     the residual being exact in f16; Q4_1 and the K-quants in f32), stored
+//     K-major with the 128-byte swizzle (4-byte k-pair stores, bank-conflict
+//     free), copy their share of the activation hi/lo planes K-major with the
+//     same swizzle, and hand the slot over on a 16-arrival mbarrier; they wait
+//     on the slot's MMA commit only before reusing it.
 // The epilogue reads the accumulator with tcgen05.ld (warp w owns TMEM lanes
 // 32w..32w+31 = weight columns) and applies the same F32 / ADD / QKV / SwiGLU
 // outputs as the decode GEMV.  Every mbarrier wait is bounded; on expiry the
