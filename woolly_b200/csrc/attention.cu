@@ -17,6 +17,9 @@
 // unnormalised partial (o, m, l) that k_attn_combine merges with the
 // log-sum-exp rule.  Every mbarrier wait is bounded; on expiry the kernel
 // raises an error flag instead of spinning.
+//
+// Prompt chunks of one session take k_attn_prefill instead (tensor cores,
+// see below); decode rows and short chunks the paged kernel.
 #include <cuda_fp16.h>
 
 #include <cmath>
