@@ -126,6 +126,7 @@ typedef struct wl_synth_config {
   uint64_t seed;
   uint32_t vd_type;       /* 0 = weight_type; else the type of attn_v and ffn_down
                            * (the K-quant mixes keep those as Q6_K beside Q4_K) */
+  uint32_t embd_type;     /* type of token_embd.weight (WL_F32 = 0 by default) */
 } wl_synth_config;
 
 int wl_synth_gguf(const char* path, const wl_synth_config* cfg);

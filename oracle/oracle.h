@@ -140,6 +140,7 @@ typedef struct or_synth_cfg {
   float rope_theta, norm_eps;
   uint64_t seed;
   uint32_t vd_type;        /* 0 = weight_type; else the type of attn_v and ffn_down */
+  uint32_t embd_type;      /* type of token_embd.weight (OR_F32 = 0 by default) */
 } or_synth_cfg;
 int or_synth_gguf(const char* path, const or_synth_cfg* cfg);
 

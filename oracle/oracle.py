@@ -37,7 +37,7 @@ class SynthCfg(C.Structure):
                 ("context_length", C.c_uint32), ("weight_type", C.c_uint32),
                 ("output_type", C.c_uint32), ("sliding_window", C.c_uint32),
                 ("rope_theta", C.c_float), ("norm_eps", C.c_float), ("seed", C.c_uint64),
-                ("vd_type", C.c_uint32)]
+                ("vd_type", C.c_uint32), ("embd_type", C.c_uint32)]
 
 
 _lib = None
@@ -93,13 +93,13 @@ def synth_gguf(path: str, *, hidden: int, layers: int, heads: int, kv_heads: int
                vocab: int, weight_type: int = Q4_0, output_type: int | None = None,
                tied: bool = False, context_length: int = 4096, sliding_window: int = 0,
                rope_theta: float = 10000.0, norm_eps: float = 1e-5, seed: int = 0,
-               vd_type: int = 0) -> str:
+               vd_type: int = 0, embd_type: int = 0) -> str:
     """The seeded LLaMA-shape GGUF of the product's writer, written by the
     oracle's own C writer (synth.c), so CPU-only legs never load the product
     library."""
     cfg = SynthCfg(hidden, layers, heads, kv_heads, ff, vocab, context_length, weight_type,
                    0xFFFFFFFF if tied else (weight_type if output_type is None else output_type),
-                   sliding_window, rope_theta, norm_eps, seed, vd_type)
+                   sliding_window, rope_theta, norm_eps, seed, vd_type, embd_type)
     st = lib().or_synth_gguf(str(path).encode(), C.byref(cfg))
     if st:
         raise ValueError(f"or_synth_gguf status {st}")

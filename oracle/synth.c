@@ -266,6 +266,7 @@ int or_synth_gguf(const char* path, const or_synth_cfg* c) {
   uint64_t d = c->hidden, kvd = d / c->heads * c->kv_heads, ff = c->ff, V = c->vocab;
   int has_out = c->output_type != 0xFFFFFFFFu;
   if (has_out && !(quantized(c->output_type) || c->output_type == OR_F32)) return OR_ERR_UNSUPPORTED;
+  if (!(quantized(c->embd_type) || c->embd_type == OR_F32) || (d * V) % blk(c->embd_type)) return OR_ERR_UNSUPPORTED;
   if (d % blk(wt) || kvd % blk(wt) || ff % blk(wt) || d % blk(vt) || kvd % blk(vt) ||
       (has_out && V % blk(c->output_type)))
     return OR_ERR_INVALID;
@@ -275,7 +276,7 @@ int or_synth_gguf(const char* path, const or_synth_cfg* c) {
 #define T(nm, a, b, ty, k)                                                                    \
   (snprintf(ts[i].name, sizeof ts[i].name, "%s", nm), ts[i].d0 = a, ts[i].d1 = b, ts[i].type = ty, \
    ts[i].kind = k, i++)
-  T("token_embd.weight", d, V, OR_F32, 1);
+  T("token_embd.weight", d, V, c->embd_type, 1);
   for (uint32_t l = 0; l < c->layers; l++) {
     static const char* names[9] = {"attn_norm", "attn_q",   "attn_k", "attn_v",  "attn_output",
                                    "ffn_norm",  "ffn_gate", "ffn_up", "ffn_down"};

@@ -175,3 +175,35 @@ def test_kquant_device_decode_matches_host_step(tmp_path):
     for s in a + b:
         s.close()
     m.close()
+
+
+@pytest.mark.parametrize("spec", [
+    # the Q4_K_M-style mix with a quantized embedding, as llama.cpp files hold it
+    dict(hidden=512, layers=2, heads=4, kv_heads=2, ff=768, vocab=1024, weight_type=Q4_K,
+         vd_type=Q6_K, output_type=Q6_K, embd_type=Q4_K, seed=41),
+    dict(hidden=512, layers=1, heads=8, kv_heads=8, ff=512, vocab=512, weight_type=Q6_K,
+         embd_type=Q6_K, seed=42),
+])
+@pytest.mark.parametrize("rope", [0, 1])
+def test_kquant_ggml_orientation_parity(tmp_path, spec, rope):
+    """K-quant weights and embedding in ggml orientation (rows of K values with
+    256-value super-blocks along K; token_embd one row per token), with and
+    without NeoX RoPE, against the oracle reading the file the same way."""
+    p = write_synthetic(str(tmp_path / "kqa.gguf"), **spec)
+    rng = np.random.default_rng(spec["seed"] + rope)
+    prompts = [rng.integers(0, spec["vocab"], n).tolist() for n in (7, 40, 2)]
+    _parity(p, prompts, steps=34, oracle_kw=dict(layout_a=1, rope=rope), max_sessions=3,
+            max_context=128, ggml_layout=1,
+            rope_mode=_lib.ROPE_NEOX if rope else _lib.ROPE_OFF)
+
+
+@pytest.mark.parametrize("embd", [8, 12, 14])
+def test_quantized_embedding_parity(tmp_path, embd):
+    """token_embd.weight of a quantized type is dequantized on the device as
+    woolly_gguf::dequantize reads it (bit-exact kernels) and the forward
+    matches the oracle (woolly's orientation)."""
+    p = write_synthetic(str(tmp_path / "qe.gguf"), hidden=512, layers=1, heads=4, kv_heads=2, ff=512,
+                        vocab=512, weight_type=2, embd_type=embd, seed=43)
+    rng = np.random.default_rng(embd)
+    prompts = [rng.integers(0, 512, n).tolist() for n in (20, 5)]
+    _parity(p, prompts, steps=50, max_sessions=2, max_context=96)

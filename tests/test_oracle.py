@@ -295,6 +295,11 @@ def test_layout_a_reads_ggml_rows():
     dict(hidden=512, layers=1, heads=4, kv_heads=2, ff=768, vocab=1024, weight_type=O.Q4_K,
          vd_type=O.Q6_K, output_type=O.Q6_K, seed=10),
     dict(hidden=256, layers=1, heads=2, kv_heads=2, ff=512, vocab=512, weight_type=O.Q6_K, seed=11),
+    # quantized token embeddings
+    dict(hidden=256, layers=1, heads=2, kv_heads=2, ff=512, vocab=512, weight_type=O.Q4_0,
+         embd_type=O.Q8_0, seed=12),
+    dict(hidden=256, layers=1, heads=2, kv_heads=2, ff=512, vocab=512, weight_type=O.Q4_K,
+         vd_type=O.Q6_K, embd_type=O.Q4_K, output_type=O.Q6_K, seed=13),
 ])
 def test_oracle_writer_matches_product_writer(tmp_path, kw):
     """The oracle's own GGUF writer (used where the product library must not

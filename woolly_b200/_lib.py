@@ -69,7 +69,7 @@ class SynthConfig(C.Structure):
                 ("context_length", C.c_uint32), ("weight_type", C.c_uint32),
                 ("output_type", C.c_uint32), ("sliding_window", C.c_uint32),
                 ("rope_theta", C.c_float), ("norm_eps", C.c_float), ("seed", C.c_uint64),
-                ("vd_type", C.c_uint32)]
+                ("vd_type", C.c_uint32), ("embd_type", C.c_uint32)]
 
 
 class ModelOptions(C.Structure):

@@ -159,6 +159,43 @@ struct Loader {
     cursor = align_up(cursor + bytes + 256, 256);
     return off;
   }
+  // token_embd.weight: F32 is copied whole; any other type woolly_gguf::
+  // dequantize reads (dequantize.rs:189-205) is staged and dequantized into an
+  // f32 table on the device after the upload (embd_type != WL_F32)
+  uint32_t embd_type = WL_F32;
+  size_t embd_staged = 0, embd_n = 0;
+  bool add_embd(const std::string& name, uint64_t expect, size_t* off) {
+    const GgufTensor* t = need(name);
+    if (!t) return false;
+    if (t->type == WL_F32) return add_f32(name, expect, off);
+    const uint32_t ty = t->type;
+    const bool ok_type = ty == WL_F16 || ty == WL_Q4_0 || ty == WL_Q4_1 || ty == WL_Q8_0 || ty == 12 ||
+                         ty == 14 || ty == 6 || ty == 7 || ty == 13 || ty == 15;
+    if (!ok_type) {
+      err = name + ": unsupported type " + std::to_string(ty);
+      return false;
+    }
+    if (t->nelems() != expect) {
+      err = name + ": unexpected element count " + std::to_string(t->nelems());
+      return false;
+    }
+    const uint8_t* src = g->data(*t);
+    if (!src) {
+      err = name + ": data out of bounds";
+      return false;
+    }
+    Piece p;
+    p.src = src;
+    p.src_pitch = p.row_bytes = p.dst_pitch = p.dst_bytes = t->nbytes();
+    p.rows = 1;
+    p.dst_off = embd_staged = tcursor;
+    tcursor = align_up(tcursor + p.dst_bytes + 256, 256);
+    tpieces.push_back(p);
+    embd_type = ty;
+    embd_n = expect;
+    *off = reserve(expect * sizeof(float));
+    return true;
+  }
   // f32 vector / matrix copied whole
   bool add_f32(const std::string& name, uint64_t expect, size_t* off) {
     const GgufTensor* t = need(name);
@@ -206,19 +243,27 @@ struct Loader {
       err = name + ": data out of bounds";
       return false;
     }
-    const int S = t->type == WL_F32 ? 0 : block_bytes(t->type);
-    if (t->type != WL_F32 && (!S || K % 32)) {
-      err = name + ": layout-A weights must be F32, Q4_0, Q4_1 or Q8_0 with K % 32 == 0";
+    const bool kq = kquant_type((int)t->type);
+    const int S = t->type == WL_F32 ? 0 : kq ? kquant_block_bytes((int)t->type) : block_bytes(t->type);
+    if (t->type != WL_F32 && (!S || K % (kq ? 256 : 32))) {
+      err = name + ": layout-A weights must be F32, Q4_0, Q4_1, Q8_0 (K % 32 == 0) or Q4_K, Q6_K (K % 256 == 0)";
       return false;
     }
     Piece p;
     p.src = src;
     p.rows = (size_t)N;
-    p.src_pitch = p.row_bytes = t->type == WL_F32 ? (size_t)K * 4 : (size_t)K / 32 * S;
+    p.src_pitch = p.row_bytes = t->type == WL_F32 ? (size_t)K * 4 : (size_t)K / (kq ? 256 : 32) * S;
     p.dst_pitch = p.row_bytes;
     p.dst_bytes = p.dst_pitch * p.rows;
-    p.dst_off = *off = reserve(p.dst_bytes);
-    pieces.push_back(p);
+    if (kq) {  // staged; the GEMV reads a copy with 16-byte aligned super-blocks
+      p.dst_off = tcursor;
+      tcursor = align_up(tcursor + p.dst_bytes + 256, 256);
+      *off = p.dst_off | kStaged;
+      tpieces.push_back(p);
+    } else {
+      p.dst_off = *off = reserve(p.dst_bytes);
+      pieces.push_back(p);
+    }
     out->type = t->type;
     out->K = K;
     out->N = N;
@@ -980,7 +1025,7 @@ int model_load(wl_ctx* ctx, const char* path, const wl_model_options* o, wl_mode
   Loader ld{g, m.get()};
   const int d = m->d, kvd = m->kvd, ff = m->ff, V = m->V;
   size_t off_embd, off_onorm, off_out;
-  bool ok = ld.add_f32("token_embd.weight", (uint64_t)d * V, &off_embd) &&
+  bool ok = ld.add_embd("token_embd.weight", (uint64_t)d * V, &off_embd) &&
             ld.add_f32("output_norm.weight", (uint64_t)d, &off_onorm);
   bool tied = ok && !g->find("output.weight");
   // LM head under tensor parallelism: each rank keeps V / T vocabulary
@@ -1039,6 +1084,8 @@ int model_load(wl_ctx* ctx, const char* path, const wl_model_options* o, wl_mode
   };
   uint8_t* B = m->dweights;
   m->embd = (const float*)(B + off_embd);
+  if (ld.embd_type != WL_F32)
+    WL_TRY(launch_dequant((int)ld.embd_type, staged + ld.embd_staged, ld.embd_n, (float*)(B + off_embd), m->st));
   m->out_norm = (const float*)(B + off_onorm);
   if (tied) {
     m->out.w = B + off_embd;
@@ -1062,21 +1109,26 @@ int model_load(wl_ctx* ctx, const char* path, const wl_model_options* o, wl_mode
     y.wu.w = at(z.u);
     y.wd.w = at(z.dn);
   }
-  // ---- tiled decode copies (the GEMV's lane-ready layout) of every quantized projection ----
+  // ---- tiled decode copies (the GEMV's lane-ready layout) of every quantized projection;
+  //      in the ggml orientation, K-quant rows with 16-byte aligned super-blocks ----
   {
     std::vector<QMat*> mats;
-    if (!m->ggml) {
-      for (Layer& y : m->layers)
-        for (QMat* q : {&y.wq, &y.wk, &y.wv, &y.wo, &y.wg, &y.wu, &y.wd}) mats.push_back(q);
-      mats.push_back(&m->out);
-    }
+    for (Layer& y : m->layers)
+      for (QMat* q : {&y.wq, &y.wk, &y.wv, &y.wo, &y.wg, &y.wu, &y.wd}) mats.push_back(q);
+    mats.push_back(&m->out);
     size_t total = 0;
     std::vector<size_t> offs;
     for (QMat* q : mats) {
-      const bool ok = (block_bytes(q->type) || kquant_type((int)q->type)) &&
-                      qgemv_b_fast_ok(q->type, q->K, q->N, q->pitch, q->w);
-      offs.push_back(ok ? total : SIZE_MAX);
-      if (ok) total = align_up(total + qtile_bytes((int)q->type, q->K, q->N), 256);
+      size_t bytes = 0;
+      if (m->ggml) {
+        // layout A: q->K values per row, q->N rows (the loader's [K, N] dims)
+        if (kquant_type((int)q->type)) bytes = (size_t)q->N * (q->K / 256) * kq_padded_bytes((int)q->type);
+      } else if ((block_bytes(q->type) || kquant_type((int)q->type)) &&
+                 qgemv_b_fast_ok(q->type, q->K, q->N, q->pitch, q->w)) {
+        bytes = qtile_bytes((int)q->type, q->K, q->N);
+      }
+      offs.push_back(bytes ? total : SIZE_MAX);
+      if (bytes) total = align_up(total + bytes, 256);
     }
     m->weight_bytes += total;
     if (total) {
@@ -1084,8 +1136,15 @@ int model_load(wl_ctx* ctx, const char* path, const wl_model_options* o, wl_mode
       for (size_t i = 0; i < mats.size(); i++) {
         if (offs[i] == SIZE_MAX) continue;
         QMat* q = mats[i];
-        WL_TRY(launch_repack_tiled((int)q->type, q->w, q->K, q->N, q->pitch, m->dtiled + offs[i], m->st));
-        q->wt = m->dtiled + offs[i];
+        if (m->ggml) {
+          WL_TRY(launch_kq_pad((int)q->type, q->w, (size_t)q->pitch, q->N, q->K, m->dtiled + offs[i], m->st));
+          q->w = m->dtiled + offs[i];
+          q->pitch = q->K / 256 * kq_padded_bytes((int)q->type);
+          q->wt = q->w;
+        } else {
+          WL_TRY(launch_repack_tiled((int)q->type, q->w, q->K, q->N, q->pitch, m->dtiled + offs[i], m->st));
+          q->wt = m->dtiled + offs[i];
+        }
       }
       WL_CUDA_TRY(cudaStreamSynchronize(m->st));
     }

@@ -1209,6 +1209,221 @@ int repack_tiled_t(const uint8_t* src, int K, int N, int pitch, uint8_t* dst, cu
   return WL_OK;
 }
 
+// ------------------------------------------------------------------ layout A, K-quants
+// ggml orientation (rows of K values, 256-value super-blocks along K), the
+// values woolly_gguf::dequantize reads (dequantize.rs:381-537).  The loader
+// keeps each row's super-blocks padded to 16-byte multiples (Q4_K 144 bytes,
+// Q6_K 210 -> 224: launch_kq_pad) so that a stage (256 k = one super-block
+// per row) is 9 or 14 aligned cp.async chunks.  Per 32-value (Q4_K) or
+// 16-value (Q6_K) sub-block: the integer codes enter the MMA as exact f16
+// (q, or q - 32), the activations as hi/lo planes, and each row's partial
+// sum is scaled in f32 by d*sc (Q6_K: /64); Q4_K's dmin is added once per
+// value as dmin * sum(x) through a ones-matrix MMA.
+template <int T>
+constexpr int kSBP = T == WL_Q4_K ? 144 : 224;  // padded super-block bytes
+
+__global__ void k_kq_pad(const uint8_t* src, size_t src_pitch, int rows, int nsb, int sb, int sbp,
+                         uint8_t* dst) {
+  const size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
+  const size_t row_bytes = (size_t)nsb * sbp;
+  if (i >= row_bytes * rows) return;
+  const size_t r = i / row_bytes, o = i % row_bytes;
+  const int j = (int)(o / sbp), b = (int)(o % sbp);
+  dst[i] = b < sb ? src[r * src_pitch + (size_t)j * sb + b] : 0;
+}
+
+__device__ __forceinline__ uint32_t nib_pair(uint32_t b) {  // byte -> exact f16 (low, high nibble)
+  return hsub2u(((b & 0xFu) | ((b & 0xF0u) << 12)) | kMagic, kMagic);
+}
+__device__ __forceinline__ uint32_t q6_pair(const uint8_t* sb, int i) {  // exact f16 (q(i)-32, q(i+1)-32)
+  const uint32_t v = (uint32_t)kq_code(WL_Q6_K, sb, i) | ((uint32_t)kq_code(WL_Q6_K, sb, i + 1) << 16);
+  return hsub2u(v | kMagic, 0x64206420u);
+}
+__device__ __forceinline__ float q4k_scale(const uint8_t* sb, int j) {
+  const int src = (j * 3) / 2;
+  const int sc = (j % 2 == 0) ? (sb[src] & 63) : (((sb[src] >> 6) | ((sb[src + 1] & 15) << 2)) & 63);
+  return __fmul_rn(__half2float(__ushort_as_half((uint16_t)(sb[12] | (sb[13] << 8)))), (float)sc);
+}
+
+template <int T, int NT>
+__global__ void __launch_bounds__(kThreads) k_qgemv_ak(const GemvArgs a) {
+  constexpr int BP = NT * 8;
+  constexpr int KS = 256;
+  constexpr int SBP = kSBP<T>;
+  constexpr int SP = SBP + 16;  // shared row pitch (rows of a warp start in different banks)
+  constexpr int RAW = kColsA * SP;
+  constexpr int CH = SBP / 16;
+  constexpr int STG = NT <= 2 ? kStages : 2;
+  constexpr int SST = RAW + BP * KS * 4;
+  constexpr int XP = KS + 8;
+  constexpr int PIPE = STG * SST > BP * (kColsA + 4) * 4 ? STG * SST : BP * (kColsA + 4) * 4;
+  extern __shared__ __align__(16) uint8_t smem[];
+  uint8_t* raw = smem;
+  pdl_wait();
+  pdl_trigger();
+  __half* xs = reinterpret_cast<__half*>(smem + PIPE);
+  const __half* xl_base = xs + BP * XP;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int g = lane >> 2, t = lane & 3;
+  const int gx = blockIdx.x, split = blockIdx.y;
+  const GemvSeg& S = a.seg[0];
+  const int n0 = gx * kColsA;
+  const int k0 = split * a.kchunk;
+  const int k1 = min(a.K, k0 + a.kchunk);
+  const int nstage = k1 > k0 ? (k1 - k0) / KS : 0;
+  const int ncv = min(kColsA, S.N - n0);
+  __shared__ uint64_t red_bar;
+  ClusterRed R;
+  red_begin(R, a, 0, ncv, &red_bar, smem + PIPE + 2 * BP * XP * 2);
+
+  auto load_stage = [&](int st, int buf) {
+    const size_t byte0 = (size_t)((k0 + st * KS) / KS) * SBP;
+    uint8_t* dst = raw + buf * SST;
+    for (int i = tid; i < kColsA * CH; i += kThreads) {
+      const int r = i / CH, c = i - r * CH;
+      const int row = n0 + r;
+      const bool ok = row < S.N;
+      cp_async16(dst + r * SP + c * 16, S.W + (size_t)(ok ? row : 0) * S.pitch + byte0 + c * 16,
+                 ok ? 16 : 0);
+    }
+    load_x_f32(a, reinterpret_cast<float*>(dst + RAW), BP, KS, k0 + st * KS, k1);
+  };
+#pragma unroll
+  for (int s = 0; s < STG - 1; s++) {
+    if (s < nstage) load_stage(s, s);
+    cp_commit();
+  }
+  float acc[NT][4];
+#pragma unroll
+  for (int n = 0; n < NT; n++)
+#pragma unroll
+    for (int q = 0; q < 4; q++) acc[n][q] = 0.f;
+  const uint32_t ones[4] = {kOnes, kOnes, kOnes, kOnes};
+
+  for (int st = 0; st < nstage; st++) {
+    cp_wait<STG - 2>();
+    __syncthreads();
+    {
+      const int nx = st + STG - 1;
+      if (nx < nstage) load_stage(nx, nx % STG);
+      cp_commit();
+    }
+    split_tile(reinterpret_cast<const float*>(raw + (st % STG) * SST + RAW), xs, BP, KS, XP);
+    __syncthreads();
+    const uint8_t* rA = raw + (st % STG) * SST + (warp * 16 + g) * SP;  // rows g and g + 8 of the warp
+    const uint8_t* rB = rA + 8 * SP;
+    // the activation B fragments of k step [kk, kk + 16) for batch tile n
+    auto xfrag = [&](int n, int kk, uint32_t& h0, uint32_t& h1, uint32_t& l0, uint32_t& l1) {
+      const __half* xp = xs + (n * 8 + g) * XP + kk + 2 * t;
+      const __half* lp = xl_base + (n * 8 + g) * XP + kk + 2 * t;
+      h0 = *reinterpret_cast<const uint32_t*>(xp);
+      h1 = *reinterpret_cast<const uint32_t*>(xp + 8);
+      l0 = *reinterpret_cast<const uint32_t*>(lp);
+      l1 = *reinterpret_cast<const uint32_t*>(lp + 8);
+    };
+    if constexpr (T == WL_Q4_K) {
+      const float mA = __half2float(__ushort_as_half((uint16_t)(rA[14] | (rA[15] << 8))));
+      const float mB = __half2float(__ushort_as_half((uint16_t)(rB[14] | (rB[15] << 8))));
+#pragma unroll 2
+      for (int j = 0; j < 8; j++) {
+        const float sA = q4k_scale(rA, j), sB = q4k_scale(rB, j);
+        uint32_t af[2][4];
+#pragma unroll
+        for (int s2 = 0; s2 < 2; s2++) {  // byte of k = j*32 + s2*16 + 2t (low nibble) and + 1 (high)
+          const int o = 16 + j * 16 + s2 * 8 + t;
+          af[s2][0] = nib_pair(rA[o]);
+          af[s2][1] = nib_pair(rB[o]);
+          af[s2][2] = nib_pair(rA[o + 4]);
+          af[s2][3] = nib_pair(rB[o + 4]);
+        }
+#pragma unroll
+        for (int n = 0; n < NT; n++) {
+          float c[4] = {0.f, 0.f, 0.f, 0.f}, cm[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+          for (int s2 = 0; s2 < 2; s2++) {
+            uint32_t h0, h1, l0, l1;
+            xfrag(n, j * 32 + s2 * 16, h0, h1, l0, l1);
+            mma16816(c, af[s2], h0, h1);
+            mma16816(c, af[s2], l0, l1);
+            mma16816(cm, ones, h0, h1);
+            mma16816(cm, ones, l0, l1);
+          }
+          acc[n][0] += sA * c[0] + mA * cm[0];
+          acc[n][1] += sA * c[1] + mA * cm[1];
+          acc[n][2] += sB * c[2] + mB * cm[2];
+          acc[n][3] += sB * c[3] + mB * cm[3];
+        }
+      }
+    } else {
+      const float dA = __half2float(__ushort_as_half((uint16_t)(rA[208] | (rA[209] << 8)))) * 0.015625f;
+      const float dB = __half2float(__ushort_as_half((uint16_t)(rB[208] | (rB[209] << 8)))) * 0.015625f;
+#pragma unroll 2
+      for (int j = 0; j < 16; j++) {  // 16-value sub-blocks: one k step each
+        const float sA = dA * (float)rA[192 + j], sB = dB * (float)rB[192 + j];
+        const int kk = j * 16;
+        uint32_t af[4];
+        af[0] = q6_pair(rA, kk + 2 * t);
+        af[1] = q6_pair(rB, kk + 2 * t);
+        af[2] = q6_pair(rA, kk + 8 + 2 * t);
+        af[3] = q6_pair(rB, kk + 8 + 2 * t);
+#pragma unroll
+        for (int n = 0; n < NT; n++) {
+          float c[4] = {0.f, 0.f, 0.f, 0.f};
+          uint32_t h0, h1, l0, l1;
+          xfrag(n, kk, h0, h1, l0, l1);
+          mma16816(c, af, h0, h1);
+          mma16816(c, af, l0, l1);
+          acc[n][0] += sA * c[0];
+          acc[n][1] += sA * c[1];
+          acc[n][2] += sB * c[2];
+          acc[n][3] += sB * c[3];
+        }
+      }
+    }
+  }
+  cp_wait<0>();
+  __syncthreads();
+  constexpr int TP = kColsA + 4;
+  float* tile = reinterpret_cast<float*>(smem);
+#pragma unroll
+  for (int n = 0; n < NT; n++)
+#pragma unroll
+    for (int q = 0; q < 4; q++) {
+      const int b = n * 8 + 2 * t + (q & 1);
+      const int c = warp * 16 + g + 8 * (q >> 1);
+      tile[b * TP + c] = acc[n][q];
+    }
+  __syncthreads();
+  cluster_finish(a, R, tile, TP, ncv, 0, n0);
+}
+
+template <int T>
+size_t smem_ak(int NT) {
+  const size_t BP = (size_t)NT * 8;
+  const int stg = NT <= 2 ? kStages : 2;
+  const size_t pipe = (size_t)stg * (kColsA * (kSBP<T> + 16) + BP * 256 * 4);
+  const size_t tile = BP * (kColsA + 4) * 4;
+  const size_t xs = 2 * BP * (256 + 8) * 2;
+  return std::max(pipe, tile) + xs + recv_bytes((int)BP, kColsA);
+}
+
+template <int T, int NT>
+int launch_ak_t(const GemvArgs& a, cudaStream_t st) {
+  return launch_cluster(k_qgemv_ak<T, NT>, dim3(a.seg[0].groups, a.csplit), kThreads, smem_ak<T>(NT), 1,
+                        a.csplit, a, st);
+}
+
+template <int T>
+int dispatch_ak(const GemvArgs& a, cudaStream_t st) {
+  switch ((a.B + 7) / 8) {
+    case 1: return launch_ak_t<T, 1>(a, st);
+    case 2: return launch_ak_t<T, 2>(a, st);
+    case 3: return launch_ak_t<T, 3>(a, st);
+    case 4: return launch_ak_t<T, 4>(a, st);
+  }
+  return fail(WL_ERR_INVALID_ARGUMENT, "qgemv: B must be 1..32 per launch");
+}
+
 template <int T, int NT, bool LOC = false, bool TLD = false>
 int launch_b_t(const GemvArgs& a, cudaStream_t st) {
   int groups = 0;
@@ -1280,6 +1495,17 @@ size_t smem_b_type(int type, int NT) {
 
 bool kquant_type(int type) { return type == WL_Q4_K || type == WL_Q6_K; }
 int kquant_block_bytes(int type) { return type == WL_Q4_K ? 144 : type == WL_Q6_K ? 210 : 0; }
+int kq_padded_bytes(int type) { return type == WL_Q4_K ? kSBP<WL_Q4_K> : type == WL_Q6_K ? kSBP<WL_Q6_K> : 0; }
+
+int launch_kq_pad(int type, const uint8_t* src, size_t src_pitch, int rows, int K, uint8_t* dst,
+                  cudaStream_t st) {
+  if (!kquant_type(type) || K % 256 || rows <= 0) return fail(WL_ERR_INVALID_ARGUMENT, "kq_pad: bad shape");
+  const int nsb = K / 256, sb = kquant_block_bytes(type), sbp = kq_padded_bytes(type);
+  const size_t total = (size_t)rows * nsb * sbp;
+  k_kq_pad<<<(unsigned)((total + 255) / 256), 256, 0, st>>>(src, src_pitch, rows, nsb, sb, sbp, dst);
+  WL_CUDA_TRY(cudaGetLastError());
+  return WL_OK;
+}
 
 int qgemv_group_cols(int layout) { return layout == WL_LAYOUT_B ? kColsB : kColsA; }
 
@@ -1296,6 +1522,9 @@ bool qgemv_b_fast_ok(int type, int K, int N, int pitch, const void* W) {
 }
 
 bool qgemv_a_fast_ok(int type, int K, int N, int pitch, const void* W) {
+  if (kquant_type(type))  // padded super-blocks (launch_kq_pad)
+    return K % 256 == 0 && K > 0 && pitch == K / 256 * kq_padded_bytes(type) &&
+           (reinterpret_cast<uintptr_t>(W) & 15) == 0;
   const int S = block_bytes(type);
   if (!S) return false;
   (void)N;
@@ -1432,6 +1661,8 @@ int launch_qgemv_b(const GemvArgs& a, cudaStream_t st) {
 
 int launch_qgemv_a(const GemvArgs& a, cudaStream_t st) {
   switch (a.type) {
+    case WL_Q4_K: return dispatch_ak<WL_Q4_K>(a, st);
+    case WL_Q6_K: return dispatch_ak<WL_Q6_K>(a, st);
     case WL_Q4_0: return dispatch<WL_Q4_0, false>(a, st);
     case WL_Q4_1: return dispatch<WL_Q4_1, false>(a, st);
     case WL_Q8_0: return dispatch<WL_Q8_0, false>(a, st);

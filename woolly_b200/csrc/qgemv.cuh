@@ -145,6 +145,11 @@ bool qgemv_b_fast_ok(int type, int K, int N, int pitch, const void* W);
 // Q4_K / Q6_K: run from the tiled copy only (N % 256 == 0, K % 16 == 0)
 bool kquant_type(int type);
 int kquant_block_bytes(int type);  // GGUF bytes of one 256-value super-block
+// layout A (ggml orientation) K-quants run from rows of super-blocks padded to
+// kq_padded_bytes (Q4_K 144, Q6_K 224): launch_kq_pad writes them
+int kq_padded_bytes(int type);
+int launch_kq_pad(int type, const uint8_t* src, size_t src_pitch, int rows, int K, uint8_t* dst,
+                  cudaStream_t st);
 bool qgemv_a_fast_ok(int type, int K, int N, int pitch, const void* W);
 // picks csplit / kchunk for a launch (fills the GPU)
 void qgemv_plan(GemvArgs& a, int layout, int num_sms);

@@ -322,8 +322,11 @@ int synth_gguf(const char* path, const wl_synth_config* c) {
       (c->output_type != 0xFFFFFFFFu && ok_type(c->output_type) && V % blk(c->output_type)))
     return fail(WL_ERR_INVALID_ARGUMENT,
                 "synth_gguf: quantized output dims must be multiples of the block size (32; 256 for K-quants)");
+  const uint32_t et = c->embd_type;
+  if (!ok_type(et) || (et != WL_F32 && (d * V) % blk(et)))
+    return fail(WL_ERR_UNSUPPORTED, "synth_gguf: bad token_embd type");
   std::vector<TSpec> ts;
-  ts.push_back({"token_embd.weight", d, V, WL_F32, 1});
+  ts.push_back({"token_embd.weight", d, V, et, 1});
   for (uint32_t l = 0; l < c->layers; l++) {
     std::string p = "blk." + std::to_string(l) + ".";
     ts.push_back({p + "attn_norm.weight", d, 0, WL_F32, 2});

@@ -189,15 +189,16 @@ def write_synthetic(path: str, *, hidden: int, layers: int, heads: int, kv_heads
                     vocab: int, weight_type: int = _lib.Q4_0, output_type: int | None = None,
                     tied: bool = False, context_length: int = 4096, sliding_window: int = 0,
                     rope_theta: float = 10000.0, norm_eps: float = 1e-5, seed: int = 0,
-                    vd_type: int = 0) -> str:
+                    vd_type: int = 0, embd_type: int = 0) -> str:
     """Writes the seeded LLaMA-shape GGUF used by the tests and benchmarks.
     vd_type (0 = weight_type) is the type of attn_v and ffn_down, as the
-    K-quant mixes store them (Q6_K beside Q4_K)."""
+    K-quant mixes store them (Q6_K beside Q4_K); embd_type that of
+    token_embd.weight (F32 by default)."""
     cfg = _lib.SynthConfig(hidden, layers, heads, kv_heads, ff, vocab, context_length,
                            weight_type,
                            0xFFFFFFFF if tied else (weight_type if output_type is None
                                                     else output_type),
-                           sliding_window, rope_theta, norm_eps, seed, vd_type)
+                           sliding_window, rope_theta, norm_eps, seed, vd_type, embd_type)
     check(lib().wl_synth_gguf(str(path).encode(), C.byref(cfg)))
     return str(path)
 
