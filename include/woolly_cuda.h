@@ -114,9 +114,10 @@ int wl_gguf_get_str(const wl_gguf* g, const char* key, const char** out, uint64_
 
 /* ------------------------------------------------------------------ */
 /* Synthetic model writer (host).  No reference counterpart: writes the seeded
- * LLaMA-architecture GGUF the benchmarks and parity tests use (token_embd f32
- * N(0,0.02) with dims [d, V]; projections N(0,0.02) quantized to `weight_type`
- * with dims [in, out]; norms f32 1+N(0,0.02)). */
+ * LLaMA-architecture GGUF the benchmarks and parity tests use (token_embd
+ * N(0,0.02) with dims [d, V], f32 or `embd_type`; projections N(0,0.02)
+ * quantized to `weight_type` (attn_v / ffn_down to `vd_type`) with dims
+ * [in, out]; norms f32 1+N(0,0.02)). */
 typedef struct wl_synth_config {
   uint32_t hidden, layers, heads, kv_heads, ff, vocab, context_length;
   uint32_t weight_type;   /* WL_Q4_0 / WL_Q4_1 / WL_Q8_0 / WL_Q4_K / WL_Q6_K / WL_F32 */
@@ -332,9 +333,13 @@ void wl_model_options_default(wl_model_options* o);
 int wl_init(int device, wl_ctx** out);
 void wl_ctx_free(wl_ctx* ctx);
 
-/* Loads the GGUF, uploads every weight block unchanged to HBM (a TP shard is
- * re-packed to its column/row slice).  Replaces LazyTransformer::from_gguf
- * (lazy_transformer.rs:29-95) and its dequantization cache. */
+/* Loads the GGUF into HBM.  Replaces LazyTransformer::from_gguf
+ * (lazy_transformer.rs:29-95) and its dequantization cache.  Projection
+ * weights (Q4_0, Q4_1, Q8_0, Q4_K, Q6_K or F32, mixed freely) are kept once,
+ * in the lane-ready tiled copy the GEMV and GEMM read (ggml orientation:
+ * quantized rows as stored, K-quant super-blocks padded to 16 bytes); a
+ * tensor-parallel shard keeps its column / row slice.  token_embd.weight may
+ * be F32 or any type wl_dequantize reads; it is held as an f32 table. */
 int wl_model_load_gguf(wl_ctx* ctx, const char* path, const wl_model_options* opts,
                        wl_model** out);
 void wl_model_free(wl_model* m);
