@@ -21,9 +21,9 @@
 //     free), copy their share of the activation hi/lo planes K-major with the
 //     same swizzle, and hand the slot over on a 16-arrival mbarrier; they wait
 //     on the slot's MMA commit only before reusing it.
-// The epilogue reads the accumulator with tcgen05.ld (warp w owns TMEM lanes
-// 32w..32w+31 = weight columns) and applies the same F32 / ADD / QKV / SwiGLU
-// outputs as the decode GEMV.  Every mbarrier wait is bounded; on expiry the
+// The epilogue reads the accumulator with tcgen05.ld (all 16 dequantizing
+// warps: lane quarter w % 4 = 32 weight columns, token rows 32 * (w / 4)..)
+// and applies the same F32 / ADD / QKV / SwiGLU outputs as the decode GEMV.  Every mbarrier wait is bounded; on expiry the
 // kernel raises an error bit, waits (bounded) for its issued MMAs and bulk
 // copies and frees its TMEM before returning.
 #include <cuda_fp16.h>
@@ -454,15 +454,18 @@ __global__ void __launch_bounds__(kGThreads, 1) k_qgemm_b(const GemvArgs a, int 
   if (!ok && a.err && tid == 0) atomicOr(a.err, 16);
   asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory");
 
-  if (ok && warp < 4) {
-    // warp w reads TMEM lanes 32w..32w+31 = tile columns; TMEM columns = token rows
-    const int c = warp * 32 + lane;
+  // all 16 dequantizing warps drain the accumulator: warp w reads TMEM lanes
+  // 32*(w%4).. (tile columns; a warp may only address its lane quarter) for
+  // token rows [32*(w/4), +32) (TMEM columns)
+  const int lw = warp & 3, rq = warp >> 2;
+  if (ok && warp < kGDeq / 32) {
+    const int c = lw * 32 + lane;
     float* upbuf = reinterpret_cast<float*>(sm);  // SwiGLU: up values [row][64]
-    for (int r0 = 0; r0 < kGM; r0 += 16) {
+    for (int r0 = rq * 32; r0 < rq * 32 + 32; r0 += 16) {
       uint32_t v[16];
-      tmem_ld16(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)r0, v);
+      tmem_ld16(tmem + ((uint32_t)(lw * 32) << 16) + (uint32_t)r0, v);
       if (sw) {
-        if (warp >= 2) {
+        if (lw >= 2) {
 #pragma unroll
           for (int i = 0; i < 16; i++) upbuf[(r0 + i) * 64 + (c - 64)] = __uint_as_float(v[i]);
         }
@@ -477,15 +480,15 @@ __global__ void __launch_bounds__(kGThreads, 1) k_qgemm_b(const GemvArgs a, int 
     }
   }
   __syncthreads();
-  if (ok && sw && warp < 2) {
+  if (ok && sw && warp < kGDeq / 32 && lw < 2) {
     const Epilogue& e = a.epi;
     __half* out = reinterpret_cast<__half*>(e.y[0]);
-    const int c = warp * 32 + lane;
+    const int c = lw * 32 + lane;
     const int col = n0 + c;
     const float* upbuf = reinterpret_cast<const float*>(sm);
-    for (int r0 = 0; r0 < kGM; r0 += 16) {
+    for (int r0 = rq * 32; r0 < rq * 32 + 32; r0 += 16) {
       uint32_t v[16];
-      tmem_ld16(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)r0, v);
+      tmem_ld16(tmem + ((uint32_t)(lw * 32) << 16) + (uint32_t)r0, v);
 #pragma unroll
       for (int i = 0; i < 16; i++) {
         const int row = m0 + r0 + i;
