@@ -185,3 +185,23 @@ def test_seeded_sampling_is_reproducible():
         rid = eng.submit([4, 5], cfg)
         runs.append(eng.run()[rid])
     assert runs[0] == runs[1] == sequential([4, 5], cfg)
+
+
+def test_streaming_callbacks_and_generator():
+    """Tokens reach the per-request callback as they are produced (in order,
+    the last one flagged done with its reason), and stream() yields a
+    request's tokens while other requests share the batched steps."""
+    m = FakeModel(max_batch=3, max_sessions=3)
+    eng = make_engine(m)
+    seen = {}
+    cfgs = [GenerationConfig(max_tokens=n, eos_below=0) for n in (4, 6)]
+    rids = [eng.submit([i + 1, 2 * i + 3], c, on_token=lambda rid, tok, done, why:
+                       seen.setdefault(rid, []).append((tok, done, why))) for i, c in enumerate(cfgs)]
+    streamed = list(eng.stream([9, 8, 7], GenerationConfig(max_tokens=5, eos_below=0)))
+    eng.run()
+    for rid, c, p in zip(rids, cfgs, ([1, 3], [2, 5])):
+        toks = [t for t, _, _ in seen[rid]]
+        assert toks == eng.finished[rid].tokens == sequential(p, c)
+        assert [d for _, d, _ in seen[rid]] == [False] * (c.max_tokens - 1) + [True]
+        assert seen[rid][-1][2] == "length"
+    assert streamed == sequential([9, 8, 7], GenerationConfig(max_tokens=5, eos_below=0))

@@ -108,6 +108,7 @@ class Request:
     session: object = None
     done: bool = False
     reason: str = ""
+    on_token: object = None  # callable(rid, token, done, reason) per produced token
 
 
 class BatchEngine:
@@ -143,12 +144,15 @@ class BatchEngine:
         self.finished: dict[int, Request] = {}
         self._next = 0
 
-    def submit(self, prompt, cfg: GenerationConfig | None = None) -> int:
+    def submit(self, prompt, cfg: GenerationConfig | None = None, on_token=None) -> int:
+        """Queues a request; `on_token(rid, token, done, reason)`, if given, is
+        called as each of its tokens is produced (the server's streaming
+        responses, inference.rs:271-357, forward tokens this way)."""
         prompt = [int(t) for t in prompt]
         if not prompt:
             raise ValueError("empty prompt (the reference's EMPTY_INPUT)")
         cfg = cfg or GenerationConfig()
-        r = Request(self._next, prompt, cfg, np.random.default_rng(cfg.seed))
+        r = Request(self._next, prompt, cfg, np.random.default_rng(cfg.seed), on_token=on_token)
         self._next += 1
         self.waiting.append(r)
         return r.rid
@@ -168,6 +172,8 @@ class BatchEngine:
             r.done, r.reason = True, "eos"
         elif self.max_context is not None and len(r.session) + 1 > self.max_context:
             r.done, r.reason = True, "context"
+        if r.on_token is not None:
+            r.on_token(r.rid, int(tok), r.done, r.reason)
 
     def _retire(self) -> None:
         keep = []
@@ -239,6 +245,19 @@ class BatchEngine:
                 break
             self.step()
         return {rid: r.tokens for rid, r in sorted(self.finished.items())}
+
+    def stream(self, prompt, cfg: GenerationConfig | None = None):
+        """Submits a request and yields its tokens as they are produced,
+        stepping the whole engine (other requests advance in the same batched
+        steps)."""
+        got: list = []
+        rid = self.submit(prompt, cfg, on_token=lambda _r, tok, _d, _why: got.append(tok))
+        while rid not in self.finished:
+            self.step()
+            while got:
+                yield got.pop(0)
+        while got:
+            yield got.pop(0)
 
     def close(self) -> None:
         for r in self.running:
