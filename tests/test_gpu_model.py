@@ -291,3 +291,24 @@ def test_ggml_layout_tinyllama_rope(tmp_path):
     e1, _ = compare(gp[0], op[0], "ggml tinyllama prefill")
     e2, _ = compare(gs, os_, "ggml tinyllama decode")
     print(f"ggml-orientation tinyllama (rope on): prefill max-abs {e1:.2e}, decode {e2:.2e}")
+
+
+def test_inference_engine_api_on_the_runtime(tiny_models):
+    """woolly-core's InferenceEngine / InferenceSession mirror over the CUDA
+    runtime: a named session keeps its context across infer() calls, and its
+    logits equal the Model-level forward of the whole sequence."""
+    from woolly_b200.model import InferenceEngine
+    m = CudaTransformer(tiny_models["gqa_q4_0"], max_sessions=3, max_context=64)
+    eng = InferenceEngine()
+    eng.load_model(m)
+    s = eng.create_session()
+    V = m.vocab_size()
+    a = eng.infer([3, 4, 5], s.id()).reshape(-1, V)
+    b = eng.infer([6, 7], s.id()).reshape(-1, V)
+    full = m.forward([3, 4, 5, 6, 7]).reshape(-1, V)
+    assert np.abs(np.concatenate([a, b]) - full).max() <= 1e-3
+    assert s.token_history() == [3, 4, 5, 6, 7]
+    s.deactivate()
+    eng.cleanup_sessions()
+    assert eng.list_sessions() == []
+    m.close()

@@ -239,27 +239,122 @@ class Session:
         return [self.infer(t) for t in batch]
 
 
-InferenceSession = Session
+class InferenceSession:
+    """InferenceSession (woolly-core/src/session.rs:118-330): one sequence's
+    device KV cache plus the bookkeeping the reference keeps with it -- a
+    string id, an active flag, the count of tokens processed and the token
+    history.  Errors follow the reference: inference on a deactivated session
+    (SESSION_INACTIVE) or with no tokens (empty input) raises WoollyError
+    with WL_ERR_INVALID_ARGUMENT."""
+
+    def __init__(self, model, session_id: str | None = None, backend=None):
+        import uuid
+        self.model = model
+        self._id = session_id or str(uuid.uuid4())
+        self._s = backend if backend is not None else Session(model)
+        self._active = True
+        self._history: list[int] = []
+
+    def id(self) -> str:
+        return self._id
+
+    def is_active(self) -> bool:
+        return self._active
+
+    def tokens_processed(self) -> int:
+        return len(self._history)
+
+    def token_history(self) -> list[int]:
+        return list(self._history)
+
+    def infer(self, tokens: Sequence[int]) -> np.ndarray:
+        """session.rs:193-258: appends the tokens to this session's context and
+        returns their logits, flattened [len(tokens) * vocab]."""
+        if not self._active:
+            raise WoollyError(_lib.WL_ERR_INVALID_ARGUMENT, "Session is not active")
+        if len(tokens) == 0:
+            raise WoollyError(_lib.WL_ERR_INVALID_ARGUMENT, "Empty input tokens")
+        out = self._s.infer(tokens)
+        self._history += [int(t) for t in tokens]
+        return out
+
+    def infer_batch(self, batch: Sequence[Sequence[int]]) -> list[np.ndarray]:
+        """session.rs:260-277: one infer() per item, in order."""
+        return [self.infer(t) for t in batch]
+
+    def clear(self) -> None:
+        """session.rs:280-306: drops the history and the KV cache."""
+        self._s.reset()
+        self._history = []
+
+    def deactivate(self) -> None:
+        self._active = False
+
+    def close(self) -> None:
+        self._active = False
+        self._s.close()
+
+
+class SessionInfo(dict):
+    """engine.rs SessionInfo: id, active, tokens_processed."""
 
 
 class InferenceEngine:
     """InferenceEngine (woolly-core/src/engine.rs:15-246): holds one model and
-    hands out sessions."""
+    its sessions.  create_session() registers a new session; infer(tokens,
+    session_id) runs on the named session (SESSION_NOT_FOUND if it is not
+    registered) or, without an id, on a new registered session, as
+    engine.rs:90-105 does; cleanup_sessions() drops inactive ones (closing
+    their device caches)."""
 
-    def __init__(self):
-        self.model: CudaTransformer | None = None
+    def __init__(self, session_factory=None):
+        self.model = None
+        self.sessions: list[InferenceSession] = []
+        self._factory = session_factory
 
-    def load_model(self, model: CudaTransformer) -> None:
+    def load_model(self, model) -> None:
         self.model = model
 
-    def create_session(self) -> Session:
+    def _need_model(self):
         if self.model is None:
             raise WoollyError(_lib.WL_ERR_INVALID_ARGUMENT, "No model loaded")
-        return Session(self.model)
+        return self.model
 
-    def infer(self, tokens: Sequence[int]) -> np.ndarray:
-        s = self.create_session()
-        try:
-            return s.infer(tokens)
-        finally:
-            s.close()
+    def create_session(self, session_id: str | None = None) -> InferenceSession:
+        m = self._need_model()
+        backend = self._factory() if self._factory is not None else None
+        s = InferenceSession(m, session_id, backend=backend)
+        self.sessions.append(s)
+        return s
+
+    def find_session(self, session_id: str) -> InferenceSession:
+        for s in self.sessions:
+            if s.id() == session_id:
+                return s
+        raise WoollyError(_lib.WL_ERR_INVALID_ARGUMENT, f"Session not found: {session_id}")
+
+    def infer(self, tokens: Sequence[int], session_id: str | None = None) -> np.ndarray:
+        self._need_model()
+        s = self.find_session(session_id) if session_id is not None else self.create_session()
+        return s.infer(tokens)
+
+    def list_sessions(self) -> list[SessionInfo]:
+        return [SessionInfo(id=s.id(), active=s.is_active(), tokens_processed=s.tokens_processed())
+                for s in self.sessions]
+
+    def cleanup_sessions(self) -> None:
+        keep = []
+        for s in self.sessions:
+            if s.is_active():
+                keep.append(s)
+            else:
+                s.close()
+        self.sessions = keep
+
+    def model_info(self) -> dict | None:
+        m = self.model
+        if m is None:
+            return None
+        return dict(name=m.name(), model_type=m.model_type(), vocab_size=m.vocab_size(),
+                    context_length=m.context_length(), hidden_size=m.hidden_size(),
+                    num_layers=m.num_layers(), num_heads=m.num_heads())
