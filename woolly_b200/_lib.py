@@ -30,6 +30,7 @@ WL_ERR_NCCL = 14
 WL_ERR_TIMEOUT = 15
 
 F32, F16, Q4_0, Q4_1, Q8_0 = 0, 1, 2, 3, 8
+Q4_K, Q6_K = 12, 14
 LAYOUT_A, LAYOUT_B = 0, 1
 ROPE_OFF, ROPE_NEOX = 0, 1
 LOGITS_LAST, LOGITS_ALL = 0, 1
