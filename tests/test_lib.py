@@ -86,6 +86,14 @@ def test_new_entry_points_reject_bad_arguments_on_the_host():
     assert lib.wl_qtile_repack(12, p, 64, 64, p, None) == _lib.WL_ERR_INVALID_ARGUMENT  # N % 256
     assert lib.wl_qtile_repack(2, p, 64, 48, p, None) == _lib.WL_ERR_INVALID_ARGUMENT
     assert lib.wl_qtile_repack(2, None, 64, 64, p, None) == _lib.WL_ERR_INVALID_ARGUMENT
+    # K-quant GEMV / GEMM shape rules, checked before any device work
+    B = _lib.LAYOUT_B
+    assert lib.wl_qgemv(12, B, p, 64, 128, p, 1, p, None) == _lib.WL_ERR_INVALID_ARGUMENT  # N % 256
+    assert lib.wl_qgemv(14, B, p, 40, 256, p, 1, p, None) == _lib.WL_ERR_INVALID_ARGUMENT  # K % 16
+    assert lib.wl_qgemv(12, _lib.LAYOUT_A, p, 256, 256, p, 1, p, None) == _lib.WL_ERR_UNSUPPORTED
+    assert lib.wl_qgemm(14, p, 64, 128, p, 8, p, None) == _lib.WL_ERR_INVALID_ARGUMENT  # N % 256
+    assert lib.wl_qgemm_tiled(12, p, 64, 128, p, 0, 8, p, None) == _lib.WL_ERR_INVALID_ARGUMENT
+    assert lib.wl_qgemm_tiled(13, p, 64, 256, p, 0, 8, p, None) == _lib.WL_ERR_UNSUPPORTED
     assert lib.wl_qgemv_tiled(2, p, 40, 64, p, 0, 1, p, None) == _lib.WL_ERR_INVALID_ARGUMENT  # K % 16
     assert lib.wl_qgemv_tiled(2, p, 64, 64, p, 0, 0, p, None) == _lib.WL_ERR_INVALID_ARGUMENT  # B = 0
     # tensor-parallel reduce: 1..8 ranks, <= 32 rows, non-null buffers
